@@ -1,0 +1,550 @@
+"""B200 (sm_100a) FP8 decode GEMM -- Python host interface.
+
+Mirrors the reference's C++ host API (``namespace decode_gemm`` in
+``kernels/decode_gemm.cuh`` and ``kernels/weight_prepack.cuh`` of
+ziyuhuang123/decode_opt) over the C ABI of ``libdecode_gemm_b200.so``:
+
+=============================  ===========================================
+reference (C++)                here
+=============================  ===========================================
+``KernelConfig<...>``          :class:`KernelConfig` (same 16 parameters)
+``Problem``                    :class:`Problem`
+``LaunchPlan``                 :class:`LaunchPlan`
+``Cfg::validate(m, n, k)``     :meth:`KernelConfig.validate`
+``make_launch_plan<Cfg>``      :func:`make_launch_plan`
+``make_weight_tma<Cfg>``       :func:`make_weight_tma`
+``make_activation_tma<Cfg>``   :func:`make_activation_tma`
+``launch_with_maps<Cfg>``      :func:`launch_with_maps`
+``launch<Cfg>``                :func:`launch`
+``prepack::padded_n``          :func:`padded_n`
+``prepack::packed_weight_bytes`` :func:`packed_weight_bytes`
+``prepack::launch_prepack_weight<BM,TILES>`` :func:`launch_prepack_weight`
+=============================  ===========================================
+
+Errors follow the reference: launches return a ``cudaError_t`` integer (0 ok,
+1 = ``cudaErrorInvalidValue`` for an unsupported shape or a missing split-K
+workspace), ``validate`` returns a reason string or None.
+
+:class:`B200Config` exposes the B200 schedule directly (stream-K grid,
+descriptor-ready weight layout) and :func:`fp8_decode_gemm` is a one-call
+torch entry point.  Everything runs through the CUDA library; when it is
+missing, importing the launch functions raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import Optional
+
+from . import _lib
+from ._lib import (ERR_INJECTED_TIMEOUT, FLAG_INJECT_TIMEOUT, LAYOUT_PACKED, LAYOUT_PACKED_SWIZZLED,
+                   LAYOUT_RAW, STATUS_OK, DgConfig, DgPlanInfo, DgProblem, TensorMap)
+
+__all__ = [
+    "KernelConfig", "B200Config", "Problem", "LaunchPlan", "make_launch_plan", "make_weight_tma",
+    "make_activation_tma", "launch_with_maps", "launch", "padded_n", "packed_weight_bytes",
+    "launch_prepack_weight", "prepack_weight", "fp8_decode_gemm", "default_config", "status_string",
+    "LAYOUT_RAW", "LAYOUT_PACKED", "LAYOUT_PACKED_SWIZZLED", "FLAG_INJECT_TIMEOUT",
+    "ERR_INJECTED_TIMEOUT", "STATUS_OK", "m_tile_for", "flush_l2",
+]
+
+CUDA_SUCCESS = 0
+CUDA_ERROR_INVALID_VALUE = 1
+K_BLOCK = 128
+MAX_DYNAMIC_SMEM = 227 * 1024
+
+
+def m_tile_for(m: int) -> int:
+    """The reference's M ladder (bench/bench_common.cuh:103-109)."""
+    for t in (8, 16, 32, 64):
+        if m <= t:
+            return t
+    return 128
+
+
+def _ptr(x) -> int:
+    if x is None:
+        return 0
+    if isinstance(x, int):
+        return x
+    return int(x.data_ptr())
+
+
+def _stream_handle(stream) -> int:
+    if stream is None:
+        return 0
+    if isinstance(stream, int):
+        return stream
+    return int(stream.cuda_stream)
+
+
+# ---------------------------------------------------------------------------
+# Configurations
+# ---------------------------------------------------------------------------
+
+@dataclass(frozen=True)
+class B200Config:
+    """Runtime configuration of the sm_100a kernel (``dg_config``)."""
+
+    m_tile: int = 8
+    block_n: int = 128
+    subs: int = 2
+    stages: int = 0
+    layout: int = LAYOUT_RAW
+    pdl: bool = False
+    split_k: int = 1
+    grid_ctas: int = 0
+    epi_warps: int = 0
+    flags: int = 0
+    timeout_ns: int = 0
+
+    def to_dg(self) -> DgConfig:
+        return DgConfig(self.m_tile, self.block_n, self.subs, self.stages, self.layout, int(self.pdl),
+                        self.split_k, self.grid_ctas, self.epi_warps, self.flags, self.timeout_ns)
+
+    def plan(self, m: int, n: int, k: int) -> "LaunchPlan":
+        info = DgPlanInfo()
+        _lib.lib().dg_plan(ctypes.byref(self.to_dg()), m, n, k, ctypes.byref(info))
+        return LaunchPlan._from_info(info)
+
+    def validate(self, m: int, n: int, k: int) -> Optional[str]:
+        return self.plan(m, n, k).error
+
+    @property
+    def prepacked(self) -> bool:
+        return self.layout != LAYOUT_RAW
+
+
+def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool = True) -> B200Config:
+    """The B200 schedule used by :func:`fp8_decode_gemm` and the benchmark.
+
+    128-row weight tiles (one tcgen05 M=128 tile, aligned with the 128-row
+    weight-scale groups), two 128-K blocks per stage, as many stages as fit
+    in shared memory, and a stream-K grid of one CTA per SM so every SM
+    streams the same number of weight bytes whatever the tile count.
+    """
+    return B200Config(m_tile=m_tile_for(m), block_n=128, subs=2, stages=0, layout=layout, pdl=pdl,
+                      split_k=1, grid_ctas=-1)
+
+
+@dataclass(frozen=True)
+class KernelConfig:
+    """The reference's ``decode_gemm::KernelConfig`` (kernels/decode_gemm.cuh:147-347).
+
+    Same parameters, in the same order, with the same defaults.  On sm_100a
+    they map onto :class:`B200Config` as follows:
+
+    * ``M_TILE`` -> ``m_tile``; ``OUTPUT_ROWS_PER_CTA`` -> ``block_n`` (BM); BM <= 64
+      runs tcgen05 M=64 tiles, larger BM (a B200 extension, up to 128) M=128;
+    * ``SUBS_PER_STAGE`` -> ``subs``; ``NUM_MATH_WG * STAGES_PER_WG`` -> ``stages``
+      (the ring depth, reduced if it does not fit in 227 KiB);
+    * ``PREPACK`` -> weight layout packed (True) or raw (False);
+    * ``PDL`` or ``EPI_OVERLAP`` -> ``griddepcontrol.launch_dependents`` after
+      the producer's last TMA (the sm_100a kernel has one trigger point);
+      ``launch`` sets programmatic stream serialization when ``PDL``;
+    * ``SPLIT_K_CTA`` / ``SPLITK_FACTOR`` -> ``split_k`` = kSplitKFactor with the
+      reference's normalisation (0: follow the bool, 1: off, 2/4/8: S);
+    * ``NUM_MATH_WG``, ``MATH_REGS``, ``PROD_REGS``, ``SINGLE_PRODUCER_WARP``,
+      ``PRELOAD_ACT``, ``SCALE_IN_SMEM``, ``TILES_PER_CTA`` describe the SM90
+      warp-group / register split.  They are range-checked exactly as the
+      reference's static_asserts check them and otherwise do not change the
+      sm_100a kernel, whose warp roles are fixed (TMA warp, MMA warp,
+      epilogue warps) and which schedules one output tile per CTA slice.
+    """
+
+    M_TILE: int
+    OUTPUT_ROWS_PER_CTA: int
+    NUM_MATH_WG: int
+    MATH_REGS: int
+    STAGES_PER_WG: int
+    TILES_PER_CTA: int
+    SUBS_PER_STAGE: int
+    PREPACK: bool
+    PDL: bool
+    EPI_OVERLAP: bool
+    SPLIT_K_CTA: bool
+    PROD_REGS: int = 32
+    SINGLE_PRODUCER_WARP: bool = False
+    PRELOAD_ACT: bool = False
+    SCALE_IN_SMEM: Optional[bool] = None
+    SPLITK_FACTOR: int = 0
+
+    def __post_init__(self):
+        # The reference's static_asserts (kernels/decode_gemm.cuh:166-198), kept
+        # as construction-time errors.
+        mt, bm, wg = self.M_TILE, self.OUTPUT_ROWS_PER_CTA, self.NUM_MATH_WG
+        if mt not in (8, 16, 32, 64, 128):
+            raise ValueError("M_TILE must be one of 8/16/32/64/128")
+        if not (0 < bm <= 64 and bm % 8 == 0) and bm != 128:
+            raise ValueError("OUTPUT_ROWS_PER_CTA (BM) must be a multiple of 8 in (0, 64] "
+                             "(or 128, the B200 full-tile extension)")
+        if wg not in (1, 2, 4):
+            raise ValueError("NUM_MATH_WG must be 1, 2 or 4")
+        if self.TILES_PER_CTA <= 0 or wg % self.TILES_PER_CTA != 0:
+            raise ValueError("NUM_MATH_WG must be divisible by TILES_PER_CTA")
+        if self.STAGES_PER_WG <= 0:
+            raise ValueError("STAGES_PER_WG must be positive")
+        if not (0 < self.SUBS_PER_STAGE <= 64):
+            raise ValueError("SUBS_PER_STAGE must be in [1, 64]")
+        for name in ("MATH_REGS", "PROD_REGS"):
+            v = getattr(self, name)
+            if not (24 <= v <= 256 and v % 8 == 0):
+                raise ValueError(f"{name} must be a multiple of 8 in the PTX range [24, 256]")
+        if (wg * self.MATH_REGS + self.PROD_REGS) * 128 > 65536:
+            raise ValueError("register budget exceeded: (WG*MATH_REGS + PROD_REGS)*128 <= 65536")
+        if self.PRELOAD_ACT and not (mt == 8 and self.PREPACK):
+            raise ValueError("PRELOAD_ACT is only allowed for M_TILE=8 + PREPACK (CONTRACT 4)")
+        if self.SPLITK_FACTOR not in (0, 1, 2, 4, 8):
+            raise ValueError("SPLITK_FACTOR must be 0 (legacy: follow SPLIT_K_CTA), 1 (off), 2, 4 or 8")
+        if self.SPLITK_FACTOR == 1 and self.SPLIT_K_CTA:
+            raise ValueError("SPLITK_FACTOR=1 means split-K off and contradicts SPLIT_K_CTA=true")
+
+    # ---- the reference's derived constants ---------------------------------
+    @property
+    def kMTile(self) -> int:
+        return self.M_TILE
+
+    @property
+    def kOutputRows(self) -> int:
+        return self.OUTPUT_ROWS_PER_CTA
+
+    @property
+    def kNumMathWgs(self) -> int:
+        return self.NUM_MATH_WG
+
+    @property
+    def kStagesPerMathWg(self) -> int:
+        return self.STAGES_PER_WG
+
+    @property
+    def kOutputTilesPerCta(self) -> int:
+        return self.TILES_PER_CTA
+
+    @property
+    def kSubsPerStage(self) -> int:
+        return self.SUBS_PER_STAGE
+
+    @property
+    def kPrepack(self) -> bool:
+        return self.PREPACK
+
+    @property
+    def kPdl(self) -> bool:
+        return self.PDL
+
+    @property
+    def kEpiOverlap(self) -> bool:
+        return self.EPI_OVERLAP
+
+    @property
+    def kSplitKFactor(self) -> int:
+        s = self.SPLITK_FACTOR
+        if s >= 2:
+            return s
+        return 1 if (s == 1 or not self.SPLIT_K_CTA) else 2
+
+    @property
+    def kSplitKCta(self) -> bool:
+        return self.kSplitKFactor > 1
+
+    @property
+    def kScaleInSmem(self) -> bool:
+        return self.M_TILE <= 16 if self.SCALE_IN_SMEM is None else bool(self.SCALE_IN_SMEM)
+
+    @property
+    def kWgsPerOutputTile(self) -> int:
+        return self.NUM_MATH_WG // self.TILES_PER_CTA
+
+    @property
+    def kStages(self) -> int:
+        return self.NUM_MATH_WG * self.STAGES_PER_WG
+
+    def to_b200(self) -> B200Config:
+        return B200Config(m_tile=self.M_TILE, block_n=self.OUTPUT_ROWS_PER_CTA,
+                          subs=self.SUBS_PER_STAGE, stages=min(self.kStages, 16),
+                          layout=LAYOUT_PACKED if self.PREPACK else LAYOUT_RAW,
+                          pdl=bool(self.PDL or self.EPI_OVERLAP), split_k=self.kSplitKFactor,
+                          grid_ctas=0)
+
+    def _fitted(self, m: int, n: int, k: int) -> B200Config:
+        # The ring depth the reference asks for, reduced until it fits.
+        cfg = self.to_b200()
+        stages = cfg.stages
+        while stages > 1:
+            c = B200Config(**{**cfg.__dict__, "stages": stages})
+            if c.plan(m, n, k).error != "dynamic shared memory exceeds 227 KiB":
+                return c
+            stages -= 1
+        return B200Config(**{**cfg.__dict__, "stages": 1})
+
+    def num_output_tiles(self, n: int) -> int:
+        return (n + self.OUTPUT_ROWS_PER_CTA - 1) // self.OUTPUT_ROWS_PER_CTA
+
+    def num_ctas_x(self, n: int) -> int:
+        return self.num_output_tiles(n)
+
+    def num_ctas(self, n: int) -> int:
+        return self.num_ctas_x(n) * self.kSplitKFactor
+
+    def k_ok_for_splitk(self, k: int) -> bool:
+        return k % (K_BLOCK * self.SUBS_PER_STAGE * self.kWgsPerOutputTile * self.kSplitKFactor) == 0
+
+    def validate(self, m: int, n: int, k: int) -> Optional[str]:
+        """The reference's rules (kernels/decode_gemm.cuh:319-346), same messages."""
+        if m < 1 or m > self.M_TILE:
+            return "M out of [1, M_TILE]"
+        if n < 1:
+            return "N must be positive"
+        if k % K_BLOCK != 0:
+            return "K must be a multiple of 128"
+        kb = k // K_BLOCK
+        if kb % self.SUBS_PER_STAGE != 0:
+            return "K/128 must be a multiple of SUBS_PER_STAGE"
+        chunks = kb // self.SUBS_PER_STAGE
+        if chunks % self.kWgsPerOutputTile != 0:
+            return "K/(128*SUBS) must be a multiple of WGsPerOutputTile"
+        if self.kSplitKCta:
+            s = self.kSplitKFactor
+            if chunks % s != 0:
+                return "SPLIT_K: K/(128*SUBS) must be a multiple of SPLITK_FACTOR"
+            if (chunks // s) % self.kWgsPerOutputTile != 0:
+                return "SPLIT_K: (K/S)/(128*SUBS) must be a multiple of WGsPerOutputTile"
+            if chunks // s < self.kWgsPerOutputTile:
+                return "SPLIT_K: not even one k group per warp group"
+        err = self._fitted(m, n, k).plan(m, n, k).error
+        return err
+
+    def dynamic_smem_bytes(self, m: int, k: int) -> int:
+        plan = self._fitted(m, 128, k).plan(m, 128, k)
+        return plan.smem_bytes
+
+
+# ---------------------------------------------------------------------------
+# Problem / plan
+# ---------------------------------------------------------------------------
+
+@dataclass
+class Problem:
+    """The reference's ``decode_gemm::Problem`` (kernels/decode_gemm.cuh:352-363).
+
+    Tensor fields take torch tensors or raw device pointers (int).  ``status``
+    (a B200 addition) is an optional device int32 the kernel sets on a
+    bounded-wait timeout.
+    """
+
+    M: int = 0
+    N: int = 0
+    K: int = 0
+    activation: object = None
+    weight: object = None
+    weight_scales: object = None
+    activation_scales: object = None
+    output: object = None
+    splitk_ws: object = None
+    splitk_sem: object = None
+    status: object = None
+
+    def to_dg(self) -> DgProblem:
+        return DgProblem(self.M, self.N, self.K, _ptr(self.activation), _ptr(self.weight),
+                         _ptr(self.weight_scales), _ptr(self.activation_scales), _ptr(self.output),
+                         _ptr(self.splitk_ws), _ptr(self.splitk_sem), _ptr(self.status))
+
+
+@dataclass
+class LaunchPlan:
+    """The reference's ``LaunchPlan`` (kernels/decode_gemm.cuh:373-380) plus B200 fields."""
+
+    grid: tuple = (0, 0, 0)
+    block: tuple = (0, 0, 0)
+    smem_bytes: int = 0
+    num_output_tiles: int = 0
+    padded_n: int = 0
+    error: Optional[str] = None
+    stages: int = 0
+    n_mma: int = 0
+    mma_m: int = 0
+    epi_warps: int = 0
+    num_ctas: int = 0
+    max_slabs: int = 1
+    ws_floats: int = 0
+    sem_ints: int = 0
+
+    @classmethod
+    def _from_info(cls, info: DgPlanInfo) -> "LaunchPlan":
+        err = info.error.decode() or None
+        return cls(grid=(info.grid_x, info.grid_y, info.grid_z), block=(info.block_x, 1, 1),
+                   smem_bytes=info.smem_bytes, num_output_tiles=info.num_output_tiles,
+                   padded_n=info.padded_n, error=err, stages=info.stages, n_mma=info.n_mma,
+                   mma_m=info.mma_m, epi_warps=info.epi_warps, num_ctas=info.num_ctas,
+                   max_slabs=info.max_slabs, ws_floats=info.ws_floats, sem_ints=info.sem_ints)
+
+
+def _b200(cfg, p: Problem) -> B200Config:
+    if isinstance(cfg, KernelConfig):
+        return cfg._fitted(p.M, p.N, p.K)
+    return cfg
+
+
+def make_launch_plan(cfg, p: Problem) -> LaunchPlan:
+    if isinstance(cfg, KernelConfig):
+        ref_err = cfg.validate(p.M, p.N, p.K)
+        plan = _b200(cfg, p).plan(p.M, p.N, p.K)
+        if ref_err is not None:
+            plan.error = ref_err
+        return plan
+    return cfg.plan(p.M, p.N, p.K)
+
+
+def make_weight_tma(cfg, p: Problem) -> TensorMap:
+    m = TensorMap()
+    rc = _lib.lib().dg_make_weight_map(ctypes.byref(_b200(cfg, p).to_dg()), _ptr(p.weight), p.N, p.K, m)
+    if rc != 0:
+        raise RuntimeError(f"cuTensorMapEncodeTiled(weight) failed: cudaError {rc}")
+    return m
+
+
+def make_activation_tma(cfg, p: Problem) -> TensorMap:
+    m = TensorMap()
+    rc = _lib.lib().dg_make_activation_map(ctypes.byref(_b200(cfg, p).to_dg()), _ptr(p.activation), p.M,
+                                            p.K, m)
+    if rc != 0:
+        raise RuntimeError(f"cuTensorMapEncodeTiled(activation) failed: cudaError {rc}")
+    return m
+
+
+def launch_with_maps(cfg, p: Problem, w_map: TensorMap, a_map: TensorMap, stream=None,
+                     pdl_attr: Optional[bool] = None) -> int:
+    """Launch with pre-built maps; returns a cudaError_t value.
+
+    ``pdl_attr`` None follows the configuration's PDL switch (the reference's
+    launch_with_maps); True/False sets programmatic stream serialization
+    explicitly (the reference harness's direct launch).
+    """
+    if isinstance(cfg, KernelConfig) and cfg.validate(p.M, p.N, p.K) is not None:
+        return CUDA_ERROR_INVALID_VALUE
+    b = _b200(cfg, p)
+    attr = b.pdl if pdl_attr is None else pdl_attr
+    if isinstance(cfg, KernelConfig) and pdl_attr is None:
+        attr = cfg.PDL
+    return _lib.lib().dg_launch_with_maps(ctypes.byref(b.to_dg()), ctypes.byref(p.to_dg()), w_map, a_map,
+                                          _stream_handle(stream), int(bool(attr)))
+
+
+def launch(cfg, p: Problem, stream=None) -> int:
+    """Encode both tensor maps, then launch (reference ``launch<Cfg>``)."""
+    if isinstance(cfg, KernelConfig):
+        if cfg.validate(p.M, p.N, p.K) is not None:
+            return CUDA_ERROR_INVALID_VALUE
+        if cfg.kSplitKCta and (p.splitk_ws is None or p.splitk_sem is None):
+            return CUDA_ERROR_INVALID_VALUE
+        # Trigger follows PDL or EPI_OVERLAP; the launch attribute follows PDL
+        # only (kernels/decode_gemm.cuh:1139-1144).
+        return launch_with_maps(cfg, p, make_weight_tma(cfg, p), make_activation_tma(cfg, p), stream,
+                                pdl_attr=bool(cfg.PDL))
+    return _lib.lib().dg_launch(ctypes.byref(cfg.to_dg()), ctypes.byref(p.to_dg()), _stream_handle(stream))
+
+
+# ---------------------------------------------------------------------------
+# Prepack (kernels/weight_prepack.cuh)
+# ---------------------------------------------------------------------------
+
+def padded_n(n: int, output_rows_per_cta: int) -> int:
+    return (n + output_rows_per_cta - 1) // output_rows_per_cta * output_rows_per_cta
+
+
+def packed_weight_bytes(n: int, k: int, output_rows_per_cta: int) -> int:
+    return padded_n(n, output_rows_per_cta) * k
+
+
+def launch_prepack_weight(output_rows_per_cta: int, output_tiles_per_cta: int, source, destination,
+                          n: int, k: int, stream=None, layout: int = LAYOUT_PACKED) -> int:
+    """``prepack::launch_prepack_weight<BM, TILES>`` (TILES does not change the layout)."""
+    if k % K_BLOCK != 0:
+        return CUDA_ERROR_INVALID_VALUE
+    del output_tiles_per_cta
+    return _lib.lib().dg_prepack_weight(_ptr(source), _ptr(destination), n, k, output_rows_per_cta, layout,
+                                        _stream_handle(stream))
+
+
+def prepack_weight(weight, block_n: int, layout: int = LAYOUT_PACKED, stream=None):
+    """torch convenience: returns a new uint8 tensor in ``layout``."""
+    import torch
+    n, k = weight.shape
+    out = torch.empty(packed_weight_bytes(n, k, block_n), dtype=torch.uint8, device=weight.device)
+    rc = launch_prepack_weight(block_n, 1, weight, out, n, k, stream, layout)
+    if rc != 0:
+        raise RuntimeError(f"prepack failed: cudaError {rc}")
+    return out
+
+
+def status_string(code: int) -> str:
+    return _lib.lib().dg_status_string(code).decode()
+
+
+def flush_l2(buf, stream=None) -> None:
+    rc = _lib.lib().dg_flush_l2(_ptr(buf), buf.numel() * buf.element_size(), _stream_handle(stream))
+    if rc != 0:
+        raise RuntimeError(f"flush failed: cudaError {rc}")
+
+
+# ---------------------------------------------------------------------------
+# One-call torch entry point
+# ---------------------------------------------------------------------------
+
+@dataclass
+class _Workspace:
+    ws: object = None
+    sem: object = None
+    status: object = None
+    ws_floats: int = 0
+    sem_ints: int = 0
+
+
+_WORKSPACES: dict = {}
+
+
+def _workspace(device, ws_floats: int, sem_ints: int) -> _Workspace:
+    import torch
+    key = (device.type, device.index)
+    w = _WORKSPACES.get(key)
+    if w is None:
+        w = _Workspace(status=torch.zeros(1, dtype=torch.int32, device=device))
+        _WORKSPACES[key] = w
+    if ws_floats > w.ws_floats:
+        w.ws = torch.empty(ws_floats, dtype=torch.float32, device=device)
+        w.ws_floats = ws_floats
+    if sem_ints > w.sem_ints:
+        w.sem = torch.zeros(sem_ints, dtype=torch.int32, device=device)
+        w.sem_ints = sem_ints
+    return w
+
+
+def fp8_decode_gemm(act, act_scales, weight, weight_scales, out=None, config: Optional[B200Config] = None,
+                    n: Optional[int] = None, stream=None):
+    """``out[M,N] = act[M,K] . W[N,K]^T`` with per-128 block scales, bf16 out.
+
+    ``act`` and ``weight`` are uint8 (e4m3 bits) or float8_e4m3fn tensors on
+    the GPU; ``weight`` is in ``config.layout`` (raw ``[N,K]`` by default, or
+    the packed byte buffer with ``n`` given).  The split-K workspace and the
+    ticket array are kept per device and reused.
+    """
+    import torch
+    m, k = act.shape
+    if n is None:
+        n = weight.shape[0]
+    if config is None:
+        config = default_config(m, n, k)
+    plan = config.plan(m, n, k)
+    if plan.error is not None:
+        raise ValueError(plan.error)
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=act.device)
+    w = _workspace(act.device, plan.ws_floats, plan.sem_ints)
+    p = Problem(m, n, k, act, weight, weight_scales, act_scales, out, w.ws, w.sem, w.status)
+    if stream is None:
+        stream = torch.cuda.current_stream(act.device)
+    rc = launch(config, p, stream)
+    if rc != 0:
+        raise RuntimeError(f"decode GEMM launch failed: cudaError {rc}")
+    return out

@@ -1,0 +1,123 @@
+"""ctypes binding of ``libdecode_gemm_b200.so`` (include/decode_gemm_b200.h).
+
+The library is the product; there is no fallback.  ``lib()`` raises when the
+shared object is missing or cannot be loaded, so a GPU run without the built
+extension fails loudly instead of computing anything elsewhere.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libdecode_gemm_b200.so")
+
+ABI_VERSION = 1
+
+LAYOUT_RAW = 0
+LAYOUT_PACKED = 1
+LAYOUT_PACKED_SWIZZLED = 2
+
+FLAG_INJECT_TIMEOUT = 2
+
+STATUS_OK = 0
+ERR_INJECTED_TIMEOUT = 0x51
+
+# Every symbol include/decode_gemm_b200.h declares.
+EXPORTED_SYMBOLS = (
+    "dg_abi_version", "dg_plan", "dg_make_weight_map", "dg_make_activation_map",
+    "dg_launch_with_maps", "dg_launch", "dg_prepack_weight", "dg_padded_n",
+    "dg_packed_weight_bytes", "dg_status_string", "dg_flush_l2",
+)
+
+
+class DgConfig(ctypes.Structure):
+    _fields_ = [
+        ("m_tile", ctypes.c_int),
+        ("block_n", ctypes.c_int),
+        ("subs", ctypes.c_int),
+        ("stages", ctypes.c_int),
+        ("layout", ctypes.c_int),
+        ("pdl", ctypes.c_int),
+        ("split_k", ctypes.c_int),
+        ("grid_ctas", ctypes.c_int),
+        ("epi_warps", ctypes.c_int),
+        ("flags", ctypes.c_int),
+        ("timeout_ns", ctypes.c_ulonglong),
+    ]
+
+
+class DgProblem(ctypes.Structure):
+    _fields_ = [
+        ("M", ctypes.c_int),
+        ("N", ctypes.c_int),
+        ("K", ctypes.c_int),
+        ("activation", ctypes.c_void_p),
+        ("weight", ctypes.c_void_p),
+        ("weight_scales", ctypes.c_void_p),
+        ("activation_scales", ctypes.c_void_p),
+        ("output", ctypes.c_void_p),
+        ("splitk_ws", ctypes.c_void_p),
+        ("splitk_sem", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+    ]
+
+
+class DgPlanInfo(ctypes.Structure):
+    _fields_ = [
+        ("grid_x", ctypes.c_uint),
+        ("grid_y", ctypes.c_uint),
+        ("grid_z", ctypes.c_uint),
+        ("block_x", ctypes.c_uint),
+        ("smem_bytes", ctypes.c_uint),
+        ("num_output_tiles", ctypes.c_int),
+        ("padded_n", ctypes.c_int),
+        ("stages", ctypes.c_int),
+        ("n_mma", ctypes.c_int),
+        ("mma_m", ctypes.c_int),
+        ("epi_warps", ctypes.c_int),
+        ("num_ctas", ctypes.c_int),
+        ("max_slabs", ctypes.c_int),
+        ("ws_floats", ctypes.c_ulonglong),
+        ("sem_ints", ctypes.c_int),
+        ("error", ctypes.c_char * 96),
+    ]
+
+
+TensorMap = ctypes.c_uint8 * 128
+
+_LIB = None
+
+
+def lib():
+    """Load the library (raises if it has not been built)."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build it with `python -m decode_opt_b200.build` "
+            "(there is no non-CUDA implementation of this operator)")
+    L = ctypes.CDLL(LIB_PATH)
+    cfgp = ctypes.POINTER(DgConfig)
+    probp = ctypes.POINTER(DgProblem)
+    L.dg_abi_version.restype = ctypes.c_int
+    L.dg_plan.argtypes = [cfgp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(DgPlanInfo)]
+    L.dg_make_weight_map.argtypes = [cfgp, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    L.dg_make_activation_map.argtypes = [cfgp, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    L.dg_launch_with_maps.argtypes = [cfgp, probp, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                      ctypes.c_int]
+    L.dg_launch.argtypes = [cfgp, probp, ctypes.c_void_p]
+    L.dg_prepack_weight.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                    ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    L.dg_padded_n.argtypes = [ctypes.c_int, ctypes.c_int]
+    L.dg_packed_weight_bytes.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    L.dg_packed_weight_bytes.restype = ctypes.c_ulonglong
+    L.dg_status_string.argtypes = [ctypes.c_int]
+    L.dg_status_string.restype = ctypes.c_char_p
+    L.dg_flush_l2.argtypes = [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_void_p]
+    if L.dg_abi_version() != ABI_VERSION:
+        raise RuntimeError(f"{LIB_PATH}: ABI version {L.dg_abi_version()} != {ABI_VERSION}")
+    _LIB = L
+    return L

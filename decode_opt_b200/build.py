@@ -1,0 +1,62 @@
+"""Build recipe for the in-tree sm_100a libraries.
+
+``python -m decode_opt_b200.build`` compiles ``csrc/dg_capi.cu`` into
+``decode_opt_b200/libdecode_gemm_b200.so`` for ``sm_100a`` only.  The library
+links the CUDA runtime statically and resolves ``cuTensorMapEncodeTiled``
+through the runtime's driver entry-point query, so it loads on hosts without a
+GPU (the CPU test suite checks its exported symbols there).
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+INCLUDE = os.path.join(ROOT, "include")
+LIB_NAME = "libdecode_gemm_b200.so"
+LIB_PATH = os.path.join(HERE, LIB_NAME)
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc() -> str:
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    cand = os.path.join(cuda_home, "bin", "nvcc")
+    return cand if os.path.exists(cand) else (shutil.which("nvcc") or "nvcc")
+
+
+def _sources():
+    return [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC))] + [
+        os.path.join(INCLUDE, f) for f in sorted(os.listdir(INCLUDE))]
+
+
+def needs_build(target: str = LIB_PATH) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(s) > t for s in _sources())
+
+
+def build(verbose: bool = False, ptxas_verbose: bool = False, force: bool = False) -> str:
+    if not force and not needs_build():
+        return LIB_PATH
+    cmd = [nvcc(), "-std=c++17", "-O3", "-lineinfo", *ARCH_FLAGS,
+           "-Xcompiler", "-fPIC", "-shared", "-cudart", "static",
+           "-I", CSRC, "-I", INCLUDE,
+           os.path.join(CSRC, "dg_capi.cu"), "-o", LIB_PATH + ".tmp"]
+    if ptxas_verbose:
+        cmd[1:1] = ["-Xptxas", "-v"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(LIB_PATH + ".tmp", LIB_PATH)
+    return LIB_PATH
+
+
+if __name__ == "__main__":
+    build(verbose=True, ptxas_verbose="-v" in sys.argv, force="-f" in sys.argv)

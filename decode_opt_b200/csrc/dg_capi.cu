@@ -1,0 +1,255 @@
+// SPDX-License-Identifier: MIT
+//
+// dg_capi.cu -- libdecode_gemm_b200.so: the C ABI declared in
+// include/decode_gemm_b200.h, over the sm_100a kernel (dg_kernel.cuh) and the
+// host planner (dg_host.cuh).  Also holds the weight prepack kernel and the
+// L2 flush helper.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+
+#include "decode_gemm_b200.h"
+#include "dg_host.cuh"
+
+namespace {
+
+using dg::Config;
+using dg::KernelFn;
+using dg::Plan;
+
+Config to_config(const dg_config* c) {
+  Config out;
+  out.m_tile = c->m_tile;
+  out.block_n = c->block_n;
+  out.subs = c->subs;
+  out.stages = c->stages;
+  out.layout = c->layout;
+  out.pdl = c->pdl;
+  out.split_k = c->split_k;
+  out.grid_ctas = c->grid_ctas;
+  out.epi_warps = c->epi_warps;
+  out.flags = c->flags;
+  out.timeout_ns = c->timeout_ns;
+  return out;
+}
+
+int current_sm_count() {
+  int dev = 0;
+  int sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return sms;
+}
+
+// One kernel per (MMA M, M_TILE, epilogue warps); everything else is runtime.
+struct KernelEntry {
+  KernelFn fn;
+  std::atomic<int> smem_high_water;
+};
+
+template <int MMA_M, int MT, int EPI>
+KernelEntry* entry() {
+  static KernelEntry e{dg::kernel_ptr<MMA_M, MT, EPI>(), {0}};
+  return &e;
+}
+
+template <int MMA_M, int EPI>
+KernelEntry* select_m_tile(int m_tile) {
+  switch (m_tile) {
+    case 8: return entry<MMA_M, 8, EPI>();
+    case 16: return entry<MMA_M, 16, EPI>();
+    case 32: return entry<MMA_M, 32, EPI>();
+    case 64: return entry<MMA_M, 64, EPI>();
+    case 128: return entry<MMA_M, 128, EPI>();
+    default: return nullptr;
+  }
+}
+
+KernelEntry* select_kernel(int mma_m, int m_tile, int epi) {
+  if (mma_m == 64) return epi == 8 ? select_m_tile<64, 8>(m_tile) : select_m_tile<64, 4>(m_tile);
+  return epi == 8 ? select_m_tile<128, 8>(m_tile) : select_m_tile<128, 4>(m_tile);
+}
+
+void fill_info(const Plan& plan, dg_plan_info* out) {
+  std::memset(out, 0, sizeof(*out));
+  if (plan.error != nullptr) {
+    std::snprintf(out->error, sizeof(out->error), "%s", plan.error);
+    return;
+  }
+  out->grid_x = plan.grid.x;
+  out->grid_y = plan.grid.y;
+  out->grid_z = plan.grid.z;
+  out->block_x = plan.block.x;
+  out->smem_bytes = plan.smem_bytes;
+  out->num_output_tiles = plan.params.num_tiles;
+  out->padded_n = plan.padded_n;
+  out->stages = plan.params.stages;
+  out->n_mma = plan.params.n_mma;
+  out->mma_m = plan.mma_m;
+  out->epi_warps = plan.epi_warps;
+  out->num_ctas = plan.params.num_ctas;
+  out->max_slabs = plan.max_slabs;
+  out->ws_floats = plan.ws_floats;
+  out->sem_ints = plan.sem_ints;
+}
+
+int launch_impl(const dg_config* cfg, const dg_problem* prob, const CUtensorMap* w_map,
+                const CUtensorMap* a_map, cudaStream_t stream, bool pdl_attr) {
+  if (cfg == nullptr || prob == nullptr) return cudaErrorInvalidValue;
+  const Config c = to_config(cfg);
+  Plan plan = dg::make_plan(c, prob->M, prob->N, prob->K, current_sm_count());
+  if (plan.error != nullptr) return cudaErrorInvalidValue;
+  dg::KernelParams& p = plan.params;
+  p.output = static_cast<__nv_bfloat16*>(prob->output);
+  p.w_scales = prob->weight_scales;
+  p.a_scales = prob->activation_scales;
+  p.ws = prob->splitk_ws;
+  p.sem = prob->splitk_sem;
+  p.status = prob->status;
+  p.weight = static_cast<const uint8_t*>(prob->weight);
+  const cudaError_t buf_err = dg::check_buffers(plan, p);
+  if (buf_err != cudaSuccess) return buf_err;
+  KernelEntry* k = select_kernel(plan.mma_m, c.m_tile, plan.epi_warps);
+  if (k == nullptr) return cudaErrorInvalidValue;
+  const cudaError_t attr_err =
+      dg::ensure_smem(reinterpret_cast<const void*>(k->fn), plan.smem_bytes, &k->smem_high_water);
+  if (attr_err != cudaSuccess) return attr_err;
+  return dg::launch_kernel(k->fn, plan, p, *w_map, *a_map, stream, pdl_attr);
+}
+
+// raw [n,k] -> [tile][kb][row][128] (optionally 128-byte swizzled), one
+// 16-byte vector per thread, grid-stride; rows >= n are zero.
+__global__ void prepack_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int n, int k,
+                               int block_n, int num_tiles, int swizzle) {
+  const uint32_t vec_per_row = static_cast<uint32_t>(k) / 16u;
+  const uint32_t kb_count = static_cast<uint32_t>(k) / 128u;
+  const size_t total = static_cast<size_t>(num_tiles) * block_n * vec_per_row;
+  for (size_t v = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    // v enumerates destination vectors: ((tile*KB + kb)*BM + r)*8 + c
+    const uint32_t c = static_cast<uint32_t>(v & 7u);
+    const size_t rest = v >> 3;
+    const uint32_t r = static_cast<uint32_t>(rest % block_n);
+    const size_t tk = rest / block_n;
+    const uint32_t kb = static_cast<uint32_t>(tk % kb_count);
+    const uint32_t tile = static_cast<uint32_t>(tk / kb_count);
+    const uint32_t row = tile * block_n + r;
+    const uint32_t src_c = swizzle ? (c ^ (r & 7u)) : c;   // dst chunk c holds src chunk c^(r%8)
+    uint4 val = make_uint4(0u, 0u, 0u, 0u);
+    if (row < static_cast<uint32_t>(n)) val = src[static_cast<size_t>(row) * vec_per_row + kb * 8u + src_c];
+    dst[v] = val;
+  }
+}
+
+__global__ void flush_kernel(uint4* buf, size_t n16) {
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    buf[i] = make_uint4(static_cast<uint32_t>(i), 1u, 2u, 3u);
+}
+
+}  // namespace
+
+extern "C" {
+
+int dg_abi_version(void) { return DG_ABI_VERSION; }
+
+int dg_plan(const dg_config* cfg, int M, int N, int K, dg_plan_info* out) {
+  if (cfg == nullptr || out == nullptr) return cudaErrorInvalidValue;
+  const Plan plan = dg::make_plan(to_config(cfg), M, N, K, current_sm_count());
+  fill_info(plan, out);
+  return plan.error == nullptr ? 0 : static_cast<int>(cudaErrorInvalidValue);
+}
+
+int dg_make_weight_map(const dg_config* cfg, const void* weight, int N, int K, void* map128) {
+  if (cfg == nullptr || map128 == nullptr) return cudaErrorInvalidValue;
+  const Config c = to_config(cfg);
+  if (dg::check_config(c) != nullptr || N < 1 || K < 128 || K % 128 != 0) return cudaErrorInvalidValue;
+  return dg::make_weight_map(static_cast<CUtensorMap*>(map128), c, weight, N, K);
+}
+
+int dg_make_activation_map(const dg_config* cfg, const void* activation, int M, int K, void* map128) {
+  if (cfg == nullptr || map128 == nullptr) return cudaErrorInvalidValue;
+  const Config c = to_config(cfg);
+  if (dg::check_config(c) != nullptr || M < 1 || M > c.m_tile || K < 128 || K % 128 != 0)
+    return cudaErrorInvalidValue;
+  return dg::make_activation_map(static_cast<CUtensorMap*>(map128), c, activation, M, K);
+}
+
+int dg_launch_with_maps(const dg_config* cfg, const dg_problem* p, const void* weight_map128,
+                        const void* activation_map128, void* stream, int pdl_attr) {
+  if (weight_map128 == nullptr || activation_map128 == nullptr) return cudaErrorInvalidValue;
+  return launch_impl(cfg, p, static_cast<const CUtensorMap*>(weight_map128),
+                     static_cast<const CUtensorMap*>(activation_map128),
+                     static_cast<cudaStream_t>(stream), pdl_attr != 0);
+}
+
+int dg_launch(const dg_config* cfg, const dg_problem* p, void* stream) {
+  if (cfg == nullptr || p == nullptr) return cudaErrorInvalidValue;
+  const Config c = to_config(cfg);
+  if (dg::check_config(c) != nullptr || p->M < 1 || p->M > c.m_tile || p->N < 1 || p->K < 128 ||
+      p->K % 128 != 0)
+    return cudaErrorInvalidValue;
+  CUtensorMap w{};
+  CUtensorMap a{};
+  cudaError_t err = dg::make_weight_map(&w, c, p->weight, p->N, p->K);
+  if (err != cudaSuccess) return err;
+  err = dg::make_activation_map(&a, c, p->activation, p->M, p->K);
+  if (err != cudaSuccess) return err;
+  return launch_impl(cfg, p, &w, &a, static_cast<cudaStream_t>(stream), c.pdl != 0);
+}
+
+int dg_prepack_weight(const void* src, void* dst, int n, int k, int block_n, int layout, void* stream) {
+  if (src == nullptr || dst == nullptr || n < 1 || k < 128 || k % 128 != 0 || block_n < 8 ||
+      block_n > 128 || block_n % 8 != 0)
+    return cudaErrorInvalidValue;
+  if (layout != DG_LAYOUT_PACKED && layout != DG_LAYOUT_PACKED_SWIZZLED) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(src) & 15u) != 0 || (reinterpret_cast<uintptr_t>(dst) & 15u) != 0)
+    return cudaErrorInvalidValue;
+  const int tiles = (n + block_n - 1) / block_n;
+  const size_t total = static_cast<size_t>(tiles) * block_n * (k / 16);
+  const int threads = 256;
+  int sms = current_sm_count();
+  if (sms <= 0) sms = 148;
+  const size_t want = (total + threads - 1) / threads;
+  const unsigned blocks = static_cast<unsigned>(want < static_cast<size_t>(sms) * 16 ? want : static_cast<size_t>(sms) * 16);
+  prepack_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<uint4*>(dst), n, k, block_n, tiles,
+      layout == DG_LAYOUT_PACKED_SWIZZLED ? 1 : 0);
+  return cudaGetLastError();
+}
+
+int dg_padded_n(int n, int block_n) { return block_n > 0 ? dg::padded_n(n, block_n) : 0; }
+
+unsigned long long dg_packed_weight_bytes(int n, int k, int block_n) {
+  return block_n > 0 ? static_cast<unsigned long long>(dg::packed_weight_bytes(n, k, block_n)) : 0ull;
+}
+
+const char* dg_status_string(int code) {
+  switch (code) {
+    case DG_STATUS_OK: return "ok";
+    case DG_ERR_PRODUCER_EMPTY_WAIT: return "producer: timed out waiting for a free smem stage";
+    case DG_ERR_MMA_FULL_WAIT: return "mma: timed out waiting for a TMA stage";
+    case DG_ERR_MMA_ACCUM_WAIT: return "mma: timed out waiting for a free TMEM accumulator";
+    case DG_ERR_EPILOGUE_ACCUM_WAIT: return "epilogue: timed out waiting for a TMEM accumulator";
+    case DG_ERR_DRAIN_TMA: return "teardown: TMA copies did not complete in time";
+    case DG_ERR_DRAIN_MMA: return "teardown: MMAs did not complete in time";
+    case DG_ERR_INJECTED_TIMEOUT: return "injected timeout (test hook)";
+    case DG_ERR_BAD_LAUNCH_SHAPE: return "launch grid/block does not match the plan";
+    default: return "unknown status";
+  }
+}
+
+int dg_flush_l2(void* buf, unsigned long long bytes, void* stream) {
+  if (buf == nullptr || bytes < 16) return cudaErrorInvalidValue;
+  int sms = current_sm_count();
+  if (sms <= 0) sms = 148;
+  flush_kernel<<<static_cast<unsigned>(sms) * 4u, 512, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint4*>(buf), static_cast<size_t>(bytes / 16));
+  return cudaGetLastError();
+}
+
+}  // extern "C"

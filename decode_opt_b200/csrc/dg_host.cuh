@@ -1,0 +1,316 @@
+// SPDX-License-Identifier: MIT
+//
+// dg_host.cuh -- host side of the B200 decode GEMM: configuration checking,
+// the launch plan (grid, smem carve-up, stream-K ranges, workspace needs),
+// tensor-map encoding and the launch itself.  Shared by the C-ABI library
+// (dg_capi.cu) and the header-only C++ drop-in (include/decode_gemm.cuh).
+//
+// Mirrors the host half of the reference's kernels/decode_gemm.cuh
+// (validate :319-346, make_weight_tma :413-447, make_activation_tma :449-468,
+// make_launch_plan :1086-1096, ensure_smem_attribute :1100-1109,
+// launch_with_maps :1113-1147) for the sm_100a kernel in dg_kernel.cuh.
+//
+// cuTensorMapEncodeTiled is resolved through cudaGetDriverEntryPoint, so
+// libraries built from this header do not link libcuda and load on machines
+// without a GPU driver (they then report cudaErrorInsufficientDriver or
+// cudaErrorNoDevice at call time).
+
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstddef>
+#include <cstdint>
+#include <cstring>
+
+#include "dg_kernel.cuh"
+
+namespace dg {
+
+// Runtime configuration.  The reference's compile-time KernelConfig knobs map
+// onto it (include/decode_gemm.cuh); grid_ctas selects the B200 stream-K
+// schedule.
+struct Config {
+  int m_tile = 8;         // compile-time bound on M: 8, 16, 32, 64, 128
+  int block_n = 128;      // BM: output rows per tile; multiple of 8, <= 128
+  int subs = 2;           // 128-K blocks per pipeline stage: 1, 2 or 4
+  int stages = 0;         // smem ring depth; 0 = as many as fit
+  int layout = kLayoutRaw;
+  int pdl = 0;            // 1: trigger dependents + programmatic serialization
+  int split_k = 1;        // reference S (grid_ctas == 0 only): 1, 2, 4, 8, ...
+  int grid_ctas = 0;      // 0: grid = tiles x split_k; > 0: stream-K over this
+                          // many CTAs; < 0: stream-K over one CTA per SM
+  int epi_warps = 0;      // 4 or 8; 0 = 4 for m_tile <= 32, else 8
+  unsigned long long timeout_ns = 0;  // bounded-wait limit; 0 = 2 s
+  int flags = 0;          // extra kernel flags (kFlagInjectTimeout: tests only)
+};
+
+struct Plan {
+  KernelParams params{};
+  dim3 grid{0, 0, 0};
+  dim3 block{0, 0, 0};
+  uint32_t smem_bytes = 0;
+  int mma_m = 0;
+  int epi_warps = 0;
+  int max_slabs = 1;        // workspace slabs needed (1 = no split tile)
+  size_t ws_floats = 0;     // max_slabs * M * N when max_slabs > 1
+  int sem_ints = 0;         // num_tiles when max_slabs > 1
+  int padded_n = 0;
+  const char* error = nullptr;
+};
+
+inline int effective_epi_warps(const Config& c) {
+  if (c.epi_warps == 4 || c.epi_warps == 8) return c.epi_warps;
+  return c.m_tile <= 32 ? 4 : 8;
+}
+
+inline int mma_m_for(int block_n) { return block_n <= 64 ? 64 : 128; }
+
+inline int n_mma_for(int m) {
+  const int r = ((m + 15) / 16) * 16;
+  return r < 16 ? 16 : r;
+}
+
+inline int padded_n(int n, int block_n) { return ((n + block_n - 1) / block_n) * block_n; }
+
+inline size_t packed_weight_bytes(int n, int k, int block_n) {
+  return static_cast<size_t>(padded_n(n, block_n)) * static_cast<size_t>(k);
+}
+
+inline int accum_buffers(int m_tile) {
+  const int cols = m_tile < 16 ? 16 : m_tile;
+  return std::min(512 / cols, kMaxAccumBuffers);
+}
+
+// Static configuration checks (no shape).
+inline const char* check_config(const Config& c) {
+  if (!(c.m_tile == 8 || c.m_tile == 16 || c.m_tile == 32 || c.m_tile == 64 || c.m_tile == 128))
+    return "m_tile must be 8, 16, 32, 64 or 128";
+  if (c.block_n < 8 || c.block_n > 128 || c.block_n % 8 != 0)
+    return "block_n (BM) must be a multiple of 8 in [8, 128]";
+  if (!(c.subs == 1 || c.subs == 2 || c.subs == 4)) return "subs must be 1, 2 or 4";
+  if (c.stages < 0 || c.stages > kMaxStages) return "stages must be in [0, 16]";
+  if (c.layout < kLayoutRaw || c.layout > kLayoutPackedSwizzled) return "unknown weight layout";
+  if (c.split_k < 1) return "split_k must be >= 1";
+  if (!(c.epi_warps == 0 || c.epi_warps == 4 || c.epi_warps == 8)) return "epi_warps must be 0, 4 or 8";
+  return nullptr;
+}
+
+// Full plan for one (M, N, K); `num_sms` sizes the stream-K grid when
+// grid_ctas < 0.  On failure plan.error names the violated rule.
+inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms) {
+  Plan plan;
+  if ((plan.error = check_config(c)) != nullptr) return plan;
+  if (M < 1 || M > c.m_tile) return plan.error = "M out of [1, m_tile]", plan;
+  if (N < 1) return plan.error = "N must be positive", plan;
+  if (K < kKBlock || K % kKBlock != 0) return plan.error = "K must be a positive multiple of 128", plan;
+  const int num_kb = K / kKBlock;
+  if (num_kb % c.subs != 0) return plan.error = "K/128 must be a multiple of subs", plan;
+  const int C = num_kb / c.subs;
+  const int T = (N + c.block_n - 1) / c.block_n;
+  const long long U = static_cast<long long>(T) * C;
+  if (U > (1ll << 40)) return plan.error = "problem too large", plan;
+
+  const int mma_m = mma_m_for(c.block_n);
+  const int n_mma = n_mma_for(M);
+  const int epi = effective_epi_warps(c);
+  const int bufs = accum_buffers(c.m_tile);
+  const uint32_t w_stage = static_cast<uint32_t>(c.subs * c.block_n * kKBlock);
+  const uint32_t a_stage = static_cast<uint32_t>(c.subs * n_mma * kKBlock);
+  const uint32_t pad = c.block_n < mma_m ? static_cast<uint32_t>((mma_m - c.block_n) * kKBlock) : 0u;
+  auto smem_for = [&](int stages) -> uint32_t {
+    const uint32_t w_region = ((stages * w_stage + pad) + 1023u) & ~1023u;
+    return 1024u + w_region + stages * a_stage + SmemBarriers::bytes(stages, bufs);
+  };
+  int stages = c.stages;
+  if (stages == 0) {
+    stages = 1;
+    while (stages < kMaxStages && smem_for(stages + 1) <= kMaxDynamicSmem) ++stages;
+  }
+  if (smem_for(stages) > kMaxDynamicSmem) return plan.error = "dynamic shared memory exceeds 227 KiB", plan;
+
+  long long G;
+  if (c.grid_ctas > 0) {
+    G = std::min<long long>(c.grid_ctas, U);
+    plan.grid = dim3(static_cast<unsigned>(G), 1u, 1u);
+  } else if (c.grid_ctas < 0) {
+    G = std::min<long long>(num_sms > 0 ? num_sms : 148, U);
+    plan.grid = dim3(static_cast<unsigned>(G), 1u, 1u);
+  } else {
+    if (C % c.split_k != 0) return plan.error = "split-K: (K/128)/subs must be a multiple of split_k", plan;
+    G = static_cast<long long>(T) * c.split_k;
+    if (T > 0x7fffffff || c.split_k > 65535) return plan.error = "grid too large", plan;
+    plan.grid = dim3(static_cast<unsigned>(T), static_cast<unsigned>(c.split_k), 1u);
+  }
+  int max_slabs = 1;
+  for (int t = 0; t < T; ++t) {
+    const long long first = cta_of_unit(static_cast<long long>(t) * C, G, U);
+    const long long last = cta_of_unit(static_cast<long long>(t) * C + C - 1, G, U);
+    max_slabs = std::max(max_slabs, static_cast<int>(last - first + 1));
+  }
+
+  KernelParams& p = plan.params;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.block_n = c.block_n;
+  p.subs = c.subs;
+  p.stages = stages;
+  p.layout = c.layout;
+  p.n_mma = n_mma;
+  p.num_tiles = T;
+  p.chunks_per_tile = C;
+  p.num_kb = num_kb;
+  p.num_scale_rows = (N + kKBlock - 1) / kKBlock;
+  p.num_ctas = static_cast<int>(G);
+  p.flags = (c.pdl ? kFlagPdlTrigger : 0) | (c.flags & ~kFlagPdlTrigger);
+  p.total_units = U;
+  p.w_stage_bytes = w_stage;
+  p.a_stage_bytes = a_stage;
+  p.w_region_bytes = ((stages * w_stage + pad) + 1023u) & ~1023u;
+  p.a_region_bytes = stages * a_stage;
+  p.smem_bytes = smem_for(stages);
+  p.timeout_ns = c.timeout_ns ? c.timeout_ns : kDefaultTimeoutNs;
+
+  plan.block = dim3(static_cast<unsigned>((2 + epi) * 32), 1u, 1u);
+  plan.smem_bytes = p.smem_bytes;
+  plan.mma_m = mma_m;
+  plan.epi_warps = epi;
+  plan.max_slabs = max_slabs;
+  plan.ws_floats = max_slabs > 1 ? static_cast<size_t>(max_slabs) * M * static_cast<size_t>(N) : 0;
+  plan.sem_ints = max_slabs > 1 ? T : 0;
+  plan.padded_n = T * c.block_n;
+  return plan;
+}
+
+// ----------------------------------------------------------- tensor maps ---
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_tiled_fn() {
+  static std::atomic<EncodeTiledFn> cached{nullptr};
+  EncodeTiledFn fn = cached.load(std::memory_order_acquire);
+  if (fn != nullptr) return fn;
+  void* sym = nullptr;
+  cudaDriverEntryPointQueryResult q{};
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &sym, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || sym == nullptr)
+    return nullptr;
+  fn = reinterpret_cast<EncodeTiledFn>(sym);
+  cached.store(fn, std::memory_order_release);
+  return fn;
+}
+
+// Weight map.  Both TMA layouts use a rank-4 map with box {128, BM, subs, 1}
+// so one copy lands subs*BM*128 bytes in [subs][BM][128] order with the
+// 128-byte swizzle the MMA descriptors expect:
+//   raw    dims {128, N, K/128, 1}, byte strides {K, 128, N*K}: dim 0 and 2
+//          walk K in 128-byte blocks, dim 1 walks rows (the K-block split
+//          keeps the inner box at the 128-byte swizzle span);
+//   packed dims {128, BM, K/128, tiles}, strides {128, BM*128, (K/128)*BM*128}.
+// The swizzled-packed layout is read with bulk copies and needs no map.
+inline cudaError_t make_weight_map(CUtensorMap* map, const Config& c, const void* weight, int N, int K) {
+  std::memset(map, 0, sizeof(*map));
+  if (c.layout == kLayoutPackedSwizzled) return cudaSuccess;
+  EncodeTiledFn encode = encode_tiled_fn();
+  if (encode == nullptr) return cudaErrorInsufficientDriver;
+  const cuuint64_t kb = static_cast<cuuint64_t>(K / kKBlock);
+  cuuint64_t dims[4];
+  cuuint64_t strides[3];
+  if (c.layout == kLayoutRaw) {
+    dims[0] = kKBlock;
+    dims[1] = static_cast<cuuint64_t>(N);
+    dims[2] = kb;
+    dims[3] = 1;
+    strides[0] = static_cast<cuuint64_t>(K);
+    strides[1] = kKBlock;
+    strides[2] = static_cast<cuuint64_t>(N) * static_cast<cuuint64_t>(K);
+  } else {
+    const cuuint64_t tiles = static_cast<cuuint64_t>((N + c.block_n - 1) / c.block_n);
+    dims[0] = kKBlock;
+    dims[1] = static_cast<cuuint64_t>(c.block_n);
+    dims[2] = kb;
+    dims[3] = tiles;
+    strides[0] = kKBlock;
+    strides[1] = static_cast<cuuint64_t>(c.block_n) * kKBlock;
+    strides[2] = kb * c.block_n * kKBlock;
+  }
+  const cuuint32_t box[4] = {kKBlock, static_cast<cuuint32_t>(c.block_n), static_cast<cuuint32_t>(c.subs), 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(weight), dims, strides,
+                            box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// Activation map: dims {128, M, K/128}, strides {K, 128}, box {128, n_mma,
+// subs}.  Rows M..n_mma-1 of the box are out of range and land as zeros.
+inline cudaError_t make_activation_map(CUtensorMap* map, const Config& c, const void* act, int M, int K) {
+  std::memset(map, 0, sizeof(*map));
+  EncodeTiledFn encode = encode_tiled_fn();
+  if (encode == nullptr) return cudaErrorInsufficientDriver;
+  const cuuint64_t dims[3] = {kKBlock, static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(K / kKBlock)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(K), kKBlock};
+  const cuuint32_t box[3] = {kKBlock, static_cast<cuuint32_t>(n_mma_for(M)), static_cast<cuuint32_t>(c.subs)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(act), dims, strides, box,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// ---------------------------------------------------------------- launch ---
+using KernelFn = void (*)(KernelParams, CUtensorMap, CUtensorMap);
+
+template <int MMA_M, int M_TILE, int EPI>
+inline KernelFn kernel_ptr() {
+  return reinterpret_cast<KernelFn>(&dg_decode_gemm_kernel<MMA_M, M_TILE, EPI>);
+}
+
+// Raises the dynamic-smem limit of `fn` once per (kernel, size).  Unlike the
+// reference's single cached value per Cfg (kernels/decode_gemm.cuh:1100-1109)
+// this keeps the largest size set so far per kernel, so interleaved callers
+// with different M never lower it under each other.
+inline cudaError_t ensure_smem(const void* fn, uint32_t bytes, std::atomic<int>* high_water) {
+  int cur = high_water->load(std::memory_order_acquire);
+  if (cur >= static_cast<int>(bytes)) return cudaSuccess;
+  const cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(kMaxDynamicSmem));
+  if (err == cudaSuccess) high_water->store(static_cast<int>(kMaxDynamicSmem), std::memory_order_release);
+  return err;
+}
+
+// Checks the pointers a plan needs before anything is enqueued.
+inline cudaError_t check_buffers(const Plan& plan, const KernelParams& p) {
+  if (p.output == nullptr || p.w_scales == nullptr || p.a_scales == nullptr) return cudaErrorInvalidValue;
+  if (plan.max_slabs > 1 && (p.ws == nullptr || p.sem == nullptr)) return cudaErrorInvalidValue;
+  if (p.layout == kLayoutPackedSwizzled &&
+      (p.weight == nullptr || (reinterpret_cast<uintptr_t>(p.weight) & 15u) != 0))
+    return cudaErrorInvalidValue;
+  return cudaSuccess;
+}
+
+inline cudaError_t launch_kernel(KernelFn fn, const Plan& plan, const KernelParams& p, const CUtensorMap& w,
+                                 const CUtensorMap& a, cudaStream_t stream, bool pdl_attr) {
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1]{};
+  cfg.gridDim = plan.grid;
+  cfg.blockDim = plan.block;
+  cfg.dynamicSmemBytes = plan.smem_bytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 0;
+  if (pdl_attr) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, fn, p, w, a);
+}
+
+}  // namespace dg

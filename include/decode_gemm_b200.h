@@ -1,0 +1,150 @@
+/* SPDX-License-Identifier: MIT
+ *
+ * decode_gemm_b200.h -- C ABI of the B200 (sm_100a) FP8 decode GEMM library
+ * (libdecode_gemm_b200.so, built from decode_opt_b200/csrc/dg_capi.cu).
+ *
+ *   out[M,N] bf16 = act[M,K] e4m3 . W[N,K]^T e4m3, with per-128-K block scales
+ *   weight_scales[ceil(N/128), K/128] and activation_scales[M, K/128], fp32
+ *   accumulation, M = 1..128 (decode).
+ *
+ * Plain C: pointers, ints and sizes only.  All tensor pointers are device
+ * pointers owned by the caller; `stream` is a cudaStream_t (NULL = legacy
+ * default stream).  Functions return a cudaError_t value (0 = success,
+ * 1 = cudaErrorInvalidValue for a rejected configuration or shape), matching
+ * the reference's host API, which returns cudaError_t from launch() /
+ * launch_with_maps() / launch_prepack_weight().
+ *
+ * Each entry point replaces the reference interface named beside it
+ * (paths are inside the reference repository ziyuhuang123/decode_opt):
+ *
+ *   dg_plan                 decode_gemm::KernelConfig::validate +
+ *                           make_launch_plan   kernels/decode_gemm.cuh:319-346, 1086-1096
+ *   dg_make_weight_map      make_weight_tma     kernels/decode_gemm.cuh:413-447
+ *   dg_make_activation_map  make_activation_tma kernels/decode_gemm.cuh:449-468
+ *   dg_launch_with_maps     launch_with_maps    kernels/decode_gemm.cuh:1113-1147
+ *                           (and the harness's direct cudaLaunchKernelEx of
+ *                           fp8_decode_gemm<Cfg>, bench/variant_impl.cuh:136-165)
+ *   dg_launch               launch              kernels/decode_gemm.cuh:1150-1159
+ *   dg_prepack_weight       prepack::launch_prepack_weight kernels/weight_prepack.cuh:101-120
+ *   dg_padded_n             prepack::padded_n   kernels/weight_prepack.cuh:45-47
+ *   dg_packed_weight_bytes  prepack::packed_weight_bytes kernels/weight_prepack.cuh:50-52
+ *   dg_status_string        (new) text of the kernel's device status codes
+ *   dg_flush_l2             bench helper flush_l2_kernel bench/bench_decode.cu:473-476
+ */
+#ifndef DECODE_GEMM_B200_H_
+#define DECODE_GEMM_B200_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DG_ABI_VERSION 1
+
+/* Weight layouts. */
+#define DG_LAYOUT_RAW 0             /* W[N,K], K contiguous (checkpoint layout) */
+#define DG_LAYOUT_PACKED 1          /* [tile][k_block][BM rows][128 B], zero-padded rows
+                                       (the reference's prepack layout) */
+#define DG_LAYOUT_PACKED_SWIZZLED 2 /* same order, each 8-row group pre-swizzled for the
+                                       tcgen05 SWIZZLE_128B operand layout (B200 native) */
+
+/* Kernel flags (dg_config.flags). */
+#define DG_FLAG_INJECT_TIMEOUT 2 /* tests: one wait can never complete, so the bounded
+                                    wait expires and the kernel reports status 0x51 */
+
+/* Device status codes written to dg_problem.status (first error wins). */
+#define DG_STATUS_OK 0
+#define DG_ERR_PRODUCER_EMPTY_WAIT 0x11
+#define DG_ERR_MMA_FULL_WAIT 0x21
+#define DG_ERR_MMA_ACCUM_WAIT 0x22
+#define DG_ERR_EPILOGUE_ACCUM_WAIT 0x31
+#define DG_ERR_DRAIN_TMA 0x41
+#define DG_ERR_DRAIN_MMA 0x42
+#define DG_ERR_INJECTED_TIMEOUT 0x51
+#define DG_ERR_BAD_LAUNCH_SHAPE 0x61
+
+/* Runtime configuration.  Zero-initialise, then set fields. */
+typedef struct dg_config {
+  int m_tile;    /* bound on M: 8, 16, 32, 64 or 128 (reference M_TILE)               */
+  int block_n;   /* BM, output rows per tile: multiple of 8 in [8,128]
+                    (reference OUTPUT_ROWS_PER_CTA; 128 = one tcgen05 M=128 tile)     */
+  int subs;      /* 128-K blocks per pipeline stage: 1, 2, 4 (reference SUBS_PER_STAGE)*/
+  int stages;    /* smem ring depth, 0 = as many as fit in 227 KiB                     */
+  int layout;    /* DG_LAYOUT_*  (reference PREPACK: false = RAW, true = PACKED)       */
+  int pdl;       /* 1: griddepcontrol.launch_dependents after the last TMA, and
+                    dg_launch sets programmatic stream serialization (reference PDL)   */
+  int split_k;   /* reference SPLITK_FACTOR S >= 1, used when grid_ctas == 0            */
+  int grid_ctas; /* 0: grid = ceil(N/BM) x split_k (reference schedule);
+                    >0: stream-K over this many CTAs; <0: stream-K, one CTA per SM     */
+  int epi_warps; /* epilogue warps 4 or 8; 0 = automatic                               */
+  int flags;     /* DG_FLAG_* (tests only)                                              */
+  unsigned long long timeout_ns; /* bounded-wait limit per wait; 0 = 2 s               */
+} dg_config;
+
+/* One GEMM (reference decode_gemm::Problem, kernels/decode_gemm.cuh:352-363). */
+typedef struct dg_problem {
+  int M, N, K;
+  const void* activation;          /* [M,K] e4m3, K contiguous, 16-byte aligned     */
+  const void* weight;              /* layout-dependent, 16-byte aligned              */
+  const float* weight_scales;      /* [ceil(N/128), K/128]                           */
+  const float* activation_scales;  /* [M, K/128]                                     */
+  void* output;                    /* [M,N] bf16, N contiguous                       */
+  float* splitk_ws;                /* >= plan.ws_floats floats when plan.max_slabs>1 */
+  int* splitk_sem;                 /* >= plan.sem_ints ints, zeroed once; the kernel
+                                      re-zeroes each ticket it uses                  */
+  int* status;                     /* device int, 0 before the launch; may be NULL   */
+} dg_problem;
+
+/* Launch plan (reference decode_gemm::LaunchPlan, kernels/decode_gemm.cuh:373-380). */
+typedef struct dg_plan_info {
+  unsigned grid_x, grid_y, grid_z;
+  unsigned block_x;
+  unsigned smem_bytes;
+  int num_output_tiles;
+  int padded_n;
+  int stages;
+  int n_mma;
+  int mma_m;
+  int epi_warps;
+  int num_ctas;
+  int max_slabs;                   /* workspace slabs a split tile needs (1 = none) */
+  unsigned long long ws_floats;    /* required splitk_ws size in floats             */
+  int sem_ints;                    /* required splitk_sem size in ints              */
+  char error[96];                  /* empty when usable                             */
+} dg_plan_info;
+
+int dg_abi_version(void);
+
+/* Validates (cfg, M, N, K) and fills *out.  Returns 0, or 1 with out->error set. */
+int dg_plan(const dg_config* cfg, int M, int N, int K, dg_plan_info* out);
+
+/* Encodes the tensor maps the kernel reads (opaque 128-byte CUtensorMap
+   blobs).  The weight map is all zero for DG_LAYOUT_PACKED_SWIZZLED. */
+int dg_make_weight_map(const dg_config* cfg, const void* weight, int N, int K, void* map128);
+int dg_make_activation_map(const dg_config* cfg, const void* activation, int M, int K, void* map128);
+
+/* Launches with pre-built maps; pdl_attr selects programmatic stream
+   serialization for this launch independently of cfg->pdl. */
+int dg_launch_with_maps(const dg_config* cfg, const dg_problem* p, const void* weight_map128,
+                        const void* activation_map128, void* stream, int pdl_attr);
+
+/* Encodes both maps, then launches (attribute follows cfg->pdl). */
+int dg_launch(const dg_config* cfg, const dg_problem* p, void* stream);
+
+/* raw [n,k] -> layout (DG_LAYOUT_PACKED or DG_LAYOUT_PACKED_SWIZZLED); dst has
+   dg_packed_weight_bytes(n, k, block_n) bytes.  k must be a multiple of 128. */
+int dg_prepack_weight(const void* src, void* dst, int n, int k, int block_n, int layout, void* stream);
+int dg_padded_n(int n, int block_n);
+unsigned long long dg_packed_weight_bytes(int n, int k, int block_n);
+
+const char* dg_status_string(int code);
+
+/* Writes `bytes` of `buf` (device) to evict L2 between timed launches. */
+int dg_flush_l2(void* buf, unsigned long long bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DECODE_GEMM_B200_H_ */
