@@ -1,0 +1,554 @@
+#!/usr/bin/env python
+"""Cold-weight FP8 decode GEMM benchmark (the BASELINE metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--m M]
+
+Workload: Y[M x N] = X[M x K] . W[N x K]^T with N = 7168,
+K = 16384, M = 1 by default; W and X are FP8 E4M3 from seeded N(0,1) draws,
+each quantised with one per-tensor fp32 scale (amax -> 448); BF16 output,
+fp32 accumulation.  Weights rotate over >= max(1 GiB, 4 x L2) of distinct
+device copies, so every launch reads its weights cold from HBM (the inputs
+are larger than L2; no flush needed).  A step is one GEMM; K steps are timed
+with CUDA events on the launching stream, replayed from a CUDA graph, and
+with programmatic dependent launch between consecutive GEMMs.
+
+Multi-GPU (launched with torch.distributed.run, one rank per GPU): W is
+N-sharded tensor-parallel, each GPU streams N/g rows, and the BF16 output
+slices are all-gathered with NCCL every step (strong scaling: the whole job
+is one GEMM of the configured size; "gemm_only" reports it without the
+gather).  Timing is the max over ranks.
+
+Metric: algorithmic bytes (N*K + M*K + 2*M*N) per GEMM / time, GB/s, and
+us per GEMM.  `e2e` repeats the measurement through the public API with the
+step's activation and scales copied in from pinned host memory and the
+output copied back, inside the timed region.
+
+`--impl reference` times the reference's own CPU implementation of the path
+(the host scalar GEMM of kernels/smoke_test.cu, compiled from the reference
+source into oracle/_ref; the oracle restatement when that build is absent)
+on all host cores, on bounded samples of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "cold-weight HBM GB/s & % of peak per B200 at M=1..128; µs per GEMM"
+SPEC_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--n", type=int, default=7168)
+    ap.add_argument("--k", type=int, default=16384)
+    ap.add_argument("--layout", choices=["raw", "packed", "swizzled"], default="swizzled")
+    ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU work the rank-0 cpu_baseline sample is sized to")
+    ap.add_argument("--graph-chunk", type=int, default=500, help="launches per captured CUDA graph")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(workload_key):
+    """DRAM bytes per launch from the committed ncu summary (profiles/)."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(workload_key)
+    except (OSError, ValueError):
+        return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons with NVML every ~20 ms."""
+
+    REASONS = {  # nvmlClocksEventReason* bits
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int):
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._marks = []
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - NVML missing: report no clocks
+            self._nvml = None
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((time.perf_counter(), mhz, reasons))
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(0.02)
+
+    def start(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def mark(self):
+        self._marks.append(time.perf_counter())
+
+    def stop(self):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=1.0)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        lo, hi = (self._marks[0], self._marks[-1]) if len(self._marks) >= 2 else (-1e30, 1e30)
+        inside = [s for s in self.samples if lo <= s[0] <= hi] or self.samples
+        mhz = statistics.median(s[1] for s in inside)
+        bits = 0
+        for s in inside:
+            bits |= s[2]
+        reasons = sorted(name for bit, name in self.REASONS.items() if bits & bit and name != "gpu_idle")
+        return {"sm_mhz": mhz, "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(inside)}
+
+
+def quantize_pertensor(x, fp8):
+    """Per-tensor scale s = amax/448, q = clamp(x/s) -> e4m3 (round to nearest even)."""
+    import torch
+    amax = x.abs().max().clamp_min(1e-4)
+    s = (amax / 448.0).float()
+    q = (x / s).clamp(-448.0, 448.0).to(fp8).view(torch.uint8)
+    return q, s
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's CPU path on all host cores
+# ---------------------------------------------------------------------------
+
+def cpu_gemm_fn():
+    """(callable, kind): the reference's own compute_reference when it was
+    built here (oracle/_ref), else the oracle restatement."""
+    import ctypes
+    import numpy as np
+    import oracle
+    ref = oracle.load_ref()
+    if ref is not None:
+        kind = "reference"
+
+        def run(a, as_, w, ws, n_rows):
+            m, k = a.shape
+            out = np.zeros((m, n_rows), np.float32)
+            ref.ref_compute_reference(m, n_rows, k, a.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)),
+                                      as_.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                      w.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)),
+                                      ws.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                      out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+            return out
+    else:
+        kind = "port"
+
+        def run(a, as_, w, ws, n_rows):
+            return oracle.compute_reference(a, as_, w, ws, n=n_rows)
+    return run, kind
+
+
+def cpu_parallel_gemm(run, a, as_, w, ws, threads):
+    """Rows of W split over threads in 128-row blocks (scale groups stay
+    whole); each block is an independent call of the single-threaded
+    reference GEMM, so the result equals the one-thread result."""
+    import numpy as np
+    n = w.shape[0]
+    blocks = max(1, (n + 127) // 128)
+    per = (blocks + threads - 1) // threads
+    parts = [None] * threads
+    kb = a.shape[1] // 128
+
+    def work(t):
+        b0, b1 = t * per, min(blocks, (t + 1) * per)
+        if b0 >= b1:
+            return
+        r0, r1 = b0 * 128, min(n, b1 * 128)
+        parts[t] = (r0, run(a, as_, np.ascontiguousarray(w[r0:r1]),
+                            np.ascontiguousarray(ws[b0:b1].reshape(-1, kb)), r1 - r0))
+
+    pool = [threading.Thread(target=work, args=(t,)) for t in range(threads)]
+    for th in pool:
+        th.start()
+    for th in pool:
+        th.join()
+    out = np.zeros((a.shape[0], n), np.float32)
+    for part in parts:
+        if part is not None:
+            out[:, part[0]:part[0] + part[1].shape[1]] = part[1]
+    return out
+
+
+def host_inputs(n, k, m, seed=20260913):
+    """Per-tensor-scaled N(0,1) e4m3 inputs on the host (torch CPU generator)."""
+    import numpy as np
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn((n, k), generator=g)
+    qw, sw = quantize_pertensor(w, torch.float8_e4m3fn)
+    del w
+    x = torch.randn((m, k), generator=g)
+    qx, sx = quantize_pertensor(x, torch.float8_e4m3fn)
+    kb = k // 128
+    ws = np.full(((n + 127) // 128, kb), float(sw), np.float32)
+    as_ = np.full((m, kb), float(sx), np.float32)
+    return qw.numpy(), ws, qx.numpy(), as_
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    import numpy as np
+    run, kind = cpu_gemm_fn()
+    threads = os.cpu_count() or 1
+    n, k, m = args.n, args.k, args.m
+    w, ws, a, as_ = host_inputs(n, k, m)
+    # Size each step's sample so the timed K steps take about a minute.
+    rows_probe = min(n, 1024)
+    t0 = time.perf_counter()
+    cpu_parallel_gemm(run, a, as_, w[:rows_probe], ws[: (rows_probe + 127) // 128], threads)
+    per_row = (time.perf_counter() - t0) / rows_probe
+    budget = 60.0 / max(args.steps + args.warmup, 1)
+    rows = int(max(128, min(n, budget / max(per_row, 1e-12))) // 128 * 128)
+    w_s, ws_s = w[:rows], ws[: rows // 128]
+    for _ in range(args.warmup):
+        cpu_parallel_gemm(run, a, as_, w_s, ws_s, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_parallel_gemm(run, a, as_, w_s, ws_s, threads)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    byt = rows * k + m * k + 2 * m * rows
+    gbs = byt / dt / 1e9
+    sample = (f"{rows} of {n} weight rows per step (x {k} K, M={m}), {threads} threads, "
+              f"reference compute_reference per 128-row block")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp8e4m3-in/f32-acc/bf16-out", "data": "synthetic",
+        "config": {"workload": f"C2 decode GEMM N={n} K={k} M={m} (CPU sample)", "M": m, "N": n, "K": k},
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+
+def b200_arm(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import decode_opt_b200 as dg
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    n, k, m = args.n, args.k, args.m
+    if n % (world * 128) != 0:
+        raise SystemExit(f"N={n} must split into {world} shards of a multiple of 128 rows")
+    n_loc = n // world
+    layout = {"raw": dg.LAYOUT_RAW, "packed": dg.LAYOUT_PACKED, "swizzled": dg.LAYOUT_PACKED_SWIZZLED}[args.layout]
+    cfg = dg.default_config(m, n_loc, k, layout=layout, pdl=not args.no_pdl)
+    plan = cfg.plan(m, n_loc, k)
+    if plan.error:
+        raise SystemExit(plan.error)
+
+    # ---- synthetic inputs (same on every rank; each keeps its W shard) -----
+    g = torch.Generator(device=dev).manual_seed(20260913)
+    w_full = torch.randn((n, k), device=dev, generator=g)
+    qw_full, sw = quantize_pertensor(w_full, torch.float8_e4m3fn)
+    del w_full
+    x = torch.randn((m, k), device=dev, generator=g)
+    qx, sx = quantize_pertensor(x, torch.float8_e4m3fn)
+    qw = qw_full[rank * n_loc:(rank + 1) * n_loc].contiguous()
+    del qw_full
+    kb = k // 128
+    wscale = torch.full(((n_loc + 127) // 128, kb), float(sw), device=dev)
+    ascale = torch.full((m, kb), float(sx), device=dev)
+    base = qw if layout == dg.LAYOUT_RAW else dg.prepack_weight(qw, cfg.block_n, layout)
+    set_bytes = base.numel()
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    nsets = max(5, math.ceil(max(1 << 30, 4 * l2) / set_bytes))
+    sets = [base] + [base.clone() for _ in range(nsets - 1)]
+    out = torch.empty((m, n_loc), dtype=torch.bfloat16, device=dev)
+    gathered = torch.empty((world * m, n_loc), dtype=torch.bfloat16, device=dev)
+    ws_buf = torch.zeros(max(plan.ws_floats, 1), dtype=torch.float32, device=dev)
+    sem = torch.zeros(max(plan.sem_ints, 1), dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    probs = [dg.Problem(m, n_loc, k, qx, s_, wscale, ascale, out, ws_buf, sem, status) for s_ in sets]
+    wmaps = [dg.make_weight_tma(cfg, p) for p in probs]
+    amap = dg.make_activation_tma(cfg, probs[0])
+    stream = torch.cuda.Stream(device=dev)
+    pg = dist.group.WORLD if world > 1 else None
+
+    def step(i, with_gather=True):
+        rc = dg.launch_with_maps(cfg, probs[i % nsets], wmaps[i % nsets], amap, stream, pdl_attr=cfg.pdl)
+        if rc != 0:
+            raise RuntimeError(f"launch failed: cudaError {rc}")
+        if world > 1 and with_gather:
+            dist.all_gather_into_tensor(gathered, out, group=pg)
+
+    def capture(count, with_gather):
+        graphs = []
+        left = count
+        with torch.cuda.stream(stream):
+            while left > 0:
+                c = min(left, args.graph_chunk)
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=stream):
+                    for i in range(c):
+                        step(i, with_gather)
+                graphs.append(gr)
+                left -= c
+        return graphs
+
+    def timed(graphs):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for gr in graphs:
+            gr.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        t = e0.elapsed_time(e1) / 1e3
+        if world > 1:
+            tt = torch.tensor([t], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+            dist.barrier()
+        return t
+
+    # ---- warm-up (eager, then the captured graphs once) ----------------------
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            step(i)
+    torch.cuda.synchronize(dev)
+    graphs = capture(args.steps, with_gather=True)
+    graphs_gemm = capture(args.steps, with_gather=False) if world > 1 else graphs
+    for gr in graphs[:1]:
+        gr.replay()
+    torch.cuda.synchronize(dev)
+    if int(status.item()) != 0:
+        raise RuntimeError(f"kernel status {dg.status_string(int(status.item()))}")
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.05)
+    clocks.mark()
+    t_total = timed(graphs)
+    clocks.mark()
+    t_gemm = timed(graphs_gemm) if world > 1 else t_total
+    clocks.stop()
+    if int(status.item()) != 0:
+        raise RuntimeError(f"kernel status {dg.status_string(int(status.item()))}")
+    del graphs, graphs_gemm
+    torch.cuda.synchronize(dev)
+
+    K = args.steps
+    byt_job = n * k + m * k + 2 * m * n                   # one GEMM, whole job
+    byt_gpu = n_loc * k + m * k + 2 * m * n_loc           # per GPU per launch
+    us_step = t_total / K * 1e6
+    us_gemm = t_gemm / K * 1e6
+    value = byt_job / (t_total / K) / 1e9
+    peak, peak_kind = measured_peaks()
+    achieved = byt_gpu / (t_gemm / K) / 1e9
+    workload_key = f"N{n_loc}_K{k}_M{m}_{args.layout}"
+    traffic = ncu_traffic(workload_key)
+
+    # ---- end to end through the public API with host buffers ---------------
+    e2e = None
+    if not args.no_e2e:
+        hx = torch.empty((m, k), dtype=torch.uint8).pin_memory()
+        hx.copy_(qx.cpu())
+        hs = torch.empty((m, kb), dtype=torch.float32).pin_memory()
+        hs.copy_(ascale.cpu())
+        hy = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+        e2e_steps = K
+        with torch.cuda.stream(stream):
+            def e2e_step(i):
+                qx.copy_(hx, non_blocking=True)
+                ascale.copy_(hs, non_blocking=True)
+                step(i)
+                if world > 1:
+                    hy.copy_(gathered.view(world, m, n_loc).permute(1, 0, 2).reshape(m, n), non_blocking=True)
+                else:
+                    hy.copy_(out, non_blocking=True)
+            for i in range(3):
+                e2e_step(i)
+            torch.cuda.synchronize(dev)
+            if world > 1:
+                dist.barrier()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(e2e_steps):
+                e2e_step(i)
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        te = e0.elapsed_time(e1) / 1e3
+        if world > 1:
+            tt = torch.tensor([te], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            te = float(tt.item())
+        e2e = {"value": byt_job / (te / e2e_steps) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": int(hx.numel() + hs.numel() * 4),
+               "d2h_bytes_per_step": int(hy.numel() * 2),
+               "us_per_step": te / e2e_steps * 1e6}
+
+    # ---- CPU baseline on rank 0 (N = 1 only), also the parity check -----------
+    cpu = None
+    parity = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+        run, kind = cpu_gemm_fn()
+        w_h = qw.cpu().numpy()
+        a_h = qx.cpu().numpy()
+        ws_h = wscale.cpu().numpy()
+        as_h = ascale.cpu().numpy()
+        # parity of the benchmarked launch: one launch on set 0 against the
+        # reference GEMM on the same bytes
+        out.zero_()
+        with torch.cuda.stream(stream):
+            step(0, with_gather=False)
+        torch.cuda.synchronize(dev)
+        got = out.float().cpu().numpy()
+        threads = 1
+        t0 = time.perf_counter()
+        want = None
+        rows_done = 0
+        reps = 0
+        while True:
+            want_i = cpu_parallel_gemm(run, a_h, as_h, w_h, ws_h, threads)
+            rows_done += n_loc
+            reps += 1
+            if want is None:
+                want = want_i
+            if time.perf_counter() - t0 >= args.cpu_seconds:
+                break
+        dt = (time.perf_counter() - t0) / reps
+        cpu_bytes = n_loc * k + m * k + 2 * m * n_loc
+        cpu = {"value": cpu_bytes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": kind,
+               "sample": f"{reps} full GEMM(s) N={n_loc} K={k} M={m}, single thread, "
+                         f"{dt * 1e3:.1f} ms per GEMM"}
+        ok, worst = oracle.elementwise_ok(got, want)
+        parity = {"rel_l2": oracle.rel_l2(got, want), "max_rel_err_floored": worst, "ok": bool(ok)}
+
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": args.warmup,
+        "ms_per_step": us_step / 1e3,
+        "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None,
+        "dtype": "fp8e4m3-in/f32-acc/bf16-out",
+        "data": "synthetic",
+        "config": {
+            "workload": f"C2 decode GEMM N={n} K={k} M={m}, cold weights"
+                        + (f", TP={world} N-shards + NCCL all-gather" if world > 1 else ""),
+            "M": m, "N": n, "K": k, "layout": args.layout, "block_n": cfg.block_n, "subs": cfg.subs,
+            "stages": plan.stages, "grid": list(plan.grid), "threads_per_cta": plan.block[0],
+            "pdl": cfg.pdl, "rotation_sets": nsets, "working_set_bytes": nsets * set_bytes,
+            "l2_bytes": l2, "cold": "inputs larger than L2 (rotated weight copies), no flush",
+            "timing": "CUDA events around CUDA-graph replays of K launches, max over ranks",
+        },
+        "us_per_gemm": us_step,
+        "gemm_only": {"us_per_gemm": us_gemm, "GBps_job": byt_job / (t_gemm / K) / 1e9},
+        "pct_of_spec_8TBs": achieved / SPEC_HBM_GBS,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                     if peak_kind == "measured" else "fallback 6.65 TB/s",
+                     "traffic": traffic, "algorithmic_bytes_per_launch": byt_gpu},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": K * (1 if world == 1 else 1),
+        "clocks": clocks.summary(),
+        "parity": parity,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            raise SystemExit("run N>1 under torch.distributed.run (one rank per GPU)")
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if args.impl == "b200" else "gloo"
+        if backend == "nccl":
+            import torch
+            torch.cuda.set_device(local_rank)
+        dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120))
+    try:
+        if args.impl == "reference":
+            reference_arm(args, rank, world)
+        else:
+            b200_arm(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -88,8 +88,8 @@ class B200Config:
     """Runtime configuration of the sm_100a kernel (``dg_config``)."""
 
     m_tile: int = 8
-    block_n: int = 128
-    subs: int = 2
+    block_n: int = 256
+    subs: int = 1
     stages: int = 0
     layout: int = LAYOUT_RAW
     pdl: bool = False
@@ -119,12 +119,12 @@ class B200Config:
 def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool = True) -> B200Config:
     """The B200 schedule used by :func:`fp8_decode_gemm` and the benchmark.
 
-    128-row weight tiles (one tcgen05 M=128 tile, aligned with the 128-row
-    weight-scale groups), two 128-K blocks per stage, as many stages as fit
-    in shared memory, and a stream-K grid of one CTA per SM so every SM
-    streams the same number of weight bytes whatever the tile count.
+    256-row weight tiles (the widest tcgen05 N: 8 KiB of weights per MMA
+    instruction), one 128-K block per stage, as many stages as fit in shared
+    memory, and a stream-K grid of one CTA per SM so every SM streams the
+    same number of weight bytes whatever the tile count.
     """
-    return B200Config(m_tile=m_tile_for(m), block_n=128, subs=2, stages=0, layout=layout, pdl=pdl,
+    return B200Config(m_tile=m_tile_for(m), block_n=256, subs=1, stages=0, layout=layout, pdl=pdl,
                       split_k=1, grid_ctas=-1)
 
 
@@ -135,8 +135,9 @@ class KernelConfig:
     Same parameters, in the same order, with the same defaults.  On sm_100a
     they map onto :class:`B200Config` as follows:
 
-    * ``M_TILE`` -> ``m_tile``; ``OUTPUT_ROWS_PER_CTA`` -> ``block_n`` (BM); BM <= 64
-      runs tcgen05 M=64 tiles, larger BM (a B200 extension, up to 128) M=128;
+    * ``M_TILE`` -> ``m_tile`` (the batch is the tcgen05 M side, padded to 64,
+      or 128 for M_TILE=128); ``OUTPUT_ROWS_PER_CTA`` -> ``block_n`` (BM), the
+      weight rows per tile on the tcgen05 N side (B200 extension: 128 or 256);
     * ``SUBS_PER_STAGE`` -> ``subs``; ``NUM_MATH_WG * STAGES_PER_WG`` -> ``stages``
       (the ring depth, reduced if it does not fit in 227 KiB);
     * ``PREPACK`` -> weight layout packed (True) or raw (False);
@@ -176,9 +177,9 @@ class KernelConfig:
         mt, bm, wg = self.M_TILE, self.OUTPUT_ROWS_PER_CTA, self.NUM_MATH_WG
         if mt not in (8, 16, 32, 64, 128):
             raise ValueError("M_TILE must be one of 8/16/32/64/128")
-        if not (0 < bm <= 64 and bm % 8 == 0) and bm != 128:
+        if not (0 < bm <= 64 and bm % 8 == 0) and bm not in (128, 256):
             raise ValueError("OUTPUT_ROWS_PER_CTA (BM) must be a multiple of 8 in (0, 64] "
-                             "(or 128, the B200 full-tile extension)")
+                             "(or 128 / 256, the B200 wide-tile extension)")
         if wg not in (1, 2, 4):
             raise ValueError("NUM_MATH_WG must be 1, 2 or 4")
         if self.TILES_PER_CTA <= 0 or wg % self.TILES_PER_CTA != 0:
@@ -363,6 +364,7 @@ class LaunchPlan:
     error: Optional[str] = None
     stages: int = 0
     n_mma: int = 0
+    a_rows: int = 0
     mma_m: int = 0
     epi_warps: int = 0
     num_ctas: int = 0
@@ -376,7 +378,7 @@ class LaunchPlan:
         return cls(grid=(info.grid_x, info.grid_y, info.grid_z), block=(info.block_x, 1, 1),
                    smem_bytes=info.smem_bytes, num_output_tiles=info.num_output_tiles,
                    padded_n=info.padded_n, error=err, stages=info.stages, n_mma=info.n_mma,
-                   mma_m=info.mma_m, epi_warps=info.epi_warps, num_ctas=info.num_ctas,
+                   a_rows=info.a_rows, mma_m=info.mma_m, epi_warps=info.epi_warps, num_ctas=info.num_ctas,
                    max_slabs=info.max_slabs, ws_floats=info.ws_floats, sem_ints=info.sem_ints)
 
 

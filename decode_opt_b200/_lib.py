@@ -13,7 +13,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libdecode_gemm_b200.so")
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 LAYOUT_RAW = 0
 LAYOUT_PACKED = 1
@@ -28,7 +28,8 @@ ERR_INJECTED_TIMEOUT = 0x51
 EXPORTED_SYMBOLS = (
     "dg_abi_version", "dg_plan", "dg_make_weight_map", "dg_make_activation_map",
     "dg_launch_with_maps", "dg_launch", "dg_prepack_weight", "dg_padded_n",
-    "dg_packed_weight_bytes", "dg_status_string", "dg_flush_l2",
+    "dg_packed_weight_bytes", "dg_status_string", "dg_flush_l2", "dg_probe_bulk_stream",
+    "dg_probe_naive_read", "dg_num_sms",
 )
 
 
@@ -75,6 +76,7 @@ class DgPlanInfo(ctypes.Structure):
         ("padded_n", ctypes.c_int),
         ("stages", ctypes.c_int),
         ("n_mma", ctypes.c_int),
+        ("a_rows", ctypes.c_int),
         ("mma_m", ctypes.c_int),
         ("epi_warps", ctypes.c_int),
         ("num_ctas", ctypes.c_int),
@@ -117,6 +119,11 @@ def lib():
     L.dg_status_string.argtypes = [ctypes.c_int]
     L.dg_status_string.restype = ctypes.c_char_p
     L.dg_flush_l2.argtypes = [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_void_p]
+    L.dg_probe_bulk_stream.argtypes = [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_uint, ctypes.c_int,
+                                       ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    L.dg_probe_naive_read.argtypes = [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_int, ctypes.c_void_p,
+                                      ctypes.c_void_p]
+    L.dg_num_sms.restype = ctypes.c_int
     if L.dg_abi_version() != ABI_VERSION:
         raise RuntimeError(f"{LIB_PATH}: ABI version {L.dg_abi_version()} != {ABI_VERSION}")
     _LIB = L

@@ -22,6 +22,7 @@ LIB_NAME = "libdecode_gemm_b200.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+SOURCES = ("dg_capi.cu", "dg_probe.cu")
 
 
 def nvcc() -> str:
@@ -48,7 +49,7 @@ def build(verbose: bool = False, ptxas_verbose: bool = False, force: bool = Fals
     cmd = [nvcc(), "-std=c++17", "-O3", "-lineinfo", *ARCH_FLAGS,
            "-Xcompiler", "-fPIC", "-shared", "-cudart", "static",
            "-I", CSRC, "-I", INCLUDE,
-           os.path.join(CSRC, "dg_capi.cu"), "-o", LIB_PATH + ".tmp"]
+           *[os.path.join(CSRC, f) for f in SOURCES], "-o", LIB_PATH + ".tmp"]
     if ptxas_verbose:
         cmd[1:1] = ["-Xptxas", "-v"]
     if verbose:

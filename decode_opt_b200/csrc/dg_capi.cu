@@ -45,33 +45,27 @@ int current_sm_count() {
   return sms;
 }
 
-// One kernel per (MMA M, M_TILE, epilogue warps); everything else is runtime.
+// One kernel per batch class (MMA M, epilogue warps per quarter); everything
+// else is runtime.
 struct KernelEntry {
   KernelFn fn;
   std::atomic<int> smem_high_water;
 };
 
-template <int MMA_M, int MT, int EPI>
+template <int MMA_M, int EPW>
 KernelEntry* entry() {
-  static KernelEntry e{dg::kernel_ptr<MMA_M, MT, EPI>(), {0}};
+  static KernelEntry e{dg::kernel_ptr<MMA_M, EPW>(), {0}};
   return &e;
 }
 
-template <int MMA_M, int EPI>
-KernelEntry* select_m_tile(int m_tile) {
-  switch (m_tile) {
-    case 8: return entry<MMA_M, 8, EPI>();
-    case 16: return entry<MMA_M, 16, EPI>();
-    case 32: return entry<MMA_M, 32, EPI>();
-    case 64: return entry<MMA_M, 64, EPI>();
-    case 128: return entry<MMA_M, 128, EPI>();
+KernelEntry* select_kernel(int mma_m, int epw) {
+  if (mma_m == 128) return epw == 4 ? entry<128, 4>() : nullptr;
+  switch (epw) {
+    case 1: return entry<64, 1>();
+    case 2: return entry<64, 2>();
+    case 4: return entry<64, 4>();
     default: return nullptr;
   }
-}
-
-KernelEntry* select_kernel(int mma_m, int m_tile, int epi) {
-  if (mma_m == 64) return epi == 8 ? select_m_tile<64, 8>(m_tile) : select_m_tile<64, 4>(m_tile);
-  return epi == 8 ? select_m_tile<128, 8>(m_tile) : select_m_tile<128, 4>(m_tile);
 }
 
 void fill_info(const Plan& plan, dg_plan_info* out) {
@@ -89,6 +83,7 @@ void fill_info(const Plan& plan, dg_plan_info* out) {
   out->padded_n = plan.padded_n;
   out->stages = plan.params.stages;
   out->n_mma = plan.params.n_mma;
+  out->a_rows = plan.params.a_rows;
   out->mma_m = plan.mma_m;
   out->epi_warps = plan.epi_warps;
   out->num_ctas = plan.params.num_ctas;
@@ -113,7 +108,7 @@ int launch_impl(const dg_config* cfg, const dg_problem* prob, const CUtensorMap*
   p.weight = static_cast<const uint8_t*>(prob->weight);
   const cudaError_t buf_err = dg::check_buffers(plan, p);
   if (buf_err != cudaSuccess) return buf_err;
-  KernelEntry* k = select_kernel(plan.mma_m, c.m_tile, plan.epi_warps);
+  KernelEntry* k = select_kernel(plan.mma_m, plan.epw);
   if (k == nullptr) return cudaErrorInvalidValue;
   const cudaError_t attr_err =
       dg::ensure_smem(reinterpret_cast<const void*>(k->fn), plan.smem_bytes, &k->smem_high_water);
@@ -204,7 +199,7 @@ int dg_launch(const dg_config* cfg, const dg_problem* p, void* stream) {
 
 int dg_prepack_weight(const void* src, void* dst, int n, int k, int block_n, int layout, void* stream) {
   if (src == nullptr || dst == nullptr || n < 1 || k < 128 || k % 128 != 0 || block_n < 8 ||
-      block_n > 128 || block_n % 8 != 0)
+      block_n > 256 || block_n % 8 != 0)
     return cudaErrorInvalidValue;
   if (layout != DG_LAYOUT_PACKED && layout != DG_LAYOUT_PACKED_SWIZZLED) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(src) & 15u) != 0 || (reinterpret_cast<uintptr_t>(dst) & 15u) != 0)

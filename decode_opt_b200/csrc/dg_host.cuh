@@ -34,16 +34,16 @@ namespace dg {
 // onto it (include/decode_gemm.cuh); grid_ctas selects the B200 stream-K
 // schedule.
 struct Config {
-  int m_tile = 8;         // compile-time bound on M: 8, 16, 32, 64, 128
-  int block_n = 128;      // BM: output rows per tile; multiple of 8, <= 128
-  int subs = 2;           // 128-K blocks per pipeline stage: 1, 2 or 4
+  int m_tile = 8;         // bound on M: 8, 16, 32, 64 (MMA M = 64) or 128 (MMA M = 128)
+  int block_n = 256;      // BN: weight rows per tile; multiple of 8, <= 256
+  int subs = 1;           // 128-K blocks per pipeline stage: 1, 2 or 4
   int stages = 0;         // smem ring depth; 0 = as many as fit
   int layout = kLayoutRaw;
   int pdl = 0;            // 1: trigger dependents + programmatic serialization
   int split_k = 1;        // reference S (grid_ctas == 0 only): 1, 2, 4, 8, ...
   int grid_ctas = 0;      // 0: grid = tiles x split_k; > 0: stream-K over this
                           // many CTAs; < 0: stream-K over one CTA per SM
-  int epi_warps = 0;      // 4 or 8; 0 = 4 for m_tile <= 32, else 8
+  int epi_warps = 0;      // informational; the tile width fixes the epilogue warps
   unsigned long long timeout_ns = 0;  // bounded-wait limit; 0 = 2 s
   int flags = 0;          // extra kernel flags (kFlagInjectTimeout: tests only)
 };
@@ -54,6 +54,7 @@ struct Plan {
   dim3 block{0, 0, 0};
   uint32_t smem_bytes = 0;
   int mma_m = 0;
+  int epw = 0;              // epilogue warps per TMEM lane quarter (1, 2 or 4)
   int epi_warps = 0;
   int max_slabs = 1;        // workspace slabs needed (1 = no split tile)
   size_t ws_floats = 0;     // max_slabs * M * N when max_slabs > 1
@@ -62,17 +63,16 @@ struct Plan {
   const char* error = nullptr;
 };
 
-inline int effective_epi_warps(const Config& c) {
-  if (c.epi_warps == 4 || c.epi_warps == 8) return c.epi_warps;
-  return c.m_tile <= 32 ? 4 : 8;
-}
+// Kernel instantiation for a batch of M rows: the MMA M (64, or 128 past 64
+// rows) and the epilogue warps per lane quarter, which fixes how many copies
+// of the batch the activation tile holds (4 / epw).
+inline int mma_m_for(int M) { return M <= 64 ? 64 : 128; }
 
-inline int mma_m_for(int block_n) { return block_n <= 64 ? 64 : 128; }
+inline int epw_for(int M) { return M <= 16 ? 1 : M <= 32 ? 2 : 4; }
 
-inline int n_mma_for(int m) {
-  const int r = ((m + 15) / 16) * 16;
-  return r < 16 ? 16 : r;
-}
+inline int epi_warps_for(int epw) { return 4 * epw; }
+
+constexpr int kAccumBuffers = 2;
 
 inline int padded_n(int n, int block_n) { return ((n + block_n - 1) / block_n) * block_n; }
 
@@ -80,22 +80,19 @@ inline size_t packed_weight_bytes(int n, int k, int block_n) {
   return static_cast<size_t>(padded_n(n, block_n)) * static_cast<size_t>(k);
 }
 
-inline int accum_buffers(int m_tile) {
-  const int cols = m_tile < 16 ? 16 : m_tile;
-  return std::min(512 / cols, kMaxAccumBuffers);
-}
+inline uint32_t align1k(uint32_t v) { return (v + 1023u) & ~1023u; }
 
 // Static configuration checks (no shape).
 inline const char* check_config(const Config& c) {
   if (!(c.m_tile == 8 || c.m_tile == 16 || c.m_tile == 32 || c.m_tile == 64 || c.m_tile == 128))
     return "m_tile must be 8, 16, 32, 64 or 128";
-  if (c.block_n < 8 || c.block_n > 128 || c.block_n % 8 != 0)
-    return "block_n (BM) must be a multiple of 8 in [8, 128]";
+  if (c.block_n < 8 || c.block_n > 256 || c.block_n % 8 != 0)
+    return "block_n (BN) must be a multiple of 8 in [8, 256]";
   if (!(c.subs == 1 || c.subs == 2 || c.subs == 4)) return "subs must be 1, 2 or 4";
   if (c.stages < 0 || c.stages > kMaxStages) return "stages must be in [0, 16]";
   if (c.layout < kLayoutRaw || c.layout > kLayoutPackedSwizzled) return "unknown weight layout";
   if (c.split_k < 1) return "split_k must be >= 1";
-  if (!(c.epi_warps == 0 || c.epi_warps == 4 || c.epi_warps == 8)) return "epi_warps must be 0, 4 or 8";
+  if (c.epi_warps != 0) return "epi_warps is chosen by the planner; leave it 0";
   return nullptr;
 }
 
@@ -114,16 +111,23 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms) {
   const long long U = static_cast<long long>(T) * C;
   if (U > (1ll << 40)) return plan.error = "problem too large", plan;
 
-  const int mma_m = mma_m_for(c.block_n);
-  const int n_mma = n_mma_for(M);
-  const int epi = effective_epi_warps(c);
-  const int bufs = accum_buffers(c.m_tile);
+  const int mma_m = mma_m_for(M);
+  const int epw = epw_for(M);
+  const int copies = 4 / epw;
+  const int n_mma = ((c.block_n + 15) / 16) * 16;
+  const int a_rows = ((M + 7) / 8) * 8;
+  if (a_rows > mma_m / copies) return plan.error = "batch does not fit its activation copy", plan;
+  const int bufs = kAccumBuffers;
   const uint32_t w_stage = static_cast<uint32_t>(c.subs * c.block_n * kKBlock);
-  const uint32_t a_stage = static_cast<uint32_t>(c.subs * n_mma * kKBlock);
-  const uint32_t pad = c.block_n < mma_m ? static_cast<uint32_t>((mma_m - c.block_n) * kKBlock) : 0u;
+  const uint32_t a_stage = static_cast<uint32_t>(c.subs * mma_m * kKBlock);
+  const uint32_t a_tx = static_cast<uint32_t>(c.subs * copies * a_rows * kKBlock);
+  // The MMA reads n_mma weight rows from each 128-K block; rows past those
+  // loaded come from the next block or this tail pad and only feed output
+  // columns that are never stored.
+  const uint32_t w_pad = static_cast<uint32_t>((n_mma - c.block_n) * kKBlock);
   auto smem_for = [&](int stages) -> uint32_t {
-    const uint32_t w_region = ((stages * w_stage + pad) + 1023u) & ~1023u;
-    return 1024u + w_region + stages * a_stage + SmemBarriers::bytes(stages, bufs);
+    return 1024u + align1k(stages * w_stage + w_pad) + align1k(stages * a_stage) +
+           SmemBarriers::bytes(stages, bufs);
   };
   int stages = c.stages;
   if (stages == 0) {
@@ -157,28 +161,30 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms) {
   p.N = N;
   p.K = K;
   p.block_n = c.block_n;
+  p.n_mma = n_mma;
+  p.a_rows = a_rows;
   p.subs = c.subs;
   p.stages = stages;
   p.layout = c.layout;
-  p.n_mma = n_mma;
   p.num_tiles = T;
   p.chunks_per_tile = C;
   p.num_kb = num_kb;
-  p.num_scale_rows = (N + kKBlock - 1) / kKBlock;
   p.num_ctas = static_cast<int>(G);
   p.flags = (c.pdl ? kFlagPdlTrigger : 0) | (c.flags & ~kFlagPdlTrigger);
   p.total_units = U;
   p.w_stage_bytes = w_stage;
   p.a_stage_bytes = a_stage;
-  p.w_region_bytes = ((stages * w_stage + pad) + 1023u) & ~1023u;
-  p.a_region_bytes = stages * a_stage;
+  p.a_tx_bytes = a_tx;
+  p.w_region_bytes = align1k(stages * w_stage + w_pad);
+  p.a_region_bytes = align1k(stages * a_stage);
   p.smem_bytes = smem_for(stages);
   p.timeout_ns = c.timeout_ns ? c.timeout_ns : kDefaultTimeoutNs;
 
-  plan.block = dim3(static_cast<unsigned>((2 + epi) * 32), 1u, 1u);
+  plan.epi_warps = epi_warps_for(epw);
+  plan.block = dim3(static_cast<unsigned>((plan.epi_warps + 2) * 32), 1u, 1u);
   plan.smem_bytes = p.smem_bytes;
   plan.mma_m = mma_m;
-  plan.epi_warps = epi;
+  plan.epw = epw;
   plan.max_slabs = max_slabs;
   plan.ws_floats = max_slabs > 1 ? static_cast<size_t>(max_slabs) * M * static_cast<size_t>(N) : 0;
   plan.sem_ints = max_slabs > 1 ? T : 0;
@@ -248,15 +254,16 @@ inline cudaError_t make_weight_map(CUtensorMap* map, const Config& c, const void
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-// Activation map: dims {128, M, K/128}, strides {K, 128}, box {128, n_mma,
-// subs}.  Rows M..n_mma-1 of the box are out of range and land as zeros.
+// Activation map: dims {128, M, K/128}, strides {K, 128}, box {128, a_rows, 1}
+// with a_rows = M rounded up to 8 (rows M..a_rows-1 land as zeros); the
+// producer issues one box per 128-K block and batch copy.
 inline cudaError_t make_activation_map(CUtensorMap* map, const Config& c, const void* act, int M, int K) {
   std::memset(map, 0, sizeof(*map));
   EncodeTiledFn encode = encode_tiled_fn();
   if (encode == nullptr) return cudaErrorInsufficientDriver;
   const cuuint64_t dims[3] = {kKBlock, static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(K / kKBlock)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(K), kKBlock};
-  const cuuint32_t box[3] = {kKBlock, static_cast<cuuint32_t>(n_mma_for(M)), static_cast<cuuint32_t>(c.subs)};
+  const cuuint32_t box[3] = {kKBlock, static_cast<cuuint32_t>(((M + 7) / 8) * 8), 1u};
   const cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(act), dims, strides, box,
                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -267,9 +274,9 @@ inline cudaError_t make_activation_map(CUtensorMap* map, const Config& c, const 
 // ---------------------------------------------------------------- launch ---
 using KernelFn = void (*)(KernelParams, CUtensorMap, CUtensorMap);
 
-template <int MMA_M, int M_TILE, int EPI>
+template <int MMA_M, int EPW>
 inline KernelFn kernel_ptr() {
-  return reinterpret_cast<KernelFn>(&dg_decode_gemm_kernel<MMA_M, M_TILE, EPI>);
+  return reinterpret_cast<KernelFn>(&dg_decode_gemm_kernel<MMA_M, EPW>);
 }
 
 // Raises the dynamic-smem limit of `fn` once per (kernel, size).  Unlike the

@@ -8,26 +8,32 @@
 //   where raw_kb is the exact fp8 dot product over one 128-wide K block.
 //
 // This is the hot path the reference implements as fp8_decode_gemm<Cfg>
-// (kernels/decode_gemm.cuh:574-1081).  It is a new design for Blackwell:
+// (kernels/decode_gemm.cuh:574-1081).  It is a new design for Blackwell.
 //
-// Swap-AB on tcgen05.  A weight tile of BM output rows is the MMA's M side
-// (M=128 when BM>64, else M=64) and the batch (M=1..128 decode rows) is the
-// narrow N side, rounded up to 16.  One `tcgen05.mma.kind::f8f6f4` covers
-// K=32, four cover one 128-wide scale block.  Each scale block accumulates into
-// its own TMEM buffer (fresh: the first of the four MMAs does not accumulate),
-// so the per-block dequantisation stays exact:
-//     partial[m] = fmaf(w_s * a_s[m], raw_kb[m], partial[m])     (fp32)
-// which is the reference's numerical path (kernels/decode_gemm.cuh:897-946).
+// Operand placement.  A tcgen05.mma takes the same ~180 cycles whatever its
+// M and N (measured on B200 for kind::f8f6f4, M in {64,128}, N in 16..256), so
+// the weights -- the only large operand -- go on the MMA's N side with up to
+// N = 256 rows per instruction: 8 KiB of weights per MMA, twice what an
+// M=128 weight tile could carry.  The decode batch (M = 1..128 rows) is the
+// MMA's M side, padded to 64 or 128; rows past M are never read back.  One
+// MMA covers K = 32; four cover one 128-wide scale block, which accumulates
+// into its own TMEM buffer (the first of the four does not accumulate), so
+// the per-block dequantisation stays exact:
+//     partial[m][n] = fmaf(w_s * a_s[m], raw_kb[m][n], partial[m][n])   (fp32)
+// the reference's numerical path (kernels/decode_gemm.cuh:897-946).
 //
-// Warp roles (one CTA per SM, 2 + EPI_WARPS warps):
-//   warp 0       TMA producer: weight + activation tiles for one pipeline
-//                stage per (tile, chunk) unit into a ring of `stages` slots;
-//   warp 1       MMA issuer and TMEM owner: one elected lane issues the
-//                tcgen05.mma chain, tcgen05.commit frees smem slots and
-//                publishes finished accumulators;
-//   warps 2..    epilogue: TMEM -> registers (tcgen05.ld), scale fold into
-//                fp32 partials held in registers, then bf16 store or the
-//                split reduction.  Warp w reads TMEM lane quarter (w % 4).
+// Warp roles (one CTA per SM):
+//   warps 0 .. 4E-1   epilogue.  Warp w reads TMEM lane quarter w % 4, i.e.
+//                     the batch rows of that quarter, and column group w / 4
+//                     (up to 128 weight rows) of the tile: tcgen05.ld, scale fold into fp32
+//                     partials held in registers, then bf16 store or the split
+//                     reduction.  Warps whose rows are all >= M, or whose
+//                     columns are past the tile, stay idle.
+//   warp 4E           TMA producer: weight and activation tiles of one
+//                     (tile, chunk) unit per pipeline stage, `stages` deep.
+//   warp 4E+1         MMA issuer and TMEM owner: one lane issues the MMAs;
+//                     tcgen05.commit frees smem stages and publishes finished
+//                     accumulators.
 //
 // Work decomposition (stream-K).  The (tile, chunk) units, chunk = `subs`
 // consecutive 128-K blocks, are numbered tile-major; CTA c of G processes the
@@ -66,12 +72,12 @@ namespace dg {
 constexpr int kKBlock = 128;                       // one scale group of K
 constexpr uint32_t kMaxDynamicSmem = 227u * 1024u; // per CTA on sm_100
 constexpr int kMaxStages = 16;
-constexpr int kMaxAccumBuffers = 16;
+constexpr int kMaxAccumBuffers = 8;
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // 2 s
 
 enum Layout : int {
   kLayoutRaw = 0,             // W[N,K], K contiguous
-  kLayoutPacked = 1,          // [tile][kb][BM rows][128 B] (reference prepack)
+  kLayoutPacked = 1,          // [tile][kb][BN rows][128 B] (reference prepack)
   kLayoutPackedSwizzled = 2,  // same order, bytes pre-swizzled for SWIZZLE_128B
 };
 
@@ -96,22 +102,23 @@ enum Status : int {
 // by value as a __grid_constant__ parameter.
 struct KernelParams {
   int M, N, K;
-  int block_n;          // BM: output rows per tile
+  int block_n;          // BN: weight rows (output columns) per tile
+  int n_mma;            // MMA N: BN rounded up to 16
+  int a_rows;           // activation rows per TMA box: M rounded up to 8
   int subs;             // 128-K blocks per pipeline stage
   int stages;           // smem ring depth
   int layout;           // Layout
-  int n_mma;            // MMA N = activation rows per box (M rounded up to 16)
-  int num_tiles;        // ceil(N / BM)
+  int num_tiles;        // ceil(N / BN)
   int chunks_per_tile;  // (K/128) / subs
   int num_kb;           // K/128
-  int num_scale_rows;   // ceil(N/128)
   int num_ctas;         // G
   int flags;
   long long total_units;     // num_tiles * chunks_per_tile
-  uint32_t w_stage_bytes;    // subs * BM * 128
-  uint32_t a_stage_bytes;    // subs * n_mma * 128
-  uint32_t w_region_bytes;   // stages * w_stage_bytes + tail pad, 1 KiB aligned
-  uint32_t a_region_bytes;   // stages * a_stage_bytes
+  uint32_t w_stage_bytes;    // subs * BN * 128
+  uint32_t a_stage_bytes;    // subs * MMA_M * 128 (smem per stage)
+  uint32_t a_tx_bytes;       // subs * copies * a_rows * 128 (bytes TMA delivers)
+  uint32_t w_region_bytes;   // stages * w_stage_bytes + pad, 1 KiB aligned
+  uint32_t a_region_bytes;   // stages * a_stage_bytes + pad, 1 KiB aligned
   uint32_t smem_bytes;       // total dynamic smem incl. 1 KiB alignment slack
   unsigned long long timeout_ns;
   __nv_bfloat16* output;     // [M, N]
@@ -123,37 +130,72 @@ struct KernelParams {
   const uint8_t* weight;     // kLayoutPackedSwizzled: bulk-copy source
 };
 
-// Compile-time geometry of one kernel instantiation.
-template <int MMA_M_, int M_TILE_, int EPI_WARPS_>
+// Compile-time geometry of one kernel instantiation: the MMA M (batch rows,
+// padded) and the number of epilogue warps per TMEM lane quarter.
+//
+// Batch replication.  TMEM lane quarter q holds accumulator rows
+// [q*R4, (q+1)*R4), R4 = MMA_M/4.  A batch that fills fewer quarters than
+// there are is replicated: the activation tile is loaded kCopies = 4/EPW
+// times, into row blocks of MMA_M/kCopies rows, so every quarter holds the
+// whole batch (or half of it) and quarter q folds only the weight columns of
+// its copy.  The MMA costs the same (its M is padded anyway); the epilogue's
+// TMEM reads and FMAs are spread over all four quarters instead of landing on
+// the one quarter that holds the real rows.
+template <int MMA_M_, int EPW_>
 struct KernelTraits {
   static constexpr int kMmaM = MMA_M_;
-  static constexpr int kMTile = M_TILE_;
-  static constexpr int kEpiWarps = EPI_WARPS_;
+  static constexpr int kEpw = EPW_;                  // epilogue warps per lane quarter
   static_assert(kMmaM == 64 || kMmaM == 128, "tcgen05 cta_group::1 M is 64 or 128");
-  static_assert(kMTile == 8 || kMTile == 16 || kMTile == 32 || kMTile == 64 || kMTile == 128,
-                "M_TILE must be 8/16/32/64/128");
-  static_assert(kEpiWarps == 4 || kEpiWarps == 8, "4 or 8 epilogue warps");
-  static constexpr int kThreads = (2 + kEpiWarps) * 32;
+  static_assert(kEpw == 1 || kEpw == 2 || kEpw == 4, "1, 2 or 4 epilogue warps per quarter");
+  static constexpr int kBnMax = 256;                 // accumulator columns per buffer
+  static constexpr int kColsPerWarp = 64;            // weight columns one epilogue warp folds
+  static constexpr int kCopies = 4 / kEpw;           // batch copies along the MMA M side
+  static constexpr int kQuartersPerCopy = 4 / kCopies;
+  static constexpr int kColsPerCopy = kBnMax / kCopies;
+  static constexpr int kRowsPerQuarter = kMmaM / 4;  // accumulator rows per lane quarter
+  static constexpr int kRowsPerCopy = kMmaM / kCopies;
+  static constexpr int kEpiWarps = 4 * kEpw;
   static constexpr int kEpiThreads = kEpiWarps * 32;
-  // TMEM columns of one accumulator buffer (fp32: one column per batch row).
-  static constexpr int kColsPerBuf = kMTile < 16 ? 16 : kMTile;
-  static constexpr int kNumBufs =
-      (512 / kColsPerBuf) < kMaxAccumBuffers ? (512 / kColsPerBuf) : kMaxAccumBuffers;
-  static constexpr int kTmemColsRaw = kNumBufs * kColsPerBuf;
-  static constexpr uint32_t kTmemCols =
-      kTmemColsRaw <= 32 ? 32u : kTmemColsRaw <= 64 ? 64u : kTmemColsRaw <= 128 ? 128u
-      : kTmemColsRaw <= 256 ? 256u : 512u;
-  // Batch columns owned by one epilogue thread (8 warps split them in halves).
-  static constexpr int kColGroups = kEpiWarps / 4;
-  static constexpr int kPartial = kMTile / kColGroups;
-  static constexpr int kLoadWidth = kPartial < 16 ? kPartial : 16;
-  static constexpr int kLoads = kPartial / kLoadWidth;
-  static_assert(kPartial % kLoadWidth == 0, "column split");
-  // Rows of the MMA tile one epilogue warp owns in its TMEM lane quarter.
-  static constexpr int kRowsPerWarp = kMmaM / 4;
+  static constexpr int kProducerWarp = kEpiWarps;
+  static constexpr int kMmaWarp = kEpiWarps + 1;
+  static constexpr int kThreads = (kEpiWarps + 2) * 32;
+  static constexpr int kNumBufs = 2;                 // 2 x 256 columns = all of TMEM
+  static constexpr uint32_t kTmemCols = 512u;
+  static_assert(kColsPerCopy == kEpw * kColsPerWarp, "column split");
 };
 
-// Shared-memory carve-up that follows the 1 KiB-aligned operand regions.
+// Where epilogue warp w works: lane quarter, batch rows, weight columns.
+template <class Tr>
+struct EpiWarp {
+  int quarter;   // TMEM lane quarter (w % 4)
+  int row0;      // first batch row of this quarter within its copy
+  int col0;      // first tile column folded by this warp
+  bool active;   // holds a batch row < M and a column < block_n
+  __host__ __device__ __forceinline__ EpiWarp(int w, int M, int block_n) {
+    quarter = w & 3;
+    const int group = w >> 2;
+    const int copy = quarter / Tr::kQuartersPerCopy;
+    row0 = (quarter % Tr::kQuartersPerCopy) * Tr::kRowsPerQuarter;
+    col0 = copy * Tr::kColsPerCopy + group * Tr::kColsPerWarp;
+    active = (row0 < M) && (col0 < block_n);
+  }
+};
+
+template <class Tr>
+__host__ __device__ __forceinline__ int active_epilogue_warps(int M, int block_n) {
+  int n = 0;
+  for (int w = 0; w < Tr::kEpiWarps; ++w) n += EpiWarp<Tr>(w, M, block_n).active ? 1 : 0;
+  return n;
+}
+
+// Rank of warp w among the active epilogue warps.
+template <class Tr>
+__device__ __forceinline__ int active_epilogue_rank(int w, int M, int block_n) {
+  int n = 0;
+  for (int v = 0; v < w; ++v) n += EpiWarp<Tr>(v, M, block_n).active ? 1 : 0;
+  return n;
+}
+
 struct SmemBarriers {
   static __host__ __device__ constexpr uint32_t bytes(int stages, int bufs) {
     return static_cast<uint32_t>((2 * stages + 2 * bufs + 2) * 8 + 16);
@@ -177,6 +219,46 @@ __device__ __forceinline__ bool wait_for_completion(uint64_t* bar, uint32_t pari
   return true;
 }
 
+// Stores `ncols` fp32 partials of one output row as bf16 (16-byte stores when
+// the row start is 16-byte aligned and the run is full), else element-wise.
+template <int COLS>
+__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float (&v)[COLS], int ncols,
+                                               bool aligned) {
+  if (aligned && ncols == COLS) {
+#pragma unroll
+    for (int j = 0; j < COLS; j += 8) {
+      uint4 pk;
+      __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
+      __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
+      __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+      pk.x = *reinterpret_cast<uint32_t*>(&h0);
+      pk.y = *reinterpret_cast<uint32_t*>(&h1);
+      pk.z = *reinterpret_cast<uint32_t*>(&h2);
+      pk.w = *reinterpret_cast<uint32_t*>(&h3);
+      *reinterpret_cast<uint4*>(dst + j) = pk;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < COLS; ++j)
+      if (j < ncols) dst[j] = __float2bfloat16_rn(v[j]);
+  }
+}
+
+// Stores `ncols` fp32 partials of one row to the split workspace (L2 only).
+template <int COLS>
+__device__ __forceinline__ void store_row_f32(float* dst, const float (&v)[COLS], int ncols, bool aligned) {
+  if (aligned && ncols == COLS) {
+#pragma unroll
+    for (int j = 0; j < COLS; j += 4)
+      __stcg(reinterpret_cast<float4*>(dst + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+  } else {
+#pragma unroll
+    for (int j = 0; j < COLS; ++j)
+      if (j < ncols) __stcg(dst + j, v[j]);
+  }
+}
+
 template <class Tr>
 __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
                                                  const CUtensorMap* w_map,
@@ -198,6 +280,7 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   const int C = p.chunks_per_tile;
   const int stages = p.stages;
   const uint64_t timeout = p.timeout_ns;
+  const int active_warps = active_epilogue_warps<Tr>(p.M, p.block_n);
 
   // ------------------------------------------------------------ smem ------
   extern __shared__ uint8_t smem_raw[];
@@ -216,14 +299,14 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* ticket_flag = abort_flag + 1;
 
-  if (warp == 0 && lane == 0) {
+  if (warp == Tr::kProducerWarp && lane == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
     for (int b = 0; b < Tr::kNumBufs; ++b) {
       mbar_init(&accum_full[b], 1);
-      mbar_init(&accum_empty[b], Tr::kEpiWarps);
+      mbar_init(&accum_empty[b], static_cast<uint32_t>(active_warps));
     }
     mbar_init(drain_bar, 1);
     mbar_init(never_bar, 1);
@@ -231,7 +314,7 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
     *ticket_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == Tr::kMmaWarp) {
     tmem_alloc(tmem_slot, Tr::kTmemCols);
     tmem_relinquish();
   }
@@ -240,15 +323,15 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp == Tr::kProducerWarp) {
     // ======================================================== PRODUCER ====
     if (lane == 0) {
-      const bool swizzled_bulk = (p.layout == kLayoutPackedSwizzled);
-      if (!swizzled_bulk) prefetch_tensor_map(w_map);
+      const bool bulk = (p.layout == kLayoutPackedSwizzled);
+      if (!bulk) prefetch_tensor_map(w_map);
       prefetch_tensor_map(a_map);
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_a = policy_evict_last();
-      const uint32_t tx_bytes = p.w_stage_bytes + p.a_stage_bytes;
+      const uint32_t tx_bytes = p.w_stage_bytes + p.a_tx_bytes;
       auto issue_weight = [&](int i) {
         const long long u = u_begin + i;
         const int tile = static_cast<int>(u / C);
@@ -271,8 +354,13 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         const int tile = static_cast<int>(u / C);
         const int chunk = static_cast<int>(u - static_cast<long long>(tile) * C);
         const int slot = i % stages;
-        tma_load_3d(a_map, &full_bar[slot], a_region + static_cast<size_t>(slot) * p.a_stage_bytes,
-                    0, 0, chunk * p.subs, pol_a);
+        uint8_t* a_stage = a_region + static_cast<size_t>(slot) * p.a_stage_bytes;
+        for (int s = 0; s < p.subs; ++s)
+#pragma unroll
+          for (int c = 0; c < Tr::kCopies; ++c)
+            tma_load_3d(a_map, &full_bar[slot],
+                        a_stage + (s * Tr::kMmaM + c * Tr::kRowsPerCopy) * kKBlock, 0, 0,
+                        chunk * p.subs + s, pol_a);
       };
       // First ring pass: weights before the grid dependency resolves.
       const int first = n_units < stages ? n_units : stages;
@@ -295,10 +383,9 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         issued = i + 1;
       }
       if (p.flags & kFlagPdlTrigger) griddep_launch_dependents();
-      // Drain: nothing may still be landing in smem when the CTA exits.  In
-      // the normal path the MMA warp has consumed every stage, so these
-      // waits return at once; after an abort they bound the wait for the
-      // copies this thread started.
+      // Nothing may still be landing in smem when the CTA exits.  In the
+      // normal path every stage has been consumed and these waits return at
+      // once; after an abort they bound the wait for copies still in flight.
       if (*abort_flag != 0) {
         const int lo = issued > stages ? issued - stages : 0;
         for (int i = lo; i < issued; ++i) {
@@ -310,12 +397,12 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
+  } else if (warp == Tr::kMmaWarp) {
     // ============================================================= MMA ====
     if (lane == 0) {
       const uint32_t idesc = make_idesc_e4m3_f32(Tr::kMmaM, static_cast<uint32_t>(p.n_mma));
       const uint32_t w_sub_bytes = static_cast<uint32_t>(p.block_n) * kKBlock;
-      const uint32_t a_sub_bytes = static_cast<uint32_t>(p.n_mma) * kKBlock;
+      const uint32_t a_sub_bytes = static_cast<uint32_t>(Tr::kMmaM) * kKBlock;
       const uint32_t w_base = smem_addr(w_region);
       const uint32_t a_base = smem_addr(a_region);
       bool any_issued = false;
@@ -341,9 +428,10 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
             break;
           }
           tc_fence_after();
-          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * Tr::kColsPerBuf);
-          const uint32_t a_addr = w_base + slot * p.w_stage_bytes + s * w_sub_bytes;
-          const uint32_t b_addr = a_base + slot * p.a_stage_bytes + s * a_sub_bytes;
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * Tr::kBnMax);
+          // A = activation rows (MMA M side), B = weight rows (MMA N side).
+          const uint32_t a_addr = a_base + slot * p.a_stage_bytes + s * a_sub_bytes;
+          const uint32_t b_addr = w_base + slot * p.w_stage_bytes + s * w_sub_bytes;
 #pragma unroll
           for (int k = 0; k < kKBlock / 32; ++k) {
             mma_f8f6f4(d_tmem, make_desc_k_sw128(a_addr + 32u * k),
@@ -364,71 +452,79 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
     __syncwarp();
   } else {
     // ======================================================== EPILOGUE ====
-    const int e = static_cast<int>(warp) - 2;           // 0 .. kEpiWarps-1
-    const int quarter = static_cast<int>(warp & 3u);    // TMEM lane quarter
-    const int col0 = (e / 4) * Tr::kPartial;            // first batch column owned
-    const int row = quarter * Tr::kRowsPerWarp + static_cast<int>(lane);
-    const bool lane_has_row = (Tr::kMmaM == 128) || (lane < 16u);
-    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const int M = p.M;
     const int N = p.N;
     const int KB = p.num_kb;
-    const bool leader = (e == 0 && lane == 0);
+    const int bn = p.block_n;
+    const EpiWarp<Tr> ew(static_cast<int>(warp), M, bn);
+    const int quarter = ew.quarter;
+    const int col0 = ew.col0;                          // first tile column owned
+    if (ew.active) {
+      const int m = ew.row0 + static_cast<int>(lane);
+      const bool row_ok = (static_cast<int>(lane) < Tr::kRowsPerQuarter) && (m < M);
+      const int m_c = m < M ? m : M - 1;
+      const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+      const bool leader = (warp == 0 && lane == 0);
+      const uint32_t epi_threads = static_cast<uint32_t>(active_warps * 32);
+      // Index of this thread among the active epilogue threads.
+      const int active_tid = active_epilogue_rank<Tr>(static_cast<int>(warp), M, bn) * 32 + static_cast<int>(lane);
+      const float* a_s_row = p.a_scales + static_cast<size_t>(m_c) * KB;
 
-    griddep_wait();   // activation scales, output and workspace come after the producer grid
+      griddep_wait();   // activation scales, output and workspace follow the preceding grid
 
-    int acc = 0;
-    long long u = u_begin;
-    while (u < u_end) {
-      const int tile = static_cast<int>(u / C);
-      const long long tile_first = static_cast<long long>(tile) * C;
-      const long long seg_end = (tile_first + C) < u_end ? (tile_first + C) : u_end;
-      const int n = tile * p.block_n + row;
-      const bool row_ok = lane_has_row && row < p.block_n && n < N;
-      const int g = (n < N ? n : N - 1) / kKBlock;
-      const float* w_s_row = p.w_scales + static_cast<size_t>(g) * KB;
+      int acc = 0;
+      long long u = u_begin;
+      while (u < u_end) {
+        const int tile = static_cast<int>(u / C);
+        const long long tile_first = static_cast<long long>(tile) * C;
+        const long long seg_end = (tile_first + C) < u_end ? (tile_first + C) : u_end;
+        // Output columns n0 .. n0+63 of this warp; at most two 128-row weight
+        // scale groups, split at tile column `split`.
+        const int n0 = tile * bn + col0;
+        const int last_scale_row = (N - 1) / kKBlock;
+        const int g_lo = min(n0 / kKBlock, last_scale_row);
+        const int g_hi = min(g_lo + 1, last_scale_row);
+        const int split = (g_lo + 1) * kKBlock - n0;     // columns >= split use g_hi
+        const float* w_lo = p.w_scales + static_cast<size_t>(g_lo) * KB;
+        const float* w_hi = p.w_scales + static_cast<size_t>(g_hi) * KB;
 
-      float partial[Tr::kPartial];
+        float partial[Tr::kColsPerWarp];
 #pragma unroll
-      for (int j = 0; j < Tr::kPartial; ++j) partial[j] = 0.0f;
+        for (int j = 0; j < Tr::kColsPerWarp; ++j) partial[j] = 0.0f;
 
-      for (long long uu = u; uu < seg_end; ++uu) {
-        const int chunk = static_cast<int>(uu - tile_first);
-        for (int s = 0; s < p.subs; ++s, ++acc) {
-          const int kb = chunk * p.subs + s;
-          const int buf = acc % Tr::kNumBufs;
-          const float w_s = __ldg(w_s_row + kb);
-          int ready = 0;
-          if (lane == 0) {
-            ready = mbar_wait_bounded(&accum_full[buf], static_cast<uint32_t>((acc / Tr::kNumBufs) & 1),
-                                      abort_flag, p.status, kErrEpilogueAccumWait, timeout)
-                        ? 1
-                        : 0;
-          }
-          ready = __shfl_sync(0xffffffffu, ready, 0);
-          if (ready) {
+        for (long long uu = u; uu < seg_end; ++uu) {
+          const int chunk = static_cast<int>(uu - tile_first);
+          for (int s = 0; s < p.subs; ++s, ++acc) {
+            const int kb = chunk * p.subs + s;
+            const int buf = acc % Tr::kNumBufs;
+            // Scales are requested before the accumulator wait so their
+            // latency hides behind it.  The reference's fold:
+            // combined = w_s * a_s, then one fma per element.
+            const float a_s = __ldg(a_s_row + kb);
+            const float c_lo = __ldg(w_lo + kb) * a_s;
+            const float c_hi = __ldg(w_hi + kb) * a_s;
+            int ready = 0;
+            if (lane == 0) {
+              ready = mbar_wait_bounded(&accum_full[buf], static_cast<uint32_t>((acc / Tr::kNumBufs) & 1),
+                                        abort_flag, p.status, kErrEpilogueAccumWait, timeout)
+                          ? 1
+                          : 0;
+            }
+            ready = __shfl_sync(0xffffffffu, ready, 0);
+            if (!ready) continue;
             tc_fence_after();
 #pragma unroll
-            for (int ld = 0; ld < Tr::kLoads; ++ld) {
-              const int c_first = col0 + ld * Tr::kLoadWidth;
-              if (c_first < M) {   // warp-uniform
-                uint32_t raw[Tr::kLoadWidth];
-                const uint32_t taddr = tmem_base + lane_addr +
-                                       static_cast<uint32_t>(buf * Tr::kColsPerBuf + c_first);
-                if constexpr (Tr::kLoadWidth == 16) {
-                  tmem_ld_x16(taddr, reinterpret_cast<uint32_t(&)[16]>(raw));
-                } else {
-                  tmem_ld_x8(taddr, reinterpret_cast<uint32_t(&)[8]>(raw));
-                }
+            for (int ch = 0; ch < Tr::kColsPerWarp / 16; ++ch) {
+              const int c_first = col0 + ch * 16;
+              if (c_first < bn) {   // warp-uniform
+                uint32_t raw[16];
+                tmem_ld_x16(tmem_base + lane_addr + static_cast<uint32_t>(buf * Tr::kBnMax + c_first), raw);
                 tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < Tr::kLoadWidth; ++j) {
-                  const int m = c_first + j;
-                  if (m < M) {
-                    const float a_s = __ldg(p.a_scales + static_cast<size_t>(m) * KB + kb);
-                    partial[ld * Tr::kLoadWidth + j] =
-                        fmaf(w_s * a_s, __uint_as_float(raw[j]), partial[ld * Tr::kLoadWidth + j]);
-                  }
+                for (int j = 0; j < 16; ++j) {
+                  const int jj = ch * 16 + j;
+                  const float c = jj < split ? c_lo : c_hi;
+                  partial[jj] = fmaf(c, __uint_as_float(raw[j]), partial[jj]);
                 }
               }
             }
@@ -437,61 +533,63 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
             if (lane == 0) mbar_arrive(&accum_empty[buf]);
           }
         }
-      }
 
-      // ------------------------------------------------------- emit ------
-      const long long c_first = cta_of_unit(tile_first, G, U);
-      const long long c_last = cta_of_unit(tile_first + C - 1, G, U);
-      const int contributors = static_cast<int>(c_last - c_first + 1);
-      if (contributors == 1) {
-        if (row_ok && *abort_flag == 0) {
-#pragma unroll
-          for (int j = 0; j < Tr::kPartial; ++j) {
-            const int m = col0 + j;
-            if (m < M) p.output[static_cast<size_t>(m) * N + n] = __float2bfloat16_rn(partial[j]);
-          }
-        }
-      } else {
-        const int slab = static_cast<int>(cta - c_first);
-        const size_t slab_stride = static_cast<size_t>(M) * N;
-        if (row_ok) {
-          float* dst = p.ws + slab * slab_stride + n;
-#pragma unroll
-          for (int j = 0; j < Tr::kPartial; ++j) {
-            const int m = col0 + j;
-            if (m < M) __stcg(dst + static_cast<size_t>(m) * N, partial[j]);
-          }
-        }
-        __threadfence();
-        named_barrier_sync(1, Tr::kEpiThreads);
-        if (leader) {
-          int last = 0;
-          if (*abort_flag == 0) {
-            const int previous = atomicAdd(p.sem + tile, 1);
-            last = (previous == contributors - 1) ? 1 : 0;
-          }
-          *ticket_flag = last;
-        }
-        named_barrier_sync(1, Tr::kEpiThreads);
-        if (*ticket_flag != 0) {
+        // ----------------------------------------------------- emit ------
+        const long long c_first = cta_of_unit(tile_first, G, U);
+        const long long c_last = cta_of_unit(tile_first + C - 1, G, U);
+        const int contributors = static_cast<int>(c_last - c_first + 1);
+        const int ncols = min(Tr::kColsPerWarp, min(bn - col0, N - n0));   // valid columns here
+        if (contributors == 1) {
+          if (row_ok && *abort_flag == 0)
+            store_row_bf16<Tr::kColsPerWarp>(p.output + static_cast<size_t>(m) * N + n0, partial, ncols,
+                                             (N & 7) == 0);
+        } else {
+          const int slab = static_cast<int>(cta - c_first);
+          const size_t slab_stride = static_cast<size_t>(M) * N;
+          if (row_ok)
+            store_row_f32<Tr::kColsPerWarp>(p.ws + slab * slab_stride + static_cast<size_t>(m) * N + n0,
+                                            partial, ncols, (N & 3) == 0);
           __threadfence();
-          if (row_ok) {
-            const float* src = p.ws + n;
-#pragma unroll
-            for (int j = 0; j < Tr::kPartial; ++j) {
-              const int m = col0 + j;
-              if (m < M) {
-                const size_t off = static_cast<size_t>(m) * N;
-                float total = __ldcg(src + off);
-                for (int sl = 1; sl < contributors; ++sl) total += __ldcg(src + sl * slab_stride + off);
-                p.output[off + n] = __float2bfloat16_rn(total);
-              }
+          named_barrier_sync(1, epi_threads);
+          if (leader) {
+            int last = 0;
+            if (*abort_flag == 0) {
+              const int previous = atomicAdd(p.sem + tile, 1);
+              last = (previous == contributors - 1) ? 1 : 0;
             }
+            *ticket_flag = last;
           }
-          if (leader) atomicExch(p.sem + tile, 0);
+          named_barrier_sync(1, epi_threads);
+          if (*ticket_flag != 0) {
+            __threadfence();
+            // The tile's M x BN outputs are spread over all active epilogue
+            // threads (consecutive threads -> consecutive columns, so every
+            // access is coalesced); each sums its element over the slabs in
+            // slab order 0, 1, ..., contributors-1 whatever the arrival order,
+            // so the result is bit-identical run to run.
+            const int bn_t = min(bn, N - tile * bn);
+            const int total_el = M * bn_t;
+            const float* base = p.ws + static_cast<size_t>(tile) * bn;
+            __nv_bfloat16* obase = p.output + static_cast<size_t>(tile) * bn;
+            for (int e = active_tid; e < total_el; e += static_cast<int>(epi_threads)) {
+              const int mm = e / bn_t;
+              const size_t off = static_cast<size_t>(mm) * N + (e - mm * bn_t);
+              float total = 0.0f;
+              for (int s0 = 0; s0 < contributors; s0 += 8) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = (s0 + j) < contributors ? __ldcg(base + (s0 + j) * slab_stride + off) : 0.0f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                  if ((s0 + j) < contributors) total = (s0 + j) == 0 ? v[j] : total + v[j];
+              }
+              obase[off] = __float2bfloat16_rn(total);
+            }
+            if (leader) atomicExch(p.sem + tile, 0);
+          }
         }
+        u = seg_end;
       }
-      u = seg_end;
     }
   }
 
@@ -499,16 +597,16 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, Tr::kTmemCols);
+  if (warp == Tr::kMmaWarp) tmem_dealloc(tmem_base, Tr::kTmemCols);
 }
 
-template <int MMA_M, int M_TILE, int EPI_WARPS>
-__global__ void __launch_bounds__((2 + EPI_WARPS) * 32, 1)
+template <int MMA_M, int EPW>
+__global__ void __launch_bounds__(KernelTraits<MMA_M, EPW>::kThreads, 1)
     dg_decode_gemm_kernel(const __grid_constant__ KernelParams p,
                           const __grid_constant__ CUtensorMap w_map,
                           const __grid_constant__ CUtensorMap a_map) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
-  decode_gemm_body<KernelTraits<MMA_M, M_TILE, EPI_WARPS>>(p, &w_map, &a_map);
+  decode_gemm_body<KernelTraits<MMA_M, EPW>>(p, &w_map, &a_map);
 #else
   if (threadIdx.x == 0 && p.status != nullptr) atomicCAS(p.status, 0, kErrBadLaunchShape);
 #endif

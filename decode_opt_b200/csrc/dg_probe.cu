@@ -1,0 +1,158 @@
+// SPDX-License-Identifier: MIT
+//
+// dg_probe.cu -- achievable-HBM-read probe for sm_100a (the B200 rebuild of
+// the reference's tools/peak_bw_probe.cu:82-211): it measures the denominator
+// of "% of achievable bandwidth" for the decode GEMM.
+//
+//   dg_probe_bulk_stream  every CTA streams a contiguous slice of a cold
+//                         buffer through an smem ring with cp.async.bulk
+//                         (op_bytes per copy, `stages` in flight), the same
+//                         copy engine and mbarrier handshake as the GEMM's
+//                         producer, with no math behind it;
+//   dg_probe_naive_read   grid-stride 16-byte ld.global.nc loads with 4
+//                         independent loads in flight per thread (the
+//                         reference's naive_read_nc control);
+//
+// The L2 honesty check (reference tma_l2_selftest, :190-211) is
+// dg_probe_bulk_stream run repeatedly over a buffer small enough to stay in
+// L2: it must read far above HBM speed, which shows the cold-buffer numbers
+// are not L2 hits.
+//
+// Timing is the caller's (CUDA events around the launch).  Every wait is
+// bounded; a timeout is reported through *status.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "decode_gemm_b200.h"
+#include "sm100.cuh"
+
+namespace {
+
+using namespace dg::sm100;
+
+constexpr int kProbeThreads = 64;   // warp 0 issues, warp 1 consumes
+constexpr uint64_t kProbeTimeoutNs = 2000000000ull;
+
+__global__ void __launch_bounds__(kProbeThreads, 1)
+    bulk_stream_kernel(const uint8_t* __restrict__ src, unsigned long long bytes, uint32_t op_bytes,
+                       int stages, int* status, unsigned long long* sink) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127u) & ~uintptr_t(127));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(stages) * op_bytes);
+  uint64_t* empty = full + stages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + stages);
+  const unsigned long long ops_total = bytes / op_bytes;
+  const unsigned long long op_begin = ops_total * blockIdx.x / gridDim.x;
+  const unsigned long long op_end = ops_total * (blockIdx.x + 1) / gridDim.x;
+  const int n = static_cast<int>(op_end - op_begin);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const uint64_t pol = policy_evict_first();
+  int issued = 0;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < n; ++i) {
+      const int s = i % stages;
+      if (i >= stages && !mbar_wait_bounded(&empty[s], static_cast<uint32_t>(((i / stages) & 1) ^ 1), abort_flag,
+                                            status, 0x71, kProbeTimeoutNs))
+        break;
+      mbar_arrive_expect_tx(&full[s], op_bytes);
+      bulk_load(smem + static_cast<size_t>(s) * op_bytes, src + (op_begin + i) * op_bytes, op_bytes, &full[s], pol);
+      issued = i + 1;
+    }
+  } else if (threadIdx.x == 32) {
+    uint32_t acc = 0;
+    for (int i = 0; i < n; ++i) {
+      const int s = i % stages;
+      if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((i / stages) & 1), abort_flag, status, 0x72,
+                             kProbeTimeoutNs))
+        break;
+      acc ^= *reinterpret_cast<const volatile uint32_t*>(smem + static_cast<size_t>(s) * op_bytes);
+      mbar_arrive(&empty[s]);
+    }
+    if (acc == 0x9e3779b9u) atomicAdd(sink, 1ull);   // keeps the consumer's reads live
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag != 0) {
+    const int lo = issued > stages ? issued - stages : 0;
+    for (int i = lo; i < issued; ++i) {
+      const int s = i % stages;
+      const uint32_t parity = static_cast<uint32_t>((i / stages) & 1);
+      const uint64_t t0 = global_timer_ns();
+      while (!mbar_try_wait(&full[s], parity) && global_timer_ns() - t0 < kProbeTimeoutNs) {
+      }
+    }
+  }
+}
+
+__global__ void naive_read_kernel(const uint4* __restrict__ src, size_t n16, unsigned long long* sink) {
+  uint32_t acc = 0;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n16; i += 4 * stride) {
+    uint4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4* p = src + i + j * stride;
+      asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(v[j].x), "=r"(v[j].y), "=r"(v[j].z), "=r"(v[j].w)
+                   : "l"(p));
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc ^= v[j].x ^ v[j].y ^ v[j].z ^ v[j].w;
+  }
+  for (; i < n16; i += stride) {
+    const uint4 v = src[i];
+    acc ^= v.x ^ v.y ^ v.z ^ v.w;
+  }
+  if (acc == 0x9e3779b9u) atomicAdd(sink, 1ull);
+}
+
+int sm_count() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return sms;
+}
+
+}  // namespace
+
+extern "C" {
+
+// Streams `bytes` (a multiple of op_bytes; op_bytes a multiple of 16) of the
+// device buffer once.  `sink` is one device uint64 (may be NULL-free scratch).
+int dg_probe_bulk_stream(const void* buf, unsigned long long bytes, unsigned op_bytes, int ctas, int stages,
+                         int* status, unsigned long long* sink, void* stream) {
+  if (buf == nullptr || sink == nullptr || op_bytes < 16 || op_bytes % 16 != 0 || stages < 1 || ctas < 1 ||
+      bytes < op_bytes || (reinterpret_cast<uintptr_t>(buf) & 15u) != 0)
+    return cudaErrorInvalidValue;
+  const size_t smem = 128 + static_cast<size_t>(stages) * op_bytes + 16 * static_cast<size_t>(stages) + 16;
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(bulk_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  bulk_stream_kernel<<<ctas, kProbeThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(buf), bytes, op_bytes, stages, status, sink);
+  return cudaGetLastError();
+}
+
+int dg_probe_naive_read(const void* buf, unsigned long long bytes, int blocks_per_sm, unsigned long long* sink,
+                        void* stream) {
+  if (buf == nullptr || sink == nullptr || bytes < 16 || blocks_per_sm < 1) return cudaErrorInvalidValue;
+  naive_read_kernel<<<sm_count() * blocks_per_sm, 512, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(buf), static_cast<size_t>(bytes / 16), sink);
+  return cudaGetLastError();
+}
+
+int dg_num_sms(void) { return sm_count(); }
+
+}  // extern "C"

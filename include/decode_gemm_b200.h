@@ -30,6 +30,10 @@
  *   dg_packed_weight_bytes  prepack::packed_weight_bytes kernels/weight_prepack.cuh:50-52
  *   dg_status_string        (new) text of the kernel's device status codes
  *   dg_flush_l2             bench helper flush_l2_kernel bench/bench_decode.cu:473-476
+ *   dg_probe_bulk_stream    tools/peak_bw_probe.cu tma_stream_probe :82-134 (and the
+ *                           L2 self-test :190-211 when run on a small buffer)
+ *   dg_probe_naive_read     tools/peak_bw_probe.cu naive_read_nc :138-170
+ *   dg_num_sms              (new) SM count of the current device
  */
 #ifndef DECODE_GEMM_B200_H_
 #define DECODE_GEMM_B200_H_
@@ -40,7 +44,7 @@
 extern "C" {
 #endif
 
-#define DG_ABI_VERSION 1
+#define DG_ABI_VERSION 2
 
 /* Weight layouts. */
 #define DG_LAYOUT_RAW 0             /* W[N,K], K contiguous (checkpoint layout) */
@@ -66,9 +70,11 @@ extern "C" {
 
 /* Runtime configuration.  Zero-initialise, then set fields. */
 typedef struct dg_config {
-  int m_tile;    /* bound on M: 8, 16, 32, 64 or 128 (reference M_TILE)               */
-  int block_n;   /* BM, output rows per tile: multiple of 8 in [8,128]
-                    (reference OUTPUT_ROWS_PER_CTA; 128 = one tcgen05 M=128 tile)     */
+  int m_tile;    /* bound on M: 8, 16, 32, 64 or 128 (reference M_TILE); the batch is
+                    the MMA's M side, padded to 64 (m_tile <= 64) or 128              */
+  int block_n;   /* weight rows (output columns) per tile = the MMA's N side:
+                    multiple of 8 in [8,256] (reference OUTPUT_ROWS_PER_CTA, <= 64
+                    there; 256 = 8 KiB of weights per tcgen05.mma, the B200 default) */
   int subs;      /* 128-K blocks per pipeline stage: 1, 2, 4 (reference SUBS_PER_STAGE)*/
   int stages;    /* smem ring depth, 0 = as many as fit in 227 KiB                     */
   int layout;    /* DG_LAYOUT_*  (reference PREPACK: false = RAW, true = PACKED)       */
@@ -77,7 +83,7 @@ typedef struct dg_config {
   int split_k;   /* reference SPLITK_FACTOR S >= 1, used when grid_ctas == 0            */
   int grid_ctas; /* 0: grid = ceil(N/BM) x split_k (reference schedule);
                     >0: stream-K over this many CTAs; <0: stream-K, one CTA per SM     */
-  int epi_warps; /* epilogue warps 4 or 8; 0 = automatic                               */
+  int epi_warps; /* 0 (or the value block_n implies: 4 per 64 tile columns)            */
   int flags;     /* DG_FLAG_* (tests only)                                              */
   unsigned long long timeout_ns; /* bounded-wait limit per wait; 0 = 2 s               */
 } dg_config;
@@ -104,8 +110,9 @@ typedef struct dg_plan_info {
   int num_output_tiles;
   int padded_n;
   int stages;
-  int n_mma;
-  int mma_m;
+  int n_mma;                       /* MMA N = block_n rounded up to 16              */
+  int a_rows;                      /* activation rows per TMA box = M rounded up to 8 */
+  int mma_m;                       /* MMA M = batch rows padded to 64 or 128        */
   int epi_warps;
   int num_ctas;
   int max_slabs;                   /* workspace slabs a split tile needs (1 = none) */
@@ -142,6 +149,17 @@ const char* dg_status_string(int code);
 
 /* Writes `bytes` of `buf` (device) to evict L2 between timed launches. */
 int dg_flush_l2(void* buf, unsigned long long bytes, void* stream);
+
+/* Achievable-HBM probes.  Each reads `bytes` of `buf` once; the caller times
+   the launch.  sink: one device unsigned long long the kernels may touch.
+   bulk_stream: `ctas` CTAs, each streaming a contiguous slice through an smem
+   ring of `stages` x op_bytes with cp.async.bulk (op_bytes % 16 == 0).
+   naive_read: ld.global.nc grid-stride reads, blocks_per_sm x SMs x 512 threads. */
+int dg_probe_bulk_stream(const void* buf, unsigned long long bytes, unsigned op_bytes, int ctas,
+                         int stages, int* status, unsigned long long* sink, void* stream);
+int dg_probe_naive_read(const void* buf, unsigned long long bytes, int blocks_per_sm,
+                        unsigned long long* sink, void* stream);
+int dg_num_sms(void);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,173 @@
+"""CPU tests of the C ABI library and the host logic (no kernel launches)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+import decode_opt_b200 as dg
+from decode_opt_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = set()
+    for fname in os.listdir(os.path.join(ROOT, "include")):
+        if not fname.endswith(".h"):
+            continue
+        text = open(os.path.join(ROOT, "include", fname)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names |= set(re.findall(r"\b(dg_\w+)\s*\(", text))
+    return names
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    L = _lib.lib()
+    declared = declared_functions()
+    assert declared, "no declarations found"
+    assert declared == set(_lib.EXPORTED_SYMBOLS)
+    for name in declared:
+        assert hasattr(L, name), name
+    assert L.dg_abi_version() == _lib.ABI_VERSION
+
+
+def test_struct_layouts_match_header(tmp_path):
+    """The ctypes mirrors have the C header's sizes and field offsets (compiled
+    with the system C compiler against include/decode_gemm_b200.h)."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    structs = {"dg_config": _lib.DgConfig, "dg_problem": _lib.DgProblem, "dg_plan_info": _lib.DgPlanInfo}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "decode_gemm_b200.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'  printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = {}
+    for line in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        name, field, val = line.split()
+        got[(name, field)] = int(val)
+    for cname, py in structs.items():
+        assert got[(cname, "size")] == ctypes.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert got[(cname, fname)] == getattr(py, fname).offset, (cname, fname)
+    assert ctypes.sizeof(_lib.TensorMap) == 128
+
+
+def test_prepack_geometry_matches_reference_formulas():
+    # kernels/weight_prepack.cuh:45-52
+    for n, bm in [(7168, 48), (7168, 56), (6144, 64), (2048, 32), (200, 128), (1, 8)]:
+        assert dg.padded_n(n, bm) == _lib.lib().dg_padded_n(n, bm) == -(-n // bm) * bm
+        assert dg.packed_weight_bytes(n, 4096, bm) == _lib.lib().dg_packed_weight_bytes(n, 4096, bm)
+
+
+def test_status_strings():
+    assert dg.status_string(0) == "ok"
+    assert "injected" in dg.status_string(dg.ERR_INJECTED_TIMEOUT)
+    assert dg.status_string(12345) == "unknown status"
+
+
+@pytest.mark.parametrize("m", [1, 8, 16, 32, 64, 128])
+def test_default_plan_c2(m):
+    p = dg.default_config(m, 7168, 16384).plan(m, 7168, 16384)
+    assert p.error is None
+    # weights on the MMA N side (256 rows per tile), batch on M (64 or 128)
+    assert p.mma_m == (64 if m <= 64 else 128) and p.n_mma == 256 and p.num_output_tiles == 28
+    assert p.a_rows == -(-m // 8) * 8
+    assert p.smem_bytes <= 227 * 1024
+    assert p.grid[0] == 148 or p.grid[0] > 0
+    assert p.ws_floats == p.max_slabs * m * 7168 and p.sem_ints == 28
+
+
+def test_plan_rejections():
+    B = dg.B200Config
+    assert B(m_tile=8).validate(9, 256, 512) == "M out of [1, m_tile]"
+    assert "multiple of 128" in B(m_tile=8).validate(1, 256, 500)
+    assert "subs" in B(m_tile=8, subs=4).validate(1, 256, 384)
+    assert "split_k" in B(m_tile=8, split_k=3).validate(1, 256, 512)
+    assert "m_tile" in B(m_tile=12).validate(1, 256, 512)
+    assert "block_n" in B(m_tile=8, block_n=12).validate(1, 256, 512)
+    assert "227" in B(m_tile=128, subs=4, stages=16).validate(128, 256, 4096)
+    assert "epi_warps" in B(m_tile=8, epi_warps=5).validate(1, 256, 512)
+
+
+def test_launch_rejections_need_no_gpu():
+    B = dg.B200Config
+    p = dg.Problem(9, 256, 512)
+    assert dg.launch(B(m_tile=8), p) == 1
+    assert dg.launch(B(m_tile=8), dg.Problem(1, 256, 500)) == 1
+
+
+def _units(G, U):
+    return [(c * U // G, (c + 1) * U // G) for c in range(G)]
+
+
+@pytest.mark.parametrize("T,C,G", [(56, 64, 148), (16, 16, 148), (128, 48, 256), (7, 128, 148), (3, 5, 15)])
+def test_stream_k_partition_covers_units_once(T, C, G):
+    """The kernel's CTA ranges and their inverse (dg_kernel.cuh cta_of_unit)."""
+    U = T * C
+    G = min(G, U)
+    ranges = _units(G, U)
+    assert ranges[0][0] == 0 and ranges[-1][1] == U
+    for (a0, a1), (b0, _) in zip(ranges, ranges[1:]):
+        assert a1 == b0 and a1 > a0
+    for u in range(U):
+        c = ((u + 1) * G - 1) // U
+        lo, hi = ranges[c]
+        assert lo <= u < hi
+
+
+def test_reference_split_k_is_stream_k_special_case():
+    """grid (tiles, S) linearised as x*S+y gives CTA y of tile x exactly the
+    y-th of S equal K slices (the reference's S-way split)."""
+    T, C, S = 64, 16, 4
+    U, G = T * C, T * S
+    for x in range(T):
+        for y in range(S):
+            c = x * S + y
+            assert (c * U // G, (c + 1) * U // G) == (x * C + y * C // S, x * C + (y + 1) * C // S)
+
+
+def test_kernel_config_mirror_reference_rules():
+    KC = dg.KernelConfig
+    s6 = KC(8, 48, 2, 80, 3, 1, 2, True, True, True, True)
+    assert s6.kSplitKFactor == 2 and s6.kSplitKCta
+    assert KC(8, 32, 2, 80, 3, 1, 2, True, True, True, True, SPLITK_FACTOR=8).kSplitKFactor == 8
+    assert KC(8, 48, 2, 80, 3, 1, 2, True, True, True, False).kSplitKFactor == 1
+    # k_ok_for_splitk pins of kernels/smoke_test.cu:481-486
+    q8 = KC(8, 32, 2, 80, 3, 1, 2, True, True, True, True, SPLITK_FACTOR=8)
+    assert q8.k_ok_for_splitk(4096)
+    assert KC(8, 56, 2, 80, 3, 1, 2, True, True, True, True, SPLITK_FACTOR=8).k_ok_for_splitk(12288)
+    # validate() messages are the reference's
+    assert s6.validate(9, 6144, 7168) == "M out of [1, M_TILE]"
+    assert s6.validate(1, 6144, 7000) == "K must be a multiple of 128"
+    assert KC(8, 64, 1, 112, 4, 1, 4, True, True, True, False).validate(1, 2048, 384) == \
+        "K/128 must be a multiple of SUBS_PER_STAGE"
+    assert s6.validate(1, 6144, 7168) is None
+    # static_assert mirrors
+    with pytest.raises(ValueError):
+        KC(12, 48, 2, 80, 3, 1, 2, True, True, True, False)
+    with pytest.raises(ValueError):
+        KC(8, 48, 2, 80, 3, 1, 2, False, True, True, False, PRELOAD_ACT=True)
+    with pytest.raises(ValueError):
+        KC(8, 48, 4, 168, 3, 1, 2, True, True, True, False)      # register budget
+    with pytest.raises(ValueError):
+        KC(8, 48, 2, 80, 3, 1, 2, True, True, True, True, SPLITK_FACTOR=1)
+
+
+def test_kernel_config_maps_onto_b200_config():
+    k = dg.KernelConfig(8, 56, 2, 80, 3, 1, 2, True, True, False, False)
+    b = k.to_b200()
+    assert (b.m_tile, b.block_n, b.subs, b.stages, b.layout, b.pdl, b.split_k, b.grid_ctas) == \
+        (8, 56, 2, 6, dg.LAYOUT_PACKED, True, 1, 0)
+    plan = dg.make_launch_plan(k, dg.Problem(1, 7168, 16384))
+    assert plan.error is None and plan.grid == (128, 1, 1) and plan.mma_m == 64 and plan.n_mma == 64
