@@ -353,10 +353,13 @@ def b200_arm(args, rank, world, local_rank):
         torch.cuda.synchronize(dev)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for gr in graphs:
-            gr.replay()
-        e1.record(stream)
+        # Graph replays launch on the current stream: make it the stream the
+        # events are recorded on.
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for gr in graphs:
+                gr.replay()
+            e1.record(stream)
         torch.cuda.synchronize(dev)
         t = e0.elapsed_time(e1) / 1e3
         if world > 1:

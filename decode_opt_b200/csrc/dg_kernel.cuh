@@ -549,43 +549,63 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
           if (row_ok)
             store_row_f32<Tr::kColsPerWarp>(p.ws + slab * slab_stride + static_cast<size_t>(m) * N + n0,
                                             partial, ncols, (N & 3) == 0);
-          __threadfence();
+          // Ticket: the CTA barrier orders every thread's workspace stores
+          // before the leader's acquire-release increment (cumulative at GPU
+          // scope), and the last arriver's increment acquires all earlier
+          // contributors' stores; the second barrier hands that to the CTA.
           named_barrier_sync(1, epi_threads);
           if (leader) {
             int last = 0;
             if (*abort_flag == 0) {
-              const int previous = atomicAdd(p.sem + tile, 1);
+              const int previous = atomic_add_acq_rel_gpu(p.sem + tile, 1);
               last = (previous == contributors - 1) ? 1 : 0;
             }
             *ticket_flag = last;
           }
           named_barrier_sync(1, epi_threads);
           if (*ticket_flag != 0) {
-            __threadfence();
             // The tile's M x BN outputs are spread over all active epilogue
-            // threads (consecutive threads -> consecutive columns, so every
-            // access is coalesced); each sums its element over the slabs in
-            // slab order 0, 1, ..., contributors-1 whatever the arrival order,
-            // so the result is bit-identical run to run.
+            // threads (consecutive threads -> consecutive columns, coalesced),
+            // four elements per thread per pass with every slab load of the
+            // pass in flight together; each element is summed over the slabs
+            // in slab order 0, 1, ..., contributors-1 whatever the arrival
+            // order, so the result is bit-identical run to run.
             const int bn_t = min(bn, N - tile * bn);
             const int total_el = M * bn_t;
+            const int T = static_cast<int>(epi_threads);
             const float* base = p.ws + static_cast<size_t>(tile) * bn;
             __nv_bfloat16* obase = p.output + static_cast<size_t>(tile) * bn;
-            for (int e = active_tid; e < total_el; e += static_cast<int>(epi_threads)) {
-              const int mm = e / bn_t;
-              const size_t off = static_cast<size_t>(mm) * N + (e - mm * bn_t);
-              float total = 0.0f;
-              for (int s0 = 0; s0 < contributors; s0 += 8) {
-                float v[8];
+            for (int e0 = active_tid; e0 < total_el; e0 += 4 * T) {
+              size_t off[4];
+              bool ok_e[4];
+              float total[4];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = (s0 + j) < contributors ? __ldcg(base + (s0 + j) * slab_stride + off) : 0.0f;
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                  if ((s0 + j) < contributors) total = (s0 + j) == 0 ? v[j] : total + v[j];
+              for (int q = 0; q < 4; ++q) {
+                const int e = e0 + q * T;
+                ok_e[q] = e < total_el;
+                const int ee = ok_e[q] ? e : e0;
+                const int mm = ee / bn_t;
+                off[q] = static_cast<size_t>(mm) * N + (ee - mm * bn_t);
+                total[q] = 0.0f;
               }
-              obase[off] = __float2bfloat16_rn(total);
+              for (int s0 = 0; s0 < contributors; s0 += 8) {
+                float v[4][8];
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+#pragma unroll
+                  for (int j = 0; j < 8; ++j)
+                    v[q][j] = (s0 + j) < contributors ? __ldcg(base + (s0 + j) * slab_stride + off[q]) : 0.0f;
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+#pragma unroll
+                  for (int j = 0; j < 8; ++j)
+                    if ((s0 + j) < contributors) total[q] = (s0 + j) == 0 ? v[q][j] : total[q] + v[q][j];
+              }
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                if (ok_e[q]) obase[off[q]] = __float2bfloat16_rn(total[q]);
             }
-            if (leader) atomicExch(p.sem + tile, 0);
+            if (leader) store_relaxed_gpu(p.sem + tile, 0);
           }
         }
         u = seg_end;

@@ -248,6 +248,20 @@ __host__ __device__ __forceinline__ constexpr uint32_t make_idesc_e4m3_f32(uint3
   return (1u << 4) | ((mma_n >> 3) << 17) | ((mma_m >> 4) << 24);
 }
 
+// ------------------------------------------------------- global atomics ----
+// Ticket increment with acquire-release semantics at GPU scope: releases the
+// CTA's earlier writes (made visible to this thread through a CTA barrier) and
+// acquires every write released by earlier increments of the same ticket.
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int* addr, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
+
+__device__ __forceinline__ void store_relaxed_gpu(int* addr, int v) {
+  asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
 // ------------------------------------------------------------ named barrier --
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
