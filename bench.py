@@ -59,6 +59,11 @@ def parse_args():
     ap.add_argument("--k", type=int, default=16384)
     ap.add_argument("--layout", choices=["raw", "packed", "swizzled"], default="swizzled")
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--pdl-mode", choices=["independent", "dependent"], default="independent",
+                    help="independent: consecutive GEMMs do not produce each other's inputs (the "
+                         "reference's back-to-back PDL protocol); dependent: every launch waits for "
+                         "the previous grid before reading its activation (a layer chain). Both are "
+                         "timed; this picks the headline.")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
@@ -293,7 +298,10 @@ def b200_arm(args, rank, world, local_rank):
         raise SystemExit(f"N={n} must split into {world} shards of a multiple of 128 rows")
     n_loc = n // world
     layout = {"raw": dg.LAYOUT_RAW, "packed": dg.LAYOUT_PACKED, "swizzled": dg.LAYOUT_PACKED_SWIZZLED}[args.layout]
-    cfg = dg.default_config(m, n_loc, k, layout=layout, pdl=not args.no_pdl)
+    cfg_dep = dg.default_config(m, n_loc, k, layout=layout, pdl=not args.no_pdl)
+    cfg_ind = dg.default_config(m, n_loc, k, layout=layout, pdl=not args.no_pdl, independent_inputs=True)
+    cfg = cfg_ind if args.pdl_mode == "independent" else cfg_dep
+    cfg_other = cfg_dep if args.pdl_mode == "independent" else cfg_ind
     plan = cfg.plan(m, n_loc, k)
     if plan.error:
         raise SystemExit(plan.error)
@@ -326,25 +334,26 @@ def b200_arm(args, rank, world, local_rank):
     stream = torch.cuda.Stream(device=dev)
     pg = dist.group.WORLD if world > 1 else None
 
-    def step(i, with_gather=True):
-        rc = dg.launch_with_maps(cfg, probs[i % nsets], wmaps[i % nsets], amap, stream, pdl_attr=cfg.pdl)
+    def step(i, with_gather=True, c=None):
+        c = cfg if c is None else c
+        rc = dg.launch_with_maps(c, probs[i % nsets], wmaps[i % nsets], amap, stream, pdl_attr=c.pdl)
         if rc != 0:
             raise RuntimeError(f"launch failed: cudaError {rc}")
         if world > 1 and with_gather:
             dist.all_gather_into_tensor(gathered, out, group=pg)
 
-    def capture(count, with_gather):
+    def capture(count, with_gather, c=None):
         graphs = []
         left = count
         with torch.cuda.stream(stream):
             while left > 0:
-                c = min(left, args.graph_chunk)
+                chunk = min(left, args.graph_chunk)
                 gr = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(gr, stream=stream):
-                    for i in range(c):
-                        step(i, with_gather)
+                    for i in range(chunk):
+                        step(i, with_gather, c)
                 graphs.append(gr)
-                left -= c
+                left -= chunk
         return graphs
 
     def timed(graphs):
@@ -390,6 +399,12 @@ def b200_arm(args, rank, world, local_rank):
     clocks.mark()
     t_gemm = timed(graphs_gemm) if world > 1 else t_total
     clocks.stop()
+    # The other PDL mode, same loop (reported beside the headline).
+    graphs_other = capture(args.steps, with_gather=True, c=cfg_other)
+    for gr in graphs_other[:1]:
+        gr.replay()
+    t_other = timed(graphs_other)
+    del graphs_other
     if int(status.item()) != 0:
         raise RuntimeError(f"kernel status {dg.status_string(int(status.item()))}")
     del graphs, graphs_gemm
@@ -506,12 +521,15 @@ def b200_arm(args, rank, world, local_rank):
                         + (f", TP={world} N-shards + NCCL all-gather" if world > 1 else ""),
             "M": m, "N": n, "K": k, "layout": args.layout, "block_n": cfg.block_n, "subs": cfg.subs,
             "stages": plan.stages, "grid": list(plan.grid), "threads_per_cta": plan.block[0],
-            "pdl": cfg.pdl, "rotation_sets": nsets, "working_set_bytes": nsets * set_bytes,
+            "pdl": cfg.pdl, "pdl_mode": args.pdl_mode, "rotation_sets": nsets, "working_set_bytes": nsets * set_bytes,
             "l2_bytes": l2, "cold": "inputs larger than L2 (rotated weight copies), no flush",
             "timing": "CUDA events around CUDA-graph replays of K launches, max over ranks",
         },
         "us_per_gemm": us_step,
         "gemm_only": {"us_per_gemm": us_gemm, "GBps_job": byt_job / (t_gemm / K) / 1e9},
+        "pdl_mode": args.pdl_mode,
+        "other_pdl_mode": {"mode": "dependent" if args.pdl_mode == "independent" else "independent",
+                           "us_per_gemm": t_other / K * 1e6, "GBps_job": byt_job / (t_other / K) / 1e9},
         "pct_of_spec_8TBs": achieved / SPEC_HBM_GBS,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"

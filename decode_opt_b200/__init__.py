@@ -38,14 +38,14 @@ from dataclasses import dataclass, field
 from typing import Optional
 
 from . import _lib
-from ._lib import (ERR_INJECTED_TIMEOUT, FLAG_INJECT_TIMEOUT, LAYOUT_PACKED, LAYOUT_PACKED_SWIZZLED,
+from ._lib import (ERR_INJECTED_TIMEOUT, FLAG_INDEPENDENT_INPUTS, FLAG_INJECT_TIMEOUT, LAYOUT_PACKED, LAYOUT_PACKED_SWIZZLED,
                    LAYOUT_RAW, STATUS_OK, DgConfig, DgPlanInfo, DgProblem, TensorMap)
 
 __all__ = [
     "KernelConfig", "B200Config", "Problem", "LaunchPlan", "make_launch_plan", "make_weight_tma",
     "make_activation_tma", "launch_with_maps", "launch", "padded_n", "packed_weight_bytes",
     "launch_prepack_weight", "prepack_weight", "fp8_decode_gemm", "default_config", "status_string",
-    "LAYOUT_RAW", "LAYOUT_PACKED", "LAYOUT_PACKED_SWIZZLED", "FLAG_INJECT_TIMEOUT",
+    "LAYOUT_RAW", "LAYOUT_PACKED", "LAYOUT_PACKED_SWIZZLED", "FLAG_INJECT_TIMEOUT", "FLAG_INDEPENDENT_INPUTS",
     "ERR_INJECTED_TIMEOUT", "STATUS_OK", "m_tile_for", "flush_l2",
 ]
 
@@ -116,16 +116,20 @@ class B200Config:
         return self.layout != LAYOUT_RAW
 
 
-def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool = True) -> B200Config:
+def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool = True,
+                   independent_inputs: bool = False) -> B200Config:
     """The B200 schedule used by :func:`fp8_decode_gemm` and the benchmark.
 
     256-row weight tiles (the widest tcgen05 N: 8 KiB of weights per MMA
-    instruction), one 128-K block per stage, as many stages as fit in shared
-    memory, and a stream-K grid of one CTA per SM so every SM streams the
-    same number of weight bytes whatever the tile count.
+    instruction), two 128-K blocks per stage in a two-deep ring (64 KiB per
+    bulk copy; deeper rings measured no faster), and a stream-K grid of one
+    CTA per SM so every SM streams the same number of weight bytes whatever
+    the tile count.  `independent_inputs` sets FLAG_INDEPENDENT_INPUTS (see
+    include/decode_gemm_b200.h).
     """
-    return B200Config(m_tile=m_tile_for(m), block_n=256, subs=1, stages=0, layout=layout, pdl=pdl,
-                      split_k=1, grid_ctas=-1)
+    return B200Config(m_tile=m_tile_for(m), block_n=256, subs=2, stages=2, layout=layout, pdl=pdl,
+                      split_k=1, grid_ctas=-1,
+                      flags=FLAG_INDEPENDENT_INPUTS if independent_inputs else 0)
 
 
 @dataclass(frozen=True)

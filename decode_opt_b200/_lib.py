@@ -20,6 +20,7 @@ LAYOUT_PACKED = 1
 LAYOUT_PACKED_SWIZZLED = 2
 
 FLAG_INJECT_TIMEOUT = 2
+FLAG_INDEPENDENT_INPUTS = 4
 
 STATUS_OK = 0
 ERR_INJECTED_TIMEOUT = 0x51

@@ -49,7 +49,8 @@
 // Programmatic dependent launch.  Weight tiles for the first ring pass are
 // requested before griddepcontrol.wait (weights are never written by a
 // preceding kernel); activation loads, scale reads and every global write
-// come after it.  The producer issues griddepcontrol.launch_dependents after
+// come after it -- unless kFlagIndependentInputs declares that the inputs are
+// not produced by the preceding grid, in which case only the writes wait.  The producer issues griddepcontrol.launch_dependents after
 // its last TMA when kFlagPdlTrigger is set (kernels/decode_gemm.cuh:708-713).
 //
 // Failure behaviour.  Every wait is bounded (sm100::mbar_wait_bounded).  On a
@@ -84,6 +85,10 @@ enum Layout : int {
 enum Flags : int {
   kFlagPdlTrigger = 1,     // producer issues griddepcontrol.launch_dependents
   kFlagInjectTimeout = 2,  // test hook: the MMA warp waits on a barrier nobody arrives on
+  // The activation and both scale arrays are not written by the preceding
+  // grid of the stream (e.g. back-to-back GEMMs on one activation): they may
+  // be read before griddepcontrol.wait.  Global writes still wait.
+  kFlagIndependentInputs = 4,
 };
 
 enum Status : int {
@@ -368,7 +373,7 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         mbar_arrive_expect_tx(&full_bar[i], tx_bytes);
         issue_weight(i);
       }
-      griddep_wait();
+      if (!(p.flags & kFlagIndependentInputs)) griddep_wait();
       for (int i = 0; i < first; ++i) issue_act(i);
       int issued = first;
       for (int i = first; i < n_units; ++i) {
@@ -470,7 +475,11 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
       const int active_tid = active_epilogue_rank<Tr>(static_cast<int>(warp), M, bn) * 32 + static_cast<int>(lane);
       const float* a_s_row = p.a_scales + static_cast<size_t>(m_c) * KB;
 
-      griddep_wait();   // activation scales, output and workspace follow the preceding grid
+      // Activation scales, the output and the workspace follow the preceding
+      // grid; with independent inputs only the writes do (waited for at the
+      // first emit).
+      bool waited = !(p.flags & kFlagIndependentInputs);
+      if (waited) griddep_wait();
 
       int acc = 0;
       long long u = u_begin;
@@ -535,6 +544,10 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         }
 
         // ----------------------------------------------------- emit ------
+        if (!waited) {
+          griddep_wait();
+          waited = true;
+        }
         const long long c_first = cta_of_unit(tile_first, G, U);
         const long long c_last = cta_of_unit(tile_first + C - 1, G, U);
         const int contributors = static_cast<int>(c_last - c_first + 1);

@@ -54,8 +54,13 @@ extern "C" {
                                        tcgen05 SWIZZLE_128B operand layout (B200 native) */
 
 /* Kernel flags (dg_config.flags). */
-#define DG_FLAG_INJECT_TIMEOUT 2 /* tests: one wait can never complete, so the bounded
-                                    wait expires and the kernel reports status 0x51 */
+#define DG_FLAG_INJECT_TIMEOUT 2     /* tests: one wait can never complete, so the bounded
+                                        wait expires and the kernel reports status 0x51 */
+#define DG_FLAG_INDEPENDENT_INPUTS 4 /* the activation and scales are not written by the
+                                        preceding kernel on the stream (e.g. back-to-back
+                                        GEMMs on one activation): with programmatic
+                                        dependent launch they are read before
+                                        griddepcontrol.wait; global writes still wait */
 
 /* Device status codes written to dg_problem.status (first error wins). */
 #define DG_STATUS_OK 0

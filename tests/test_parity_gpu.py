@@ -284,6 +284,30 @@ def test_pdl_back_to_back_split_k_stays_correct():
     assert np.array_equal(final.view(np.uint32), got.view(np.uint32))
 
 
+@pytest.mark.parametrize("independent", [False, True])
+def test_pdl_back_to_back_stream_k_both_modes(independent):
+    """Back-to-back stream-K launches with programmatic serialization, with and
+    without FLAG_INDEPENDENT_INPUTS: correct, tickets clean, bit-identical."""
+    import torch
+    n, k, m = 2048, 4096, 2
+    w, ws = oracle.gen_weight_smoke(n, k, 81)
+    a, as_ = oracle.gen_activation_smoke(m, k, 82)
+    ref = oracle.compute_reference(a, as_, w, ws)
+    dc = DeviceCase(w, ws, a, as_, n)
+    c = dg.default_config(m, n, k, layout=dg.LAYOUT_RAW, independent_inputs=independent)
+    rc, got, status = dc.run(c)
+    assert rc == 0 and status == 0
+    assert check_against_oracle(got, ref)[0]
+    p = dg.Problem(m, n, k, dc.a, dc.w, dc.ws, dc.as_, dc.out, dc.splitk_ws, dc.sem, dc.status)
+    wm, am = dg.make_weight_tma(c, p), dg.make_activation_tma(c, p)
+    for _ in range(300):
+        assert dg.launch_with_maps(c, p, wm, am, None, pdl_attr=True) == 0
+    torch.cuda.synchronize()
+    assert int(dc.status.item()) == 0
+    assert dc.sem_clean()
+    assert np.array_equal(dc.out.float().cpu().numpy().view(np.uint32), got.view(np.uint32))
+
+
 def test_rejected_launches_return_invalid_value():
     import torch
     dc = DeviceCase(*oracle.gen_weight_smoke(256, 512, 1), *oracle.gen_activation_smoke(2, 512, 2), 256)
