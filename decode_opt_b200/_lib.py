@@ -21,6 +21,8 @@ LAYOUT_PACKED_SWIZZLED = 2
 
 FLAG_INJECT_TIMEOUT = 2
 FLAG_INDEPENDENT_INPUTS = 4
+STATIC_SEM_INTS = 4096          # DG_STATIC_SEM_INTS
+STATIC_WS_FLOATS = 2097152      # DG_STATIC_WS_FLOATS
 
 STATUS_OK = 0
 ERR_INJECTED_TIMEOUT = 0x51
@@ -30,7 +32,7 @@ EXPORTED_SYMBOLS = (
     "dg_abi_version", "dg_plan", "dg_make_weight_map", "dg_make_activation_map",
     "dg_launch_with_maps", "dg_launch", "dg_prepack_weight", "dg_padded_n",
     "dg_packed_weight_bytes", "dg_status_string", "dg_flush_l2", "dg_probe_bulk_stream",
-    "dg_probe_naive_read", "dg_num_sms",
+    "dg_probe_naive_read", "dg_num_sms", "dg_launch_static_scratch",
 )
 
 
@@ -112,6 +114,7 @@ def lib():
     L.dg_launch_with_maps.argtypes = [cfgp, probp, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                       ctypes.c_int]
     L.dg_launch.argtypes = [cfgp, probp, ctypes.c_void_p]
+    L.dg_launch_static_scratch.argtypes = [cfgp, probp, ctypes.c_void_p, ctypes.POINTER(DgPlanInfo)]
     L.dg_prepack_weight.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                     ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
     L.dg_padded_n.argtypes = [ctypes.c_int, ctypes.c_int]

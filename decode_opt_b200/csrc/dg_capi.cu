@@ -11,9 +11,19 @@
 #include <atomic>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "decode_gemm_b200.h"
 #include "dg_host.cuh"
+
+// Scratch of dg_launch_static_scratch: the split-K tickets (first
+// DG_STATIC_SEM_INTS ints) followed by the split-K workspace
+// (DG_STATIC_WS_FLOATS floats).  One copy per device, shared by every call on
+// that device; it is zero at module load and otherwise keeps the last call's
+// contents.
+static_assert((DG_STATIC_SEM_INTS * sizeof(int)) % 256 == 0, "workspace must stay 256-byte aligned");
+static __device__ __align__(256) unsigned char
+    g_static_scratch[DG_STATIC_SEM_INTS * sizeof(int) + DG_STATIC_WS_FLOATS * sizeof(float)];
 
 namespace {
 
@@ -140,6 +150,29 @@ __global__ void prepack_kernel(const uint4* __restrict__ src, uint4* __restrict_
   }
 }
 
+// Device address of g_static_scratch on the current device, looked up once per
+// device (cudaGetSymbolAddress, with that device current) and cached.
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_ptr[kMaxScratchDevices] = {};
+
+cudaError_t static_scratch_on_current_device(void** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= kMaxScratchDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_static_scratch);
+    if (err != cudaSuccess) return err;
+    if (ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 255u) != 0) return cudaErrorInvalidDevicePointer;
+    g_scratch_ptr[dev] = ptr;
+  }
+  *out = g_scratch_ptr[dev];
+  return cudaSuccess;
+}
+
 __global__ void flush_kernel(uint4* buf, size_t n16) {
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
@@ -195,6 +228,42 @@ int dg_launch(const dg_config* cfg, const dg_problem* p, void* stream) {
   err = dg::make_activation_map(&a, c, p->activation, p->M, p->K);
   if (err != cudaSuccess) return err;
   return launch_impl(cfg, p, &w, &a, static_cast<cudaStream_t>(stream), c.pdl != 0);
+}
+
+int dg_launch_static_scratch(const dg_config* cfg, const dg_problem* p, void* stream, dg_plan_info* info) {
+  if (info != nullptr) std::memset(info, 0, sizeof(*info));
+  if (cfg == nullptr || p == nullptr) return cudaErrorInvalidValue;
+  const Config c = to_config(cfg);
+  const Plan plan = dg::make_plan(c, p->M, p->N, p->K, current_sm_count());
+  if (plan.error != nullptr) {
+    if (info != nullptr) fill_info(plan, info);
+    return cudaErrorInvalidValue;
+  }
+  if (plan.ws_floats > DG_STATIC_WS_FLOATS || static_cast<unsigned>(plan.sem_ints) > DG_STATIC_SEM_INTS) {
+    if (info != nullptr) {
+      fill_info(plan, info);
+      std::snprintf(info->error, sizeof(info->error), "static scratch too small: needs %llu ws floats (max %u), %d tickets (max %u)",
+                    static_cast<unsigned long long>(plan.ws_floats), DG_STATIC_WS_FLOATS, plan.sem_ints,
+                    DG_STATIC_SEM_INTS);
+    }
+    return cudaErrorInvalidValue;
+  }
+  void* scratch = nullptr;
+  cudaError_t err = static_scratch_on_current_device(&scratch);
+  if (err != cudaSuccess) return err;
+  int* sem = static_cast<int*>(scratch);
+  float* ws = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) + DG_STATIC_SEM_INTS * sizeof(int));
+  // The tickets must start at zero; the workspace slabs are fully written
+  // before they are read, so they need no clearing.
+  if (plan.sem_ints > 0) {
+    err = cudaMemsetAsync(sem, 0, static_cast<size_t>(plan.sem_ints) * sizeof(int), static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return err;
+  }
+  dg_problem q = *p;
+  q.splitk_ws = ws;
+  q.splitk_sem = sem;
+  if (info != nullptr) fill_info(plan, info);
+  return dg_launch(cfg, &q, stream);
 }
 
 int dg_prepack_weight(const void* src, void* dst, int n, int k, int block_n, int layout, void* stream) {

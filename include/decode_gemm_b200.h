@@ -25,6 +25,8 @@
  *                           (and the harness's direct cudaLaunchKernelEx of
  *                           fp8_decode_gemm<Cfg>, bench/variant_impl.cuh:136-165)
  *   dg_launch               launch              kernels/decode_gemm.cuh:1150-1159
+ *   dg_launch_static_scratch (none: no counterpart in the reference) dg_launch
+ *                           with library-owned static split-K scratch
  *   dg_prepack_weight       prepack::launch_prepack_weight kernels/weight_prepack.cuh:101-120
  *   dg_padded_n             prepack::padded_n   kernels/weight_prepack.cuh:45-47
  *   dg_packed_weight_bytes  prepack::packed_weight_bytes kernels/weight_prepack.cuh:50-52
@@ -143,6 +145,30 @@ int dg_launch_with_maps(const dg_config* cfg, const dg_problem* p, const void* w
 
 /* Encodes both maps, then launches (attribute follows cfg->pdl). */
 int dg_launch(const dg_config* cfg, const dg_problem* p, void* stream);
+
+/* Capacity of the library's static split-K scratch (dg_launch_static_scratch):
+   4096 tickets (16 KiB) + 2 Mi workspace floats (8 MiB) per device. */
+#define DG_STATIC_SEM_INTS 4096u
+#define DG_STATIC_WS_FLOATS 2097152u
+
+/* No counterpart in the reference (which always takes caller-allocated
+   splitk_ws / splitk_sem).  dg_launch for callers that cannot allocate device
+   memory: p->splitk_ws and p->splitk_sem are ignored and the split-K tickets
+   and workspace come from a file-scope __device__ array inside the library, so
+   the call allocates nothing (no cudaMalloc / cudaFree, no allocating library
+   routine).  It clears the tickets it will use (cudaMemsetAsync on `stream`)
+   and launches on `stream` as dg_launch does.
+   - Limit: returns cudaErrorInvalidValue (1), with info->error saying so, when
+     the plan needs more than DG_STATIC_WS_FLOATS workspace floats or more than
+     DG_STATIC_SEM_INTS tickets (dg_plan reports both as ws_floats, sem_ints).
+   - The first call on each device looks up the array's address
+     (cudaGetSymbolAddress with that device current): make that first call
+     before any stream capture on the device.
+   - Every call on a device shares the one array: calls that overlap on the GPU
+     (other streams, other host threads) race.  Calls in order on one stream are
+     safe.
+   `info` may be NULL; when given it receives the plan (or the error). */
+int dg_launch_static_scratch(const dg_config* cfg, const dg_problem* p, void* stream, dg_plan_info* info);
 
 /* raw [n,k] -> layout (DG_LAYOUT_PACKED or DG_LAYOUT_PACKED_SWIZZLED); dst has
    dg_packed_weight_bytes(n, k, block_n) bytes.  k must be a multiple of 128. */

@@ -1,0 +1,106 @@
+"""GPU tests of dg_launch_static_scratch, the entry point that allocates
+nothing: its split-K tickets and workspace live in the library's static
+__device__ array.  Each case runs two calls in a row through the C ABI (the
+second sees the first call's leftover scratch) and compares both outputs with
+dg_launch on caller-allocated workspace.  Named so pytest collects it last.
+"""
+
+import ctypes
+
+import pytest
+
+import decode_opt_b200 as dg
+from decode_opt_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+N, K = 4096, 7168
+
+
+def _inputs(m, seed):
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    act = (torch.randn(m, K, device="cuda", generator=g) * 2).to(torch.float8_e4m3fn)
+    a_s = torch.rand(m, K // 128, device="cuda", generator=g) * 0.02 + 0.001
+    return act, a_s
+
+
+def _weight(layout):
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(7)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 2).to(torch.float8_e4m3fn)
+    w_s = torch.rand((N + 127) // 128, K // 128, device="cuda", generator=g) * 0.02 + 0.001
+    w_dev = w if layout == dg.LAYOUT_RAW else dg.prepack_weight(w, 256, layout)
+    return w_dev, w_s
+
+
+def _with_workspace(cfg, m, act, a_s, w_dev, w_s, status):
+    """dg_launch with caller-allocated split-K scratch (the existing path)."""
+    import torch
+    plan = cfg.plan(m, N, K)
+    assert plan.error is None, plan.error
+    ws = torch.empty(max(plan.ws_floats, 1), dtype=torch.float32, device="cuda")
+    sem = torch.zeros(max(plan.sem_ints, 1), dtype=torch.int32, device="cuda")
+    out = torch.zeros(m, N, dtype=torch.bfloat16, device="cuda")
+    p = dg.Problem(m, N, K, act, w_dev, w_s, a_s, out, ws, sem, status)
+    rc = _lib.lib().dg_launch(ctypes.byref(cfg.to_dg()), ctypes.byref(p.to_dg()),
+                              torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    return out
+
+
+def _close(got, want):
+    g, w = got.float(), want.float()
+    rms = w.pow(2).mean().sqrt().item()
+    rel = ((g - w).norm() / w.norm().clamp_min(1e-30)).item()
+    bound = 1e-2 * w.abs().clamp_min(1e-2 * rms)
+    return rel <= 1e-6 and bool(((g - w).abs() <= bound).all())
+
+
+@pytest.mark.parametrize("m,layout", [(1, dg.LAYOUT_PACKED_SWIZZLED), (8, dg.LAYOUT_RAW),
+                                      (32, dg.LAYOUT_PACKED_SWIZZLED)])
+def test_static_scratch_matches_dg_launch_twice(m, layout):
+    import torch
+    cfg = dg.default_config(m, N, K, layout=layout)
+    w_dev, w_s = _weight(layout)
+    inputs = [_inputs(m, 100 + m), _inputs(m, 200 + m)]
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    wants = [_with_workspace(cfg, m, a, s, w_dev, w_s, status) for a, s in inputs]
+    outs = [torch.zeros(m, N, dtype=torch.bfloat16, device="cuda") for _ in inputs]
+    torch.cuda.synchronize()
+    allocated = torch.cuda.memory_allocated()
+    for (act, a_s), out in zip(inputs, outs):
+        # splitk_ws / splitk_sem are ignored: pass NULL.
+        p = dg.Problem(m, N, K, act, w_dev, w_s, a_s, out, None, None, status)
+        info = _lib.DgPlanInfo()
+        rc = _lib.lib().dg_launch_static_scratch(ctypes.byref(cfg.to_dg()), ctypes.byref(p.to_dg()),
+                                                 torch.cuda.current_stream().cuda_stream, ctypes.byref(info))
+        assert rc == 0, info.error
+        assert info.max_slabs > 1, "the case must split tiles, so that the static scratch is used"
+        assert info.ws_floats <= _lib.STATIC_WS_FLOATS
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated() == allocated
+    assert int(status.item()) == 0, dg.status_string(int(status.item()))
+    for got, want in zip(outs, wants):
+        assert _close(got, want)
+
+
+def test_static_scratch_rejects_plans_over_the_limit():
+    import torch
+    m, n, k = 128, 7168, 16384
+    cfg = dg.default_config(m, n, k, layout=dg.LAYOUT_RAW)
+    plan = cfg.plan(m, n, k)
+    assert plan.error is None and plan.ws_floats > _lib.STATIC_WS_FLOATS
+    act = torch.zeros(m, k, dtype=torch.uint8, device="cuda")
+    w = torch.zeros(n, k, dtype=torch.uint8, device="cuda")
+    w_s = torch.ones((n + 127) // 128, k // 128, device="cuda")
+    a_s = torch.ones(m, k // 128, device="cuda")
+    out = torch.zeros(m, n, dtype=torch.bfloat16, device="cuda")
+    p = dg.Problem(m, n, k, act, w, w_s, a_s, out, None, None, None)
+    info = _lib.DgPlanInfo()
+    rc = _lib.lib().dg_launch_static_scratch(ctypes.byref(cfg.to_dg()), ctypes.byref(p.to_dg()),
+                                             torch.cuda.current_stream().cuda_stream, ctypes.byref(info))
+    assert rc == dg.CUDA_ERROR_INVALID_VALUE
+    assert b"static scratch too small" in info.error
+    torch.cuda.synchronize()
+    assert not out.any()
