@@ -55,27 +55,28 @@ int current_sm_count() {
   return sms;
 }
 
-// One kernel per batch class (MMA M, epilogue warps per quarter); everything
-// else is runtime.
+// One kernel per batch class (MMA M, batch copies, epilogue warps per
+// quarter); everything else is runtime.
 struct KernelEntry {
   KernelFn fn;
   std::atomic<int> smem_high_water;
+  cudaError_t pool_check;   // register pool covers the setmaxnreg split
 };
 
-template <int MMA_M, int EPW>
+template <int MMA_M, int COPIES, int EPW>
 KernelEntry* entry() {
-  static KernelEntry e{dg::kernel_ptr<MMA_M, EPW>(), {0}};
+  static KernelEntry e{dg::kernel_ptr<MMA_M, COPIES, EPW>(), {0},
+                       dg::check_register_pool(reinterpret_cast<const void*>(dg::kernel_ptr<MMA_M, COPIES, EPW>()),
+                                               COPIES, EPW)};
   return &e;
 }
 
-KernelEntry* select_kernel(int mma_m, int epw) {
-  if (mma_m == 128) return epw == 4 ? entry<128, 4>() : nullptr;
-  switch (epw) {
-    case 1: return entry<64, 1>();
-    case 2: return entry<64, 2>();
-    case 4: return entry<64, 4>();
-    default: return nullptr;
-  }
+KernelEntry* select_kernel(int mma_m, int copies, int epw) {
+  if (mma_m == 64 && copies == 4 && epw == 1) return entry<64, 4, 1>();
+  if (mma_m == 128 && copies == 4 && epw == 1) return entry<128, 4, 1>();
+  if (mma_m == 128 && copies == 2 && epw == 2) return entry<128, 2, 2>();
+  if (mma_m == 128 && copies == 1 && epw == 2) return entry<128, 1, 2>();
+  return nullptr;
 }
 
 void fill_info(const Plan& plan, dg_plan_info* out) {
@@ -118,8 +119,9 @@ int launch_impl(const dg_config* cfg, const dg_problem* prob, const CUtensorMap*
   p.weight = static_cast<const uint8_t*>(prob->weight);
   const cudaError_t buf_err = dg::check_buffers(plan, p);
   if (buf_err != cudaSuccess) return buf_err;
-  KernelEntry* k = select_kernel(plan.mma_m, plan.epw);
+  KernelEntry* k = select_kernel(plan.mma_m, plan.copies, plan.epw);
   if (k == nullptr) return cudaErrorInvalidValue;
+  if (k->pool_check != cudaSuccess) return k->pool_check;
   const cudaError_t attr_err =
       dg::ensure_smem(reinterpret_cast<const void*>(k->fn), plan.smem_bytes, &k->smem_high_water);
   if (attr_err != cudaSuccess) return attr_err;
@@ -303,6 +305,7 @@ const char* dg_status_string(int code) {
     case DG_ERR_DRAIN_MMA: return "teardown: MMAs did not complete in time";
     case DG_ERR_INJECTED_TIMEOUT: return "injected timeout (test hook)";
     case DG_ERR_BAD_LAUNCH_SHAPE: return "launch grid/block does not match the plan";
+    case DG_ERR_REDUCE_WAIT: return "split reduction: a workspace bulk copy did not land in time";
     default: return "unknown status";
   }
 }

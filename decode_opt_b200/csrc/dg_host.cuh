@@ -54,6 +54,7 @@ struct Plan {
   dim3 block{0, 0, 0};
   uint32_t smem_bytes = 0;
   int mma_m = 0;
+  int copies = 0;           // batch copies along the MMA M side (1, 2 or 4)
   int epw = 0;              // epilogue warps per TMEM lane quarter (1, 2 or 4)
   int epi_warps = 0;
   int max_slabs = 1;        // workspace slabs needed (1 = no split tile)
@@ -63,14 +64,27 @@ struct Plan {
   const char* error = nullptr;
 };
 
-// Kernel instantiation for a batch of M rows: the MMA M (64, or 128 past 64
-// rows) and the epilogue warps per lane quarter, which fixes how many copies
-// of the batch the activation tile holds (4 / epw).
-inline int mma_m_for(int M) { return M <= 64 ? 64 : 128; }
+// Kernel instantiation for a batch of M rows: the MMA M, the batch copies
+// the activation tile holds along it, and the epilogue warps per TMEM lane
+// quarter.  Every class keeps all four lane quarters busy in the epilogue:
+//   M <= 16   MMA M  64, 4 copies of 16 rows, 4 warps x 64 columns
+//   M <= 32   MMA M 128, 4 copies of 32 rows, 4 warps x 64 columns
+//   M <= 64   MMA M 128, 2 copies of 64 rows, 8 warps x 64 columns
+//   M <= 128  MMA M 128, 1 copy,             8 warps x 128 columns
+struct BatchClass {
+  int mma_m;
+  int copies;
+  int epw;
+};
 
-inline int epw_for(int M) { return M <= 16 ? 1 : M <= 32 ? 2 : 4; }
+inline BatchClass batch_class_for(int M) {
+  if (M <= 16) return {64, 4, 1};
+  if (M <= 32) return {128, 4, 1};
+  if (M <= 64) return {128, 2, 2};
+  return {128, 1, 2};
+}
 
-inline int epi_warps_for(int epw) { return 4 * epw; }
+inline int mma_m_for(int M) { return batch_class_for(M).mma_m; }
 
 constexpr int kAccumBuffers = 2;
 
@@ -111,9 +125,10 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms) {
   const long long U = static_cast<long long>(T) * C;
   if (U > (1ll << 40)) return plan.error = "problem too large", plan;
 
-  const int mma_m = mma_m_for(M);
-  const int epw = epw_for(M);
-  const int copies = 4 / epw;
+  const BatchClass bc = batch_class_for(M);
+  const int mma_m = bc.mma_m;
+  const int epw = bc.epw;
+  const int copies = bc.copies;
   const int n_mma = ((c.block_n + 15) / 16) * 16;
   const int a_rows = ((M + 7) / 8) * 8;
   if (a_rows > mma_m / copies) return plan.error = "batch does not fit its activation copy", plan;
@@ -155,6 +170,7 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms) {
     const long long last = cta_of_unit(static_cast<long long>(t) * C + C - 1, G, U);
     max_slabs = std::max(max_slabs, static_cast<int>(last - first + 1));
   }
+  if (max_slabs > kMaxContributors) return plan.error = "split too fine: more than 1023 CTAs share one tile", plan;
 
   KernelParams& p = plan.params;
   p.M = M;
@@ -170,7 +186,11 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms) {
   p.chunks_per_tile = C;
   p.num_kb = num_kb;
   p.num_ctas = static_cast<int>(G);
-  p.flags = (c.pdl ? kFlagPdlTrigger : 0) | (c.flags & ~kFlagPdlTrigger);
+  // Contributors of a split tile may wait (bounded) for one another only when
+  // the whole grid fits on the device at once: one CTA per SM always fits.
+  const bool coop = num_sms > 0 && G <= num_sms;
+  p.flags = (c.pdl ? kFlagPdlTrigger : 0) | (coop ? kFlagCoopReduce : 0) |
+            (c.flags & ~(kFlagPdlTrigger | kFlagCoopReduce));
   p.total_units = U;
   p.w_stage_bytes = w_stage;
   p.a_stage_bytes = a_stage;
@@ -180,10 +200,11 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms) {
   p.smem_bytes = smem_for(stages);
   p.timeout_ns = c.timeout_ns ? c.timeout_ns : kDefaultTimeoutNs;
 
-  plan.epi_warps = epi_warps_for(epw);
-  plan.block = dim3(static_cast<unsigned>((plan.epi_warps + 2) * 32), 1u, 1u);
+  plan.epi_warps = 4 * epw;
+  plan.block = dim3(static_cast<unsigned>(block_threads(copies, epw)), 1u, 1u);
   plan.smem_bytes = p.smem_bytes;
   plan.mma_m = mma_m;
+  plan.copies = copies;
   plan.epw = epw;
   plan.max_slabs = max_slabs;
   plan.ws_floats = max_slabs > 1 ? static_cast<size_t>(max_slabs) * M * static_cast<size_t>(N) : 0;
@@ -274,9 +295,23 @@ inline cudaError_t make_activation_map(CUtensorMap* map, const Config& c, const 
 // ---------------------------------------------------------------- launch ---
 using KernelFn = void (*)(KernelParams, CUtensorMap, CUtensorMap);
 
-template <int MMA_M, int EPW>
+template <int MMA_M, int COPIES, int EPW>
 inline KernelFn kernel_ptr() {
-  return reinterpret_cast<KernelFn>(&dg_decode_gemm_kernel<MMA_M, EPW>);
+  return reinterpret_cast<KernelFn>(&dg_decode_gemm_kernel<MMA_M, COPIES, EPW>);
+}
+
+// A kernel that reallocates registers (setmaxnreg) needs a launch register
+// pool, threads x registers per thread at launch, that covers the split;
+// setmaxnreg.inc would otherwise wait forever.  Checked once per kernel.
+inline cudaError_t check_register_pool(const void* fn, int copies, int epw) {
+  if (!uses_reg_realloc(copies, epw)) return cudaSuccess;
+  cudaFuncAttributes attr{};
+  const cudaError_t err = cudaFuncGetAttributes(&attr, fn);
+  if (err != cudaSuccess) return err;
+  const long long pool = static_cast<long long>(attr.numRegs) * block_threads(copies, epw);
+  const long long need = static_cast<long long>(kEpiRegs) * 32 * 4 * epw +
+                         static_cast<long long>(kCtrlRegs) * 32 * ctrl_warps(copies, epw);
+  return pool >= need ? cudaSuccess : cudaErrorInvalidConfiguration;
 }
 
 // Raises the dynamic-smem limit of `fn` once per (kernel, size).  Unlike the

@@ -25,24 +25,31 @@
 // Warp roles (one CTA per SM):
 //   warps 0 .. 4E-1   epilogue.  Warp w reads TMEM lane quarter w % 4, i.e.
 //                     the batch rows of that quarter, and column group w / 4
-//                     (up to 128 weight rows) of the tile: tcgen05.ld, scale fold into fp32
-//                     partials held in registers, then bf16 store or the split
-//                     reduction.  Warps whose rows are all >= M, or whose
-//                     columns are past the tile, stay idle.
+//                     (64 or 128 weight rows) of the tile: tcgen05.ld, scale
+//                     fold into fp32 partials held in registers (packed
+//                     fma.rn.f32x2), then bf16 store or the split reduction.
+//                     Warps whose rows are all >= M, or whose columns are past
+//                     the tile, stay idle.
 //   warp 4E           TMA producer: weight and activation tiles of one
 //                     (tile, chunk) unit per pipeline stage, `stages` deep.
 //   warp 4E+1         MMA issuer and TMEM owner: one lane issues the MMAs;
 //                     tcgen05.commit frees smem stages and publishes finished
 //                     accumulators.
+//   warps 4E+2, 4E+3  only when each epilogue warp folds 128 columns: idle
+//                     warps that complete the control warpgroup, which then
+//                     hands registers to the epilogue warpgroups (setmaxnreg).
 //
 // Work decomposition (stream-K).  The (tile, chunk) units, chunk = `subs`
 // consecutive 128-K blocks, are numbered tile-major; CTA c of G processes the
 // contiguous range [floor(c*U/G), floor((c+1)*U/G)).  A tile whose units all
 // fall in one CTA is written directly in bf16.  Otherwise each contributing
-// CTA stores its fp32 partial into workspace slab (c - first contributor);
-// a per-tile ticket elects the last arriver, which sums the slabs in slab
-// order 0,1,2,... -- a fixed order, so results are run-to-run bit-identical --
-// stores bf16 and re-zeroes the ticket.  The reference's S-way CTA split-K
+// CTA stores its fp32 partial into workspace slab (c - first contributor) and
+// counts itself in the tile's state word.  When a CTA has finished its range
+// it reduces chunks of its split tiles -- each element summed over the slabs
+// in slab order 0,1,2,..., a fixed order, so results are run-to-run
+// bit-identical -- and stores bf16: every contributor helps when the whole
+// grid is resident at once (kFlagCoopReduce), else the last arriver alone;
+// the finisher of the last chunk re-zeroes the word.  The reference's S-way CTA split-K
 // (gridDim.y = S, kernels/decode_gemm.cuh:1015-1077) is the special case
 // G = tiles*S, where every range is one S-th of one tile.
 //
@@ -50,8 +57,9 @@
 // requested before griddepcontrol.wait (weights are never written by a
 // preceding kernel); activation loads, scale reads and every global write
 // come after it -- unless kFlagIndependentInputs declares that the inputs are
-// not produced by the preceding grid, in which case only the writes wait.  The producer issues griddepcontrol.launch_dependents after
-// its last TMA when kFlagPdlTrigger is set (kernels/decode_gemm.cuh:708-713).
+// not produced by the preceding grid, in which case only the writes wait.  The
+// producer issues griddepcontrol.launch_dependents after its last TMA when
+// kFlagPdlTrigger is set (kernels/decode_gemm.cuh:708-713).
 //
 // Failure behaviour.  Every wait is bounded (sm100::mbar_wait_bounded).  On a
 // timeout the CTA records an error code in *status, raises a CTA-wide abort
@@ -89,7 +97,25 @@ enum Flags : int {
   // grid of the stream (e.g. back-to-back GEMMs on one activation): they may
   // be read before griddepcontrol.wait.  Global writes still wait.
   kFlagIndependentInputs = 4,
+  // Set by the planner when the whole grid can be resident at once: every
+  // contributor of a split tile helps reduce it (bounded wait for the others).
+  kFlagCoopReduce = 8,
 };
+
+// State word of a split tile (one int per tile, zero between launches):
+//   bits  0..9   contributors that have stored their slab (arrivals)
+//   bits 10..20  reduction chunks claimed
+//   bits 21..31  reduction chunks finished
+// The CTA that finishes the last chunk stores zero.
+constexpr int kArrivalMask = 0x3ff;
+constexpr int kMaxContributors = kArrivalMask;   // 1023 CTAs per tile at most
+constexpr int kClaimShift = 10;
+constexpr int kDoneShift = 21;
+constexpr int kCountMask = 0x7ff;
+// How long a contributor that has finished its own work waits for the other
+// contributors of its split tiles before leaving their reduction to the last
+// arriver (no error: the last arriver reduces every chunk nobody claimed).
+constexpr uint64_t kHelpWaitNs = 20000ull;
 
 enum Status : int {
   kStatusOk = 0,
@@ -101,6 +127,7 @@ enum Status : int {
   kErrDrainMma = 0x42,
   kErrInjectedTimeout = 0x51,
   kErrBadLaunchShape = 0x61,
+  kErrReduceWait = 0x71,      // split reduction: a workspace bulk copy did not land in time
 };
 
 // Everything the kernel needs, computed on the host (dg_host.cuh) and passed
@@ -135,38 +162,61 @@ struct KernelParams {
   const uint8_t* weight;     // kLayoutPackedSwizzled: bulk-copy source
 };
 
+// Epilogue geometry shared with the host planner: weight columns one
+// epilogue warp folds, control warps, threads per CTA.
+__host__ __device__ constexpr int cols_per_warp(int copies, int epw) { return 256 / (copies * epw); }
+// 128 fp32 partials per thread need more registers than an even split of the
+// register file gives, so the control warps then fill a whole warpgroup that
+// hands registers to the epilogue warpgroups (setmaxnreg).
+__host__ __device__ constexpr bool uses_reg_realloc(int copies, int epw) { return cols_per_warp(copies, epw) > 64; }
+__host__ __device__ constexpr int ctrl_warps(int copies, int epw) { return uses_reg_realloc(copies, epw) ? 4 : 2; }
+__host__ __device__ constexpr int block_threads(int copies, int epw) {
+  return (4 * epw + ctrl_warps(copies, epw)) * 32;
+}
+constexpr uint32_t kCtrlRegs = 40;    // per thread, control warpgroup after setmaxnreg.dec
+constexpr uint32_t kEpiRegs = 232;    // per thread, epilogue warpgroups after setmaxnreg.inc
+
 // Compile-time geometry of one kernel instantiation: the MMA M (batch rows,
-// padded) and the number of epilogue warps per TMEM lane quarter.
+// padded), the number of batch copies along it and the number of epilogue
+// warps per TMEM lane quarter.
 //
 // Batch replication.  TMEM lane quarter q holds accumulator rows
 // [q*R4, (q+1)*R4), R4 = MMA_M/4.  A batch that fills fewer quarters than
-// there are is replicated: the activation tile is loaded kCopies = 4/EPW
-// times, into row blocks of MMA_M/kCopies rows, so every quarter holds the
-// whole batch (or half of it) and quarter q folds only the weight columns of
-// its copy.  The MMA costs the same (its M is padded anyway); the epilogue's
-// TMEM reads and FMAs are spread over all four quarters instead of landing on
-// the one quarter that holds the real rows.
-template <int MMA_M_, int EPW_>
+// there are is replicated: the activation tile is loaded kCopies times, into
+// row blocks of MMA_M/kCopies rows, so the quarters of copy c hold the whole
+// batch and fold only the weight columns [c*256/kCopies, (c+1)*256/kCopies).
+// The MMA costs the same (its M is padded anyway); the epilogue's TMEM reads
+// and FMAs are spread over all four quarters instead of landing on the
+// quarters that hold the real rows.
+template <int MMA_M_, int COPIES_, int EPW_>
 struct KernelTraits {
   static constexpr int kMmaM = MMA_M_;
+  static constexpr int kCopies = COPIES_;            // batch copies along the MMA M side
   static constexpr int kEpw = EPW_;                  // epilogue warps per lane quarter
   static_assert(kMmaM == 64 || kMmaM == 128, "tcgen05 cta_group::1 M is 64 or 128");
+  static_assert(kCopies == 1 || kCopies == 2 || kCopies == 4, "1, 2 or 4 batch copies");
   static_assert(kEpw == 1 || kEpw == 2 || kEpw == 4, "1, 2 or 4 epilogue warps per quarter");
   static constexpr int kBnMax = 256;                 // accumulator columns per buffer
-  static constexpr int kColsPerWarp = 64;            // weight columns one epilogue warp folds
-  static constexpr int kCopies = 4 / kEpw;           // batch copies along the MMA M side
   static constexpr int kQuartersPerCopy = 4 / kCopies;
   static constexpr int kColsPerCopy = kBnMax / kCopies;
+  static constexpr int kColsPerWarp = cols_per_warp(kCopies, kEpw);
+  static_assert(kColsPerWarp == 64 || kColsPerWarp == 128, "64 or 128 columns per epilogue warp");
   static constexpr int kRowsPerQuarter = kMmaM / 4;  // accumulator rows per lane quarter
   static constexpr int kRowsPerCopy = kMmaM / kCopies;
   static constexpr int kEpiWarps = 4 * kEpw;
   static constexpr int kEpiThreads = kEpiWarps * 32;
+  static constexpr bool kRegRealloc = uses_reg_realloc(kCopies, kEpw);
   static constexpr int kProducerWarp = kEpiWarps;
   static constexpr int kMmaWarp = kEpiWarps + 1;
-  static constexpr int kThreads = (kEpiWarps + 2) * 32;
+  static constexpr int kThreads = block_threads(kCopies, kEpw);
+  static constexpr int kLdBatch = 4;                 // 16-column TMEM loads per wait
+  static constexpr int kRedGroups = 2;               // plain-path reduction units in flight per thread
   static constexpr int kNumBufs = 2;                 // 2 x 256 columns = all of TMEM
   static constexpr uint32_t kTmemCols = 512u;
   static_assert(kColsPerCopy == kEpw * kColsPerWarp, "column split");
+  static_assert((kColsPerWarp / 16) % kLdBatch == 0, "whole load batches");
+  static_assert(!kRegRealloc || (kEpiWarps % 4 == 0 && kThreads == (kEpiWarps + 4) * 32),
+                "register reallocation needs whole warpgroups");
 };
 
 // Where epilogue warp w works: lane quarter, batch rows, weight columns.
@@ -201,9 +251,12 @@ __device__ __forceinline__ int active_epilogue_rank(int w, int M, int block_n) {
   return n;
 }
 
+// mbarriers (ring full/empty, accumulator full/empty, drain, test hook, two
+// for the split reduction), then the TMEM address slot, the CTA abort flag
+// and the two-int mailbox of the split reduction.
 struct SmemBarriers {
   static __host__ __device__ constexpr uint32_t bytes(int stages, int bufs) {
-    return static_cast<uint32_t>((2 * stages + 2 * bufs + 2) * 8 + 16);
+    return static_cast<uint32_t>((2 * stages + 2 * bufs + 4) * 8 + 16);
   }
 };
 
@@ -250,6 +303,19 @@ __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float (
   }
 }
 
+// Stores `ncols` (a multiple of 4) fp32 partials of row m < M8 of a blocked
+// workspace slab (layout: see ws_blocked_offset): 16 bytes per 4 columns.
+__device__ __forceinline__ size_t ws_blocked_offset(int m, int n, int N);
+template <int COLS>
+__device__ __forceinline__ void store_row_f32_blocked(float* slab, int m, int n0, int N, const float (&v)[COLS],
+                                                      int ncols) {
+#pragma unroll
+  for (int j = 0; j < COLS; j += 4)
+    if (j < ncols)
+      __stcg(reinterpret_cast<float4*>(slab + ws_blocked_offset(m, n0 + j, N)),
+             make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+}
+
 // Stores `ncols` fp32 partials of one row to the split workspace (L2 only).
 template <int COLS>
 __device__ __forceinline__ void store_row_f32(float* dst, const float (&v)[COLS], int ncols, bool aligned) {
@@ -261,6 +327,327 @@ __device__ __forceinline__ void store_row_f32(float* dst, const float (&v)[COLS]
 #pragma unroll
     for (int j = 0; j < COLS; ++j)
       if (j < ncols) __stcg(dst + j, v[j]);
+  }
+}
+
+// ------------------------------------------------------ split workspace ----
+// Slab layout (M x N floats per slab, the reference's workspace size).  When
+// N % 4 == 0 and the workspace is 16-byte aligned ("blocked"), rows
+// [0, M8), M8 = M rounded down to a multiple of 8, are stored as
+// [M8/8][N/4][8][4]: the 8 rows x 4 columns of one (row block, column group)
+// are 128 contiguous bytes -- the 8 lanes of a warp that hold one row block
+// store one full line per float4 store, and one row block of one tile is
+// bn*32 contiguous bytes for a single bulk copy.  Rows [M8, M), and every row
+// when not blocked, are row-major.
+__device__ __forceinline__ size_t ws_blocked_offset(int m, int n, int N) {   // m < M8, n % 4 == 0
+  return ((static_cast<size_t>(m >> 3) * static_cast<size_t>(N >> 2) + static_cast<size_t>(n >> 2)) * 8u +
+          static_cast<size_t>(m & 7)) * 4u;
+}
+
+// The reduction of one split tile walks "row blocks": 8-row blocks of the
+// blocked rows, then single rows.  Chunks are contiguous runs of row blocks:
+// one per contributor at most, and at least 32 KiB of slab data each (a
+// smaller chunk costs more in claim round trips than it saves).  Every CTA
+// computes the same count.
+struct SplitGeometry {
+  int M;
+  int m8;         // rows in 8-row blocks
+  int nb;         // row blocks of a tile
+  __device__ __forceinline__ SplitGeometry(int M_, bool blocked) : M(M_) {
+    m8 = blocked ? (M & ~7) : 0;
+    nb = m8 / 8 + (M - m8);
+  }
+  __device__ __forceinline__ int chunks(int contributors, int bn_t) const {
+    const long long bytes = static_cast<long long>(contributors) * M * bn_t * 4;
+    const int by_size = static_cast<int>(bytes / 32768);
+    return max(1, min(min(contributors, nb), by_size));
+  }
+};
+
+// Sums slabs 0, 1, ..., n_c-1 -- in that order, whoever runs it, so results
+// are bit-identical run to run -- of row blocks [b0, b1) of `tile` and stores
+// bf16.  Bulk path: the leader copies all slabs of one row block into half
+// of the (now idle) smem ring with cp.async.bulk while the CTA sums the
+// previous block from the other half.  Plain path (unaligned pointers, or a
+// block whose slabs do not fit half the ring): cached loads from L2.
+// Returns false if a copy did not land in time (status set, copies drained).
+template <int GROUPS>
+__device__ __noinline__ bool reduce_row_blocks(const KernelParams& p, int tile, int n_c, int b0, int b1,
+                                               bool blocked, bool out_vec, bool allow_bulk, uint8_t* ring,
+                                               uint32_t ring_bytes,
+                                               uint64_t* red_bar, uint32_t& red_phase, bool leader, int tid,
+                                               int nthreads, volatile int* mailbox, volatile int* abort_flag) {
+  using namespace sm100;
+  const int N = p.N;
+  const int bn = p.block_n;
+  const int bn_t = min(bn, N - tile * bn);
+  const int col0 = tile * bn;
+  const SplitGeometry geo(p.M, blocked);
+  const size_t slab_stride = static_cast<size_t>(p.M) * N;
+  const uint32_t half = (ring_bytes / 2u) & ~127u;
+  // Bulk copies pay off for blocked row blocks of at least 32 KiB over all
+  // slabs (below that, plain loads have the lower latency) and need all
+  // slabs of the largest piece, a blocked row block of bn_t * 32 bytes, to fit
+  // half the ring.
+  const uint32_t block_bytes = static_cast<uint32_t>(n_c) * static_cast<uint32_t>(bn_t) * 32u;
+  const bool bulk = allow_bulk && blocked && geo.m8 > 0 && block_bytes >= 32768u && block_bytes <= half;
+  __nv_bfloat16* out = p.output;
+
+  auto piece = [&](int b, int s, uint32_t& bytes) -> const float* {
+    const float* slab = p.ws + static_cast<size_t>(s) * slab_stride;
+    if (b < geo.m8 / 8) {
+      bytes = static_cast<uint32_t>(bn_t) * 32u;
+      return slab + ws_blocked_offset(8 * b, col0, N);
+    }
+    const int m = geo.m8 + (b - geo.m8 / 8);
+    bytes = static_cast<uint32_t>(bn_t) * 4u;
+    return slab + static_cast<size_t>(m) * N + col0;
+  };
+  // Output of one float4 unit: row m, columns c .. c+3 of the tile.
+  auto emit4 = [&](int m, int c, const float4& v) {
+    __nv_bfloat16* dst = out + static_cast<size_t>(m) * N + col0 + c;
+    if (out_vec) {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y);
+      __nv_bfloat162 hi = __floats2bfloat162_rn(v.z, v.w);
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&lo);
+      pk.y = *reinterpret_cast<uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(dst) = pk;
+    } else {
+      dst[0] = __float2bfloat16_rn(v.x);
+      dst[1] = __float2bfloat16_rn(v.y);
+      dst[2] = __float2bfloat16_rn(v.z);
+      dst[3] = __float2bfloat16_rn(v.w);
+    }
+  };
+
+  if (bulk) {
+    const uint64_t pol = policy_evict_first();
+    auto issue = [&](int b, int buf) {
+      uint32_t bytes = 0;
+      piece(b, 0, bytes);
+      uint8_t* dst = ring + buf * half;
+      mbar_arrive_expect_tx(&red_bar[buf], bytes * static_cast<uint32_t>(n_c));
+      for (int s = 0; s < n_c; ++s) {
+        uint32_t pb = 0;
+        const float* src = piece(b, s, pb);
+        bulk_load(dst + static_cast<size_t>(s) * pb, src, pb, &red_bar[buf], pol);
+      }
+    };
+    bool ok = true;
+    bool inflight[2] = {false, false};
+    if (leader) {
+      fence_proxy_async_global();   // slabs acquired from other CTAs -> bulk copies
+      issue(b0, 0);
+    }
+    inflight[0] = true;
+    for (int b = b0, k = 0; b < b1; ++b, ++k) {
+      const int buf = k & 1;
+      if (b + 1 < b1) {
+        if (leader) issue(b + 1, buf ^ 1);
+        inflight[buf ^ 1] = true;
+      }
+      // The leader waits (bounded) and shares the outcome, so every thread
+      // takes the same path through the barriers below; then each thread
+      // observes the completed phase itself.
+      if (leader)
+        mailbox[0] = mbar_wait_bounded(&red_bar[buf], (red_phase >> buf) & 1u, abort_flag, p.status,
+                                       kErrReduceWait, p.timeout_ns) ? 1 : 0;
+      named_barrier_sync(1, static_cast<uint32_t>(nthreads));
+      const bool landed = mailbox[0] != 0;
+      named_barrier_sync(1, static_cast<uint32_t>(nthreads));
+      if (!landed) {
+        ok = false;
+        break;
+      }
+      mbar_try_wait(&red_bar[buf], (red_phase >> buf) & 1u);
+      red_phase ^= 1u << buf;
+      inflight[buf] = false;
+      uint32_t pb = 0;
+      piece(b, 0, pb);
+      const float4* src = reinterpret_cast<const float4*>(ring + buf * half);
+      const int units = static_cast<int>(pb / 16u);
+      const int stride4 = units;    // float4s per slab piece
+      for (int u = tid; u < units; u += nthreads) {
+        float4 tot = src[u];
+        for (int s = 1; s < n_c; ++s) {
+          const float4 v = src[s * stride4 + u];
+          tot.x += v.x;
+          tot.y += v.y;
+          tot.z += v.z;
+          tot.w += v.w;
+        }
+        if (b < geo.m8 / 8) emit4(8 * b + (u & 7), 4 * (u >> 3), tot);   // [col group][8 rows][4]
+        else emit4(geo.m8 + (b - geo.m8 / 8), 4 * u, tot);
+      }
+      named_barrier_sync(1, static_cast<uint32_t>(nthreads));   // buffer free for block b+2
+    }
+    if (!ok) {
+      // Copies still landing in smem must finish before the CTA moves on.
+      for (int buf = 0; buf < 2; ++buf)
+        if (inflight[buf]) {
+          wait_for_completion(&red_bar[buf], (red_phase >> buf) & 1u, p.timeout_ns);
+          red_phase ^= 1u << buf;
+        }
+      named_barrier_sync(1, static_cast<uint32_t>(nthreads));
+    }
+    return ok;
+  }
+
+  // Plain path: one flat run of units over the chunk's row blocks, so that
+  // GROUPS units x 8 slabs of loads stay in flight per thread whatever the
+  // row count.  A unit is 4 columns of one row (1 column when the workspace
+  // is row-major with N % 4 != 0 or unaligned).
+  const bool vec4 = blocked || ((N & 3) == 0 && (reinterpret_cast<uintptr_t>(p.ws) & 15u) == 0);
+  const int nb8 = geo.m8 / 8;
+  const int ub = bn_t * 2;                     // units of a blocked row block (8 rows x bn_t / 4)
+  const int ut = vec4 ? bn_t / 4 : bn_t;       // units of a row-major row
+  auto before = [&](int b) { return min(b, nb8) * ub + max(0, b - nb8) * ut; };
+  const int g_end = before(b1);
+  for (int g0 = before(b0) + tid; g0 < g_end; g0 += GROUPS * nthreads) {
+    size_t off[GROUPS];
+    int orow[GROUPS];
+    int ocol[GROUPS];
+#pragma unroll
+    for (int q = 0; q < GROUPS; ++q) {
+      const int g = min(g0 + q * nthreads, g_end - 1);
+      if (g < nb8 * ub) {
+        const int b = g / ub;
+        const int u = g - b * ub;
+        off[q] = ws_blocked_offset(8 * b, col0, N) + static_cast<size_t>(u) * 4u;
+        orow[q] = 8 * b + (u & 7);
+        ocol[q] = 4 * (u >> 3);
+      } else {
+        const int gg = g - nb8 * ub;
+        const int r = gg / ut;
+        const int u = gg - r * ut;
+        orow[q] = geo.m8 + r;
+        ocol[q] = vec4 ? 4 * u : u;
+        off[q] = static_cast<size_t>(orow[q]) * N + col0 + ocol[q];
+      }
+    }
+    float4 tot[GROUPS];
+    for (int s0 = 0; s0 < n_c; s0 += 8) {
+      float4 v[GROUPS][8];
+#pragma unroll
+      for (int q = 0; q < GROUPS; ++q)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[q][j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          if (s0 + j < n_c) {
+            const float* src = p.ws + static_cast<size_t>(s0 + j) * slab_stride + off[q];
+            if (vec4) v[q][j] = __ldcg(reinterpret_cast<const float4*>(src));
+            else v[q][j].x = __ldcg(src);
+          }
+        }
+#pragma unroll
+      for (int q = 0; q < GROUPS; ++q)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (s0 + j >= n_c) continue;
+          if (s0 + j == 0) {
+            tot[q] = v[q][j];
+          } else {
+            tot[q].x += v[q][j].x;
+            tot[q].y += v[q][j].y;
+            tot[q].z += v[q][j].z;
+            tot[q].w += v[q][j].w;
+          }
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < GROUPS; ++q) {
+      if (g0 + q * nthreads >= g_end) continue;
+      if (vec4) emit4(orow[q], ocol[q], tot[q]);
+      else out[static_cast<size_t>(orow[q]) * N + col0 + ocol[q]] = __float2bfloat16_rn(tot[q].x);
+    }
+  }
+  return true;
+}
+
+// Reduction of this CTA's split tiles of more than one chunk (at most two:
+// its first and last segments), run by the active epilogue threads after
+// their last segment.
+// The leader polls each tile's state word; once every contributor has
+// arrived it claims a chunk by compare-and-swap (a claim can never land after
+// the word is reset), the CTA reduces it, and the leader counts it finished;
+// whoever finishes the tile's last chunk resets the word to zero.  With
+// kFlagCoopReduce every contributor helps and waits at most kHelpWaitNs for
+// the others; otherwise only the last arriver (bit set in `completed`)
+// reduces, and never waits.  An arrival
+// count of zero means the tile is already reduced and reset.
+template <int GROUPS>
+__device__ __noinline__ void reduce_split_tiles(const KernelParams& p, const int (&tiles)[2], const int (&contrib)[2],
+                                                int n_split, int completed, bool leader, int tid, int nthreads,
+                                                bool blocked, bool out_vec, uint8_t* ring, uint32_t ring_bytes,
+                                                uint64_t* red_bar, volatile int* mailbox, volatile int* abort_flag) {
+  using namespace sm100;
+  const bool coop = (p.flags & kFlagCoopReduce) != 0;
+  const SplitGeometry geo(p.M, blocked);
+  auto tile_chunks = [&](int i) { return geo.chunks(contrib[i], min(p.block_n, p.N - tiles[i] * p.block_n)); };
+  const int pending_init = coop ? ((1 << n_split) - 1) : completed;
+  int pending = pending_init;   // meaningful on the leader only
+  uint32_t red_phase = 0;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    if (leader) {
+      int action = -1;   // (split index << 16) | chunk
+      for (int i = 0; i < n_split && action < 0; ++i) {
+        if (!(pending & (1 << i))) continue;
+        const int tile = tiles[i];
+        const int n_c = contrib[i];
+        const int R = tile_chunks(i);
+        int s = load_acquire_gpu(p.sem + tile);
+        while (true) {
+          const int arrived = s & kArrivalMask;
+          if (arrived == 0) {                 // reduced and reset already
+            pending &= ~(1 << i);
+            break;
+          }
+          if (arrived != n_c) break;          // a contributor is still running
+          const int claimed = (s >> kClaimShift) & kCountMask;
+          if (claimed >= R) {                 // every chunk taken
+            pending &= ~(1 << i);
+            break;
+          }
+          const int prev = atomic_cas_acq_rel_gpu(p.sem + tile, s, s + (1 << kClaimShift));
+          if (prev == s) {
+            action = (i << 16) | claimed;
+            break;
+          }
+          s = prev;
+        }
+      }
+      if (action < 0 && pending != 0 && (*abort_flag != 0 || global_timer_ns() - start > kHelpWaitNs))
+        pending = 0;
+      mailbox[0] = action;
+      mailbox[1] = pending;
+    }
+    named_barrier_sync(1, static_cast<uint32_t>(nthreads));
+    const int action = mailbox[0];
+    const int more = mailbox[1];
+    named_barrier_sync(1, static_cast<uint32_t>(nthreads));   // all have read it
+    if (action >= 0) {
+      const int i = action >> 16;
+      const int chunk = action & 0xffff;
+      const int tile = tiles[i];
+      const int n_c = contrib[i];
+      const int R = tile_chunks(i);
+      const int b0 = static_cast<int>(static_cast<long long>(geo.nb) * chunk / R);
+      const int b1 = static_cast<int>(static_cast<long long>(geo.nb) * (chunk + 1) / R);
+      const bool ok = reduce_row_blocks<GROUPS>(p, tile, n_c, b0, b1, blocked, out_vec, true, ring, ring_bytes,
+                                                red_bar, red_phase, leader, tid, nthreads, mailbox, abort_flag);
+      if (!ok) break;
+      named_barrier_sync(1, static_cast<uint32_t>(nthreads));
+      if (leader) {
+        const int prev = atomic_add_acq_rel_gpu(p.sem + tile, 1 << kDoneShift);
+        if (((prev >> kDoneShift) & kCountMask) == R - 1) store_relaxed_gpu(p.sem + tile, 0);
+      }
+    } else if (more == 0) {
+      break;
+    } else if (leader) {
+      __nanosleep(200);
+    }
   }
 }
 
@@ -300,9 +687,10 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   uint64_t* accum_empty = accum_full + Tr::kNumBufs; // [bufs]   epilogue -> MMA
   uint64_t* drain_bar = accum_empty + Tr::kNumBufs;  // MMA drain after abort
   uint64_t* never_bar = drain_bar + 1;               // test hook: nobody arrives
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(never_bar + 1);
+  uint64_t* red_bar = never_bar + 1;                 // [2] split reduction bulk copies
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* ticket_flag = abort_flag + 1;
+  volatile int* red_mailbox = abort_flag + 1;   // [2]
 
   if (warp == Tr::kProducerWarp && lane == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -315,8 +703,9 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
     }
     mbar_init(drain_bar, 1);
     mbar_init(never_bar, 1);
+    mbar_init(&red_bar[0], 1);
+    mbar_init(&red_bar[1], 1);
     *abort_flag = 0;
-    *ticket_flag = 0;
     fence_barrier_init();
   }
   if (warp == Tr::kMmaWarp) {
@@ -328,6 +717,13 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // With register reallocation the control warpgroup (producer, MMA, two
+  // idle warps) gives registers to the epilogue warpgroups: each warpgroup
+  // runs its setmaxnreg once, at the top of its branch, so the code below it
+  // is compiled for the new budget.  The host checks that the launch's
+  // register pool covers the split before it launches.
+  if (warp >= static_cast<uint32_t>(Tr::kEpiWarps)) {
+  if constexpr (Tr::kRegRealloc) regs_decrease<kCtrlRegs>();
   if (warp == Tr::kProducerWarp) {
     // ======================================================== PRODUCER ====
     if (lane == 0) {
@@ -455,8 +851,10 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
       }
     }
     __syncwarp();
+  }
   } else {
     // ======================================================== EPILOGUE ====
+    if constexpr (Tr::kRegRealloc) regs_increase<kEpiRegs>();
     const int M = p.M;
     const int N = p.N;
     const int KB = p.num_kb;
@@ -480,6 +878,18 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
       // first emit).
       bool waited = !(p.flags & kFlagIndependentInputs);
       if (waited) griddep_wait();
+
+      // 16-byte output and workspace rows need N and the base pointers aligned.
+      const bool out_vec = (N & 7) == 0 && (reinterpret_cast<uintptr_t>(p.output) & 15u) == 0;
+      const bool ws_vec = (N & 3) == 0 && (reinterpret_cast<uintptr_t>(p.ws) & 15u) == 0;
+      const int m8 = ws_vec ? (M & ~7) : 0;   // workspace rows stored in 8-row blocks
+      // Split tiles this CTA contributed to (only its first and last segments
+      // can be split); `completed` (leader only): bit i set when this CTA's
+      // arrival was the tile's last.
+      int split_tile[2] = {0, 0};
+      int split_contrib[2] = {0, 0};
+      int n_split = 0;
+      int completed = 0;
 
       int acc = 0;
       long long u = u_begin;
@@ -522,18 +932,28 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
             ready = __shfl_sync(0xffffffffu, ready, 0);
             if (!ready) continue;
             tc_fence_after();
+            // kLdBatch 16-column loads in flight per wait.  Columns past the
+            // tile width are folded too (they lie inside the 256-column
+            // buffer) and never stored.  An 8-column run starts on a multiple
+            // of 8 of the output, as does every 128-row scale group, so one
+            // scale covers the run; each pair is one packed fma.
+            const uint32_t t_row = tmem_base + lane_addr + static_cast<uint32_t>(buf * Tr::kBnMax + col0);
 #pragma unroll
-            for (int ch = 0; ch < Tr::kColsPerWarp / 16; ++ch) {
-              const int c_first = col0 + ch * 16;
-              if (c_first < bn) {   // warp-uniform
-                uint32_t raw[16];
-                tmem_ld_x16(tmem_base + lane_addr + static_cast<uint32_t>(buf * Tr::kBnMax + c_first), raw);
-                tmem_wait_ld();
+            for (int b = 0; b < Tr::kColsPerWarp / 16; b += Tr::kLdBatch) {
+              uint32_t raw[Tr::kLdBatch][16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  const int jj = ch * 16 + j;
-                  const float c = jj < split ? c_lo : c_hi;
-                  partial[jj] = fmaf(c, __uint_as_float(raw[j]), partial[jj]);
+              for (int q = 0; q < Tr::kLdBatch; ++q) tmem_ld_x16(t_row + static_cast<uint32_t>((b + q) * 16), raw[q]);
+              tmem_wait_ld();
+#pragma unroll
+              for (int q = 0; q < Tr::kLdBatch; ++q) {
+#pragma unroll
+                for (int h = 0; h < 16; h += 8) {
+                  const int c8 = (b + q) * 16 + h;
+                  const float c = c8 < split ? c_lo : c_hi;
+#pragma unroll
+                  for (int j = 0; j < 8; j += 2)
+                    ffma2(partial[c8 + j], partial[c8 + j + 1], c, __uint_as_float(raw[q][h + j]),
+                          __uint_as_float(raw[q][h + j + 1]));
                 }
               }
             }
@@ -555,74 +975,69 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         if (contributors == 1) {
           if (row_ok && *abort_flag == 0)
             store_row_bf16<Tr::kColsPerWarp>(p.output + static_cast<size_t>(m) * N + n0, partial, ncols,
-                                             (N & 7) == 0);
+                                             out_vec);
         } else {
           const int slab = static_cast<int>(cta - c_first);
           const size_t slab_stride = static_cast<size_t>(M) * N;
-          if (row_ok)
-            store_row_f32<Tr::kColsPerWarp>(p.ws + slab * slab_stride + static_cast<size_t>(m) * N + n0,
-                                            partial, ncols, (N & 3) == 0);
-          // Ticket: the CTA barrier orders every thread's workspace stores
-          // before the leader's acquire-release increment (cumulative at GPU
-          // scope), and the last arriver's increment acquires all earlier
-          // contributors' stores; the second barrier hands that to the CTA.
-          named_barrier_sync(1, epi_threads);
-          if (leader) {
-            int last = 0;
-            if (*abort_flag == 0) {
-              const int previous = atomic_add_acq_rel_gpu(p.sem + tile, 1);
-              last = (previous == contributors - 1) ? 1 : 0;
-            }
-            *ticket_flag = last;
+          if (row_ok) {
+            float* slab_base = p.ws + slab * slab_stride;
+            if (ws_vec && m < m8)
+              store_row_f32_blocked<Tr::kColsPerWarp>(slab_base, m, n0, N, partial, ncols);
+            else
+              store_row_f32<Tr::kColsPerWarp>(slab_base + static_cast<size_t>(m) * N + n0, partial, ncols, ws_vec);
           }
+          // Arrival: the CTA barrier orders every thread's workspace stores
+          // before the leader's acquire-release increment (cumulative at GPU
+          // scope); whoever later sees every arrival acquires them all.
           named_barrier_sync(1, epi_threads);
-          if (*ticket_flag != 0) {
-            // The tile's M x BN outputs are spread over all active epilogue
-            // threads (consecutive threads -> consecutive columns, coalesced),
-            // four elements per thread per pass with every slab load of the
-            // pass in flight together; each element is summed over the slabs
-            // in slab order 0, 1, ..., contributors-1 whatever the arrival
-            // order, so the result is bit-identical run to run.
-            const int bn_t = min(bn, N - tile * bn);
-            const int total_el = M * bn_t;
-            const int T = static_cast<int>(epi_threads);
-            const float* base = p.ws + static_cast<size_t>(tile) * bn;
-            __nv_bfloat16* obase = p.output + static_cast<size_t>(tile) * bn;
-            for (int e0 = active_tid; e0 < total_el; e0 += 4 * T) {
-              size_t off[4];
-              bool ok_e[4];
-              float total[4];
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const int e = e0 + q * T;
-                ok_e[q] = e < total_el;
-                const int ee = ok_e[q] ? e : e0;
-                const int mm = ee / bn_t;
-                off[q] = static_cast<size_t>(mm) * N + (ee - mm * bn_t);
-                total[q] = 0.0f;
-              }
-              for (int s0 = 0; s0 < contributors; s0 += 8) {
-                float v[4][8];
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
-#pragma unroll
-                  for (int j = 0; j < 8; ++j)
-                    v[q][j] = (s0 + j) < contributors ? __ldcg(base + (s0 + j) * slab_stride + off[q]) : 0.0f;
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
-#pragma unroll
-                  for (int j = 0; j < 8; ++j)
-                    if ((s0 + j) < contributors) total[q] = (s0 + j) == 0 ? v[q][j] : total[q] + v[q][j];
-              }
-#pragma unroll
-              for (int q = 0; q < 4; ++q)
-                if (ok_e[q]) obase[off[q]] = __float2bfloat16_rn(total[q]);
+          int last = 0;
+          if (leader && *abort_flag == 0) {
+            const int previous = atomic_add_acq_rel_gpu(p.sem + tile, 1);
+            last = (previous & kArrivalMask) == contributors - 1 ? 1 : 0;
+          }
+          const int bn_t = min(bn, N - tile * bn);
+          if (SplitGeometry(M, ws_vec).chunks(contributors, bn_t) == 1) {
+            // One chunk: the last arriver reduces it at once (plain loads,
+            // the smem ring is still streaming) and resets the word.
+            if (leader) red_mailbox[0] = last;
+            named_barrier_sync(1, epi_threads);
+            last = red_mailbox[0];
+            named_barrier_sync(1, epi_threads);
+            if (last) {
+              uint32_t no_phase = 0;
+              reduce_row_blocks<Tr::kRedGroups>(p, tile, contributors, 0, SplitGeometry(M, ws_vec).nb, ws_vec,
+                                                out_vec, false, smem, 0, red_bar, no_phase, leader, active_tid,
+                                                static_cast<int>(epi_threads), red_mailbox, abort_flag);
+              named_barrier_sync(1, epi_threads);
+              if (leader) store_relaxed_gpu(p.sem + tile, 0);
             }
-            if (leader) store_relaxed_gpu(p.sem + tile, 0);
+          } else {
+            if (last) completed |= 1 << n_split;
+            split_tile[n_split] = tile;
+            split_contrib[n_split] = contributors;
+            ++n_split;
           }
         }
         u = seg_end;
       }
+      // ----------------------------------------------- split reduction ----
+      // Only a CTA with reduction work enters the (cold) reduction code: any
+      // recorded tile (all have more than one chunk) under kFlagCoopReduce,
+      // else a tile this CTA completed.
+      bool red_work = false;
+      if (n_split > 0) {
+        red_work = (p.flags & kFlagCoopReduce) != 0;
+        if (!red_work) {
+          if (leader) red_mailbox[0] = completed;
+          named_barrier_sync(1, epi_threads);
+          red_work = red_mailbox[0] != 0;
+          named_barrier_sync(1, epi_threads);
+        }
+      }
+      if (red_work)
+        reduce_split_tiles<Tr::kRedGroups>(p, split_tile, split_contrib, n_split, completed, leader,
+                                           active_tid, static_cast<int>(epi_threads), ws_vec, out_vec, smem,
+                                           p.w_region_bytes + p.a_region_bytes, red_bar, red_mailbox, abort_flag);
     }
   }
 
@@ -633,13 +1048,13 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   if (warp == Tr::kMmaWarp) tmem_dealloc(tmem_base, Tr::kTmemCols);
 }
 
-template <int MMA_M, int EPW>
-__global__ void __launch_bounds__(KernelTraits<MMA_M, EPW>::kThreads, 1)
+template <int MMA_M, int COPIES, int EPW>
+__global__ void __launch_bounds__(KernelTraits<MMA_M, COPIES, EPW>::kThreads, 1)
     dg_decode_gemm_kernel(const __grid_constant__ KernelParams p,
                           const __grid_constant__ CUtensorMap w_map,
                           const __grid_constant__ CUtensorMap a_map) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
-  decode_gemm_body<KernelTraits<MMA_M, EPW>>(p, &w_map, &a_map);
+  decode_gemm_body<KernelTraits<MMA_M, COPIES, EPW>>(p, &w_map, &a_map);
 #else
   if (threadIdx.x == 0 && p.status != nullptr) atomicCAS(p.status, 0, kErrBadLaunchShape);
 #endif

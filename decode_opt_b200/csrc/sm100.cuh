@@ -262,9 +262,56 @@ __device__ __forceinline__ void store_relaxed_gpu(int* addr, int v) {
   asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
 }
 
+// Orders this thread's earlier generic-proxy view of global memory (e.g.
+// data acquired from other CTAs) before its later bulk copies (async proxy).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__device__ __forceinline__ int load_acquire_gpu(const int* addr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// Compare-and-swap with acquire-release semantics at GPU scope; returns the
+// value found.
+__device__ __forceinline__ int atomic_cas_acq_rel_gpu(int* addr, int expected, int desired) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.cas.b32 %0, [%1], %2, %3;"
+               : "=r"(old)
+               : "l"(addr), "r"(expected), "r"(desired)
+               : "memory");
+  return old;
+}
+
 // ------------------------------------------------------------ named barrier --
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ------------------------------------------------------------- packed fp32 --
+// (d0, d1) = fma(a, (b0, b1), (d0, d1)): one fma.rn.f32x2, each lane rounded
+// exactly as a scalar fmaf.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a, float b0, float b1) {
+  uint64_t acc = (static_cast<uint64_t>(__float_as_uint(d1)) << 32) | __float_as_uint(d0);
+  asm("{\n\t.reg .b64 sa, sb;\n\tmov.b64 sa, {%1, %1};\n\tmov.b64 sb, {%2, %3};\n\t"
+      "fma.rn.f32x2 %0, sa, sb, %0;\n\t}"
+      : "+l"(acc)
+      : "f"(a), "f"(b0), "f"(b1));
+  d0 = __uint_as_float(static_cast<uint32_t>(acc));
+  d1 = __uint_as_float(static_cast<uint32_t>(acc >> 32));
+}
+
+// ----------------------------------------------------- register reallocation --
+// Warpgroup-wide change of the per-thread register allocation.
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_increase() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_decrease() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
 }
 
 }  // namespace sm100

@@ -74,11 +74,13 @@ extern "C" {
 #define DG_ERR_DRAIN_MMA 0x42
 #define DG_ERR_INJECTED_TIMEOUT 0x51
 #define DG_ERR_BAD_LAUNCH_SHAPE 0x61
+#define DG_ERR_REDUCE_WAIT 0x71
 
 /* Runtime configuration.  Zero-initialise, then set fields. */
 typedef struct dg_config {
   int m_tile;    /* bound on M: 8, 16, 32, 64 or 128 (reference M_TILE); the batch is
-                    the MMA's M side, padded to 64 (m_tile <= 64) or 128              */
+                    the MMA's M side: 64 rows holding 4 copies of M <= 16, else 128
+                    rows holding 4, 2 or 1 copies (M <= 32, 64, 128)                 */
   int block_n;   /* weight rows (output columns) per tile = the MMA's N side:
                     multiple of 8 in [8,256] (reference OUTPUT_ROWS_PER_CTA, <= 64
                     there; 256 = 8 KiB of weights per tcgen05.mma, the B200 default) */
@@ -119,7 +121,7 @@ typedef struct dg_plan_info {
   int stages;
   int n_mma;                       /* MMA N = block_n rounded up to 16              */
   int a_rows;                      /* activation rows per TMA box = M rounded up to 8 */
-  int mma_m;                       /* MMA M = batch rows padded to 64 or 128        */
+  int mma_m;                       /* MMA M: 64 (M <= 16) or 128                    */
   int epi_warps;
   int num_ctas;
   int max_slabs;                   /* workspace slabs a split tile needs (1 = none) */

@@ -52,21 +52,24 @@ class DeviceCase:
             self.packed[key] = dg.prepack_weight(self.w, cfg.block_n, cfg.layout)
         return self.packed[key]
 
-    def run(self, cfg, clear_out: bool = True, stream=None):
-        """One launch through the C ABI; returns (rc, out as float32 numpy, status)."""
+    def run(self, cfg, clear_out: bool = True, stream=None, ws_offset: int = 0):
+        """One launch through the C ABI; returns (rc, out as float32 numpy, status).
+        ``ws_offset`` floats shift the split workspace off its 16-byte alignment."""
         import decode_opt_b200 as dg
         torch = self.torch
         plan = cfg.plan(self.m, self.n, self.k)
         assert plan.error is None, plan.error
-        if plan.ws_floats and (self.splitk_ws is None or self.splitk_ws.numel() < plan.ws_floats):
-            self.splitk_ws = torch.zeros(plan.ws_floats, dtype=torch.float32, device=self.w.device)
+        need = plan.ws_floats + ws_offset
+        if plan.ws_floats and (self.splitk_ws is None or self.splitk_ws.numel() < need):
+            self.splitk_ws = torch.zeros(need, dtype=torch.float32, device=self.w.device)
         if plan.sem_ints and (self.sem is None or self.sem.numel() < plan.sem_ints):
             self.sem = torch.zeros(plan.sem_ints, dtype=torch.int32, device=self.w.device)
         if clear_out:
             self.out.zero_()
         self.status.zero_()
+        ws = self.splitk_ws[ws_offset:] if (self.splitk_ws is not None and ws_offset) else self.splitk_ws
         p = dg.Problem(self.m, self.n, self.k, self.a, self.weight_for(cfg), self.ws, self.as_, self.out,
-                       self.splitk_ws, self.sem, self.status)
+                       ws, self.sem, self.status)
         rc = dg.launch(cfg, p, stream)
         torch.cuda.synchronize()
         got = self.out.float().cpu().numpy()

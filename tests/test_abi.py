@@ -80,8 +80,11 @@ def test_status_strings():
 def test_default_plan_c2(m):
     p = dg.default_config(m, 7168, 16384).plan(m, 7168, 16384)
     assert p.error is None
-    # weights on the MMA N side (256 rows per tile), batch on M (64 or 128)
-    assert p.mma_m == (64 if m <= 64 else 128) and p.n_mma == 256 and p.num_output_tiles == 28
+    # weights on the MMA N side (256 rows per tile), batch on M: 64 rows (4
+    # copies of 16) up to M = 16, else 128 rows holding 4, 2 or 1 copies
+    assert p.mma_m == (64 if m <= 16 else 128) and p.n_mma == 256 and p.num_output_tiles == 28
+    assert p.block[0] == {1: 192, 8: 192, 16: 192, 32: 192, 64: 320, 128: 384}[m]
+    assert p.epi_warps == {1: 4, 8: 4, 16: 4, 32: 4, 64: 8, 128: 8}[m]
     assert p.a_rows == -(-m // 8) * 8
     assert p.smem_bytes <= 227 * 1024
     assert p.grid[0] == 148 or p.grid[0] > 0

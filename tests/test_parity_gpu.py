@@ -231,6 +231,34 @@ def test_stream_k_bit_determinism(grid):
             assert np.array_equal(got.view(np.uint32), first.view(np.uint32))
 
 
+@pytest.mark.parametrize("m", [3, 9, 13, 37, 64, 100, 128])
+@pytest.mark.parametrize("ws_offset", [0, 1])
+def test_split_workspace_layouts(m, ws_offset):
+    """Split tiles through both workspace layouts: 8-row blocks plus row-major
+    tail rows (16-byte aligned workspace, bulk-copy reduction), and row-major
+    only with plain loads (workspace one float off alignment); with the grid
+    on one CTA per SM every contributor helps reduce.  Bit-identical across
+    runs, tickets clean."""
+    n, k = 2048, 4096
+    w, ws = oracle.gen_weight_smoke(n, k, 41)
+    a, as_ = oracle.gen_activation_smoke(m, k, 42 + m)
+    ref = oracle.compute_reference(a, as_, w, ws, threads=8)
+    dc = DeviceCase(w, ws, a, as_, n)
+    c = dg.default_config(m, n, k, layout=dg.LAYOUT_PACKED_SWIZZLED)
+    assert c.plan(m, n, k).max_slabs > 1
+    first = None
+    for _ in range(3):
+        rc, got, status = dc.run(c, ws_offset=ws_offset)
+        assert rc == 0 and status == 0, dg.status_string(status)
+        if first is None:
+            first = got
+            ok, rl2, worst = check_against_oracle(got, ref)
+            assert ok, (rl2, worst)
+        else:
+            assert np.array_equal(got.view(np.uint32), first.view(np.uint32))
+    assert dc.sem_clean()
+
+
 @pytest.mark.parametrize("n,k,m,bm", [(1, 128, 1, 128), (129, 256, 3, 128), (200, 384, 8, 48), (1000, 1152, 5, 64),
                                       (136, 4096, 1, 8), (777, 640, 17, 128), (96, 256, 128, 56)])
 @pytest.mark.parametrize("layout", [0, 1, 2])
