@@ -12,11 +12,13 @@ are larger than L2; no flush needed).  A step is one GEMM; K steps are timed
 with CUDA events on the launching stream, replayed from a CUDA graph, and
 with programmatic dependent launch between consecutive GEMMs.
 
-Multi-GPU (launched with torch.distributed.run, one rank per GPU): W is
-N-sharded tensor-parallel, each GPU streams N/g rows, and the BF16 output
-slices are all-gathered with NCCL every step (strong scaling: the whole job
-is one GEMM of the configured size; "gemm_only" reports it without the
-gather).  Timing is the max over ranks.
+Multi-GPU (launched with torch.distributed.run, one rank per GPU): the path
+partitions by weight rows with no exchange inside the GEMM, so the headline
+is weak scaling: every rank streams its own N x K shard of one
+tensor-parallel layer of g*N rows, value = all ranks' bytes / the max-over-
+ranks time.  Beside it: the same step with the NCCL all-gather of the BF16
+output slices, and the strong-scaling layer (the single N x K matrix
+N-sharded g ways, with and without the gather).
 
 Metric: algorithmic bytes (N*K + M*K + 2*M*N) per GEMM / time, GB/s, and
 us per GEMM.  `e2e` repeats the measurement through the public API with the
@@ -51,7 +53,7 @@ FALLBACK_HBM_GBS = 6650.0
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--m", type=int, default=1)
@@ -69,6 +71,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU work the rank-0 cpu_baseline sample is sized to")
     ap.add_argument("--graph-chunk", type=int, default=500, help="launches per captured CUDA graph")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the M = 1..128 sweep")
+    ap.add_argument("--no-cublas", action="store_true", help="skip the cuBLASLt FP8 baseline")
     return ap.parse_args()
 
 
@@ -88,7 +92,7 @@ def measured_peaks():
 
 def ncu_traffic(workload_key):
     """DRAM bytes per launch from the committed ncu summary (profiles/)."""
-    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
     try:
         with open(path) as f:
             return json.load(f).get(workload_key)
@@ -285,6 +289,60 @@ def reference_arm(args, rank, world):
 # B200 arm
 # ---------------------------------------------------------------------------
 
+class Rotation:
+    """One weight shard of n x k e4m3 in `layout`, rotated over enough
+    distinct device copies (>= max(1 GiB, 4 x L2)) that every launch reads
+    its weights cold from HBM, plus the problems and tensor maps for one
+    batch size."""
+
+    def __init__(self, qw, layout, block_n, dev):
+        import torch
+        import decode_opt_b200 as dg
+        self.n, self.k = qw.shape
+        base = qw if layout == dg.LAYOUT_RAW else dg.prepack_weight(qw, block_n, layout)
+        self.set_bytes = base.numel()
+        l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+        self.l2 = l2
+        self.nsets = max(5, math.ceil(max(1 << 30, 4 * l2) / self.set_bytes))
+        self.sets = [base] + [base.clone() for _ in range(self.nsets - 1)]
+
+
+class GemmSetup:
+    """Problems, maps and buffers for one (rotation, M, config)."""
+
+    def __init__(self, rot, cfg, m, qx, wscale, ascale, dev):
+        import torch
+        import decode_opt_b200 as dg
+        self.cfg = cfg
+        self.m = m
+        self.plan = cfg.plan(m, rot.n, rot.k)
+        if self.plan.error:
+            raise SystemExit(self.plan.error)
+        self.out = torch.empty((m, rot.n), dtype=torch.bfloat16, device=dev)
+        self.ws = torch.zeros(max(self.plan.ws_floats, 1), dtype=torch.float32, device=dev)
+        self.sem = torch.zeros(max(self.plan.sem_ints, 1), dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.probs = [dg.Problem(m, rot.n, rot.k, qx, w, wscale, ascale, self.out, self.ws, self.sem, self.status)
+                      for w in rot.sets]
+        self.wmaps = [dg.make_weight_tma(cfg, p) for p in self.probs]
+        self.amap = dg.make_activation_tma(cfg, self.probs[0])
+        self.nsets = rot.nsets
+
+    def launch(self, i, stream, cfg=None):
+        import decode_opt_b200 as dg
+        c = self.cfg if cfg is None else cfg
+        rc = dg.launch_with_maps(c, self.probs[i % self.nsets], self.wmaps[i % self.nsets], self.amap, stream,
+                                 pdl_attr=c.pdl)
+        if rc != 0:
+            raise RuntimeError(f"launch failed: cudaError {rc}")
+
+    def check_status(self):
+        import decode_opt_b200 as dg
+        st = int(self.status.item())
+        if st != 0:
+            raise RuntimeError(f"kernel status {dg.status_string(st)}")
+
+
 def b200_arm(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -294,172 +352,254 @@ def b200_arm(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     n, k, m = args.n, args.k, args.m
-    if n % (world * 128) != 0:
-        raise SystemExit(f"N={n} must split into {world} shards of a multiple of 128 rows")
-    n_loc = n // world
     layout = {"raw": dg.LAYOUT_RAW, "packed": dg.LAYOUT_PACKED, "swizzled": dg.LAYOUT_PACKED_SWIZZLED}[args.layout]
-    cfg_dep = dg.default_config(m, n_loc, k, layout=layout, pdl=not args.no_pdl)
-    cfg_ind = dg.default_config(m, n_loc, k, layout=layout, pdl=not args.no_pdl, independent_inputs=True)
-    cfg = cfg_ind if args.pdl_mode == "independent" else cfg_dep
-    cfg_other = cfg_dep if args.pdl_mode == "independent" else cfg_ind
-    plan = cfg.plan(m, n_loc, k)
-    if plan.error:
-        raise SystemExit(plan.error)
-
-    # ---- synthetic inputs (same on every rank; each keeps its W shard) -----
-    g = torch.Generator(device=dev).manual_seed(20260913)
-    w_full = torch.randn((n, k), device=dev, generator=g)
-    qw_full, sw = quantize_pertensor(w_full, torch.float8_e4m3fn)
-    del w_full
-    x = torch.randn((m, k), device=dev, generator=g)
-    qx, sx = quantize_pertensor(x, torch.float8_e4m3fn)
-    qw = qw_full[rank * n_loc:(rank + 1) * n_loc].contiguous()
-    del qw_full
-    kb = k // 128
-    wscale = torch.full(((n_loc + 127) // 128, kb), float(sw), device=dev)
-    ascale = torch.full((m, kb), float(sx), device=dev)
-    base = qw if layout == dg.LAYOUT_RAW else dg.prepack_weight(qw, cfg.block_n, layout)
-    set_bytes = base.numel()
-    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
-    nsets = max(5, math.ceil(max(1 << 30, 4 * l2) / set_bytes))
-    sets = [base] + [base.clone() for _ in range(nsets - 1)]
-    out = torch.empty((m, n_loc), dtype=torch.bfloat16, device=dev)
-    gathered = torch.empty((world * m, n_loc), dtype=torch.bfloat16, device=dev)
-    ws_buf = torch.zeros(max(plan.ws_floats, 1), dtype=torch.float32, device=dev)
-    sem = torch.zeros(max(plan.sem_ints, 1), dtype=torch.int32, device=dev)
-    status = torch.zeros(1, dtype=torch.int32, device=dev)
-    probs = [dg.Problem(m, n_loc, k, qx, s_, wscale, ascale, out, ws_buf, sem, status) for s_ in sets]
-    wmaps = [dg.make_weight_tma(cfg, p) for p in probs]
-    amap = dg.make_activation_tma(cfg, probs[0])
+    pdl = not args.no_pdl
+    independent = args.pdl_mode == "independent"
     stream = torch.cuda.Stream(device=dev)
     pg = dist.group.WORLD if world > 1 else None
 
-    def step(i, with_gather=True, c=None):
-        c = cfg if c is None else c
-        rc = dg.launch_with_maps(c, probs[i % nsets], wmaps[i % nsets], amap, stream, pdl_attr=c.pdl)
-        if rc != 0:
-            raise RuntimeError(f"launch failed: cudaError {rc}")
-        if world > 1 and with_gather:
-            dist.all_gather_into_tensor(gathered, out, group=pg)
+    def device_max(t):
+        if world > 1:
+            tt = torch.tensor([t], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            return float(tt.item())
+        return t
 
-    def capture(count, with_gather, c=None):
+    def capture(fn, count):
+        """CUDA graphs of `count` calls of fn(i) on `stream` (chunks of graph_chunk)."""
         graphs = []
         left = count
+        base = 0
         with torch.cuda.stream(stream):
             while left > 0:
                 chunk = min(left, args.graph_chunk)
                 gr = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(gr, stream=stream):
                     for i in range(chunk):
-                        step(i, with_gather, c)
+                        fn(base + i)
                 graphs.append(gr)
                 left -= chunk
+                base += chunk
         return graphs
 
-    def timed(graphs):
+    def timed(graphs, warm=True):
+        """Seconds for one replay of all graphs: barrier + synchronize on both
+        sides, CUDA events on the launching stream, max over ranks."""
+        if warm:
+            with torch.cuda.stream(stream):
+                graphs[0].replay()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        # Graph replays launch on the current stream: make it the stream the
-        # events are recorded on.
         with torch.cuda.stream(stream):
             e0.record(stream)
             for gr in graphs:
                 gr.replay()
             e1.record(stream)
         torch.cuda.synchronize(dev)
-        t = e0.elapsed_time(e1) / 1e3
+        t = device_max(e0.elapsed_time(e1) / 1e3)
         if world > 1:
-            tt = torch.tensor([t], device=dev)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            t = float(tt.item())
             dist.barrier()
         return t
 
-    # ---- warm-up (eager, then the captured graphs once) ----------------------
+    # ---- synthetic inputs: per-tensor-scaled N(0,1) e4m3 --------------------
+    # Weak scaling: every rank holds a full n x k shard of one tensor-parallel
+    # layer of world*n rows (rank r: rows [r*n, (r+1)*n)); the activation is
+    # shared.  Seeds make every rank's shard distinct and reproducible.
+    g = torch.Generator(device=dev).manual_seed(20260913 + 7919 * rank)
+    w_full = torch.randn((n, k), device=dev, generator=g)
+    qw, sw = quantize_pertensor(w_full, torch.float8_e4m3fn)
+    del w_full
+    gx = torch.Generator(device=dev).manual_seed(20260913)
+    x = torch.randn((128, k), device=dev, generator=gx)
+    kb = k // 128
+    wscale = torch.full(((n + 127) // 128, kb), float(sw), device=dev)
+
+    def act(mm):
+        q, s = quantize_pertensor(x[:mm], torch.float8_e4m3fn)
+        return q.contiguous(), torch.full((mm, kb), float(s), device=dev), float(s)
+
+    qx, ascale, sx = act(m)
+    cfg = dg.default_config(m, n, k, layout=layout, pdl=pdl, independent_inputs=independent)
+    cfg_other = dg.default_config(m, n, k, layout=layout, pdl=pdl, independent_inputs=not independent)
+    rot = Rotation(qw, layout, cfg.block_n, dev)
+    gs = GemmSetup(rot, cfg, m, qx, wscale, ascale, dev)
+    gathered = torch.empty((world * m, n), dtype=torch.bfloat16, device=dev)
+
+    def gemm_step(i):
+        gs.launch(i, stream)
+
+    def tp_step(i):
+        gs.launch(i, stream)
+        dist.all_gather_into_tensor(gathered, gs.out, group=pg)
+
+    K = args.steps
+    # ---- warm-up: eager launches, then every graph once (in timed()) ------------
     with torch.cuda.stream(stream):
         for i in range(max(args.warmup, 3)):
-            step(i)
+            gs.launch(i, stream)
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, gs.out, group=pg)
     torch.cuda.synchronize(dev)
-    graphs = capture(args.steps, with_gather=True)
-    graphs_gemm = capture(args.steps, with_gather=False) if world > 1 else graphs
-    for gr in graphs[:1]:
-        gr.replay()
-    torch.cuda.synchronize(dev)
-    if int(status.item()) != 0:
-        raise RuntimeError(f"kernel status {dg.status_string(int(status.item()))}")
+    gs.check_status()
 
+    graphs = capture(gemm_step, K)
     clocks = ClockSampler(local_rank)
     clocks.start()
     time.sleep(0.05)
-    clocks.mark()
-    t_total = timed(graphs)
-    clocks.mark()
-    t_gemm = timed(graphs_gemm) if world > 1 else t_total
-    clocks.stop()
-    # The other PDL mode, same loop (reported beside the headline).
-    graphs_other = capture(args.steps, with_gather=True, c=cfg_other)
-    for gr in graphs_other[:1]:
-        gr.replay()
-    t_other = timed(graphs_other)
-    del graphs_other
-    if int(status.item()) != 0:
-        raise RuntimeError(f"kernel status {dg.status_string(int(status.item()))}")
-    del graphs, graphs_gemm
+    with torch.cuda.stream(stream):
+        graphs[0].replay()
     torch.cuda.synchronize(dev)
+    clocks.mark()
+    t_gemm = timed(graphs, warm=False)
+    clocks.mark()
+    clocks.stop()
+    del graphs
+    gs.check_status()
+    graphs = capture(lambda i: gs.launch(i, stream, cfg_other), K)
+    t_other = timed(graphs)
+    del graphs
+    gs.check_status()
 
-    K = args.steps
-    byt_job = n * k + m * k + 2 * m * n                   # one GEMM, whole job
-    byt_gpu = n_loc * k + m * k + 2 * m * n_loc           # per GPU per launch
-    us_step = t_total / K * 1e6
+    byt_gpu = n * k + m * k + 2 * m * n             # one rank's GEMM per step
+    byt_job = world * byt_gpu
     us_gemm = t_gemm / K * 1e6
-    value = byt_job / (t_total / K) / 1e9
+    value = byt_job / (t_gemm / K) / 1e9
     peak, peak_kind = measured_peaks()
     achieved = byt_gpu / (t_gemm / K) / 1e9
-    workload_key = f"N{n_loc}_K{k}_M{m}_{args.layout}"
-    traffic = ncu_traffic(workload_key)
+    workload_key = f"N{n}_K{k}_M{m}_{args.layout}"
 
-    # ---- end to end through the public API with host buffers ---------------
+    # ---- multi-GPU: with the NCCL gather, and the strong-scaling layer ---------
+    tp = None
+    if world > 1:
+        graphs = capture(tp_step, K)
+        t_tp = timed(graphs)
+        del graphs
+        # Strong scaling (BASELINE config 5): the one n x k layer N-sharded over
+        # the ranks, each streaming n/world rows, then the gather.
+        n_s = n // world
+        strong = None
+        if n % world == 0 and n_s % 128 == 0:
+            q_s = qw[:n_s].contiguous()
+            cfg_s = dg.default_config(m, n_s, k, layout=layout, pdl=pdl, independent_inputs=independent)
+            rot_s = Rotation(q_s, layout, cfg_s.block_n, dev)
+            gs_s = GemmSetup(rot_s, cfg_s, m, qx, wscale[: n_s // 128].contiguous(), ascale, dev)
+            gathered_s = torch.empty((world * m, n_s), dtype=torch.bfloat16, device=dev)
+            graphs = capture(lambda i: gs_s.launch(i, stream), K)
+            t_s = timed(graphs)
+            del graphs
+
+            def strong_tp(i):
+                gs_s.launch(i, stream)
+                dist.all_gather_into_tensor(gathered_s, gs_s.out, group=pg)
+            graphs = capture(strong_tp, K)
+            t_s_tp = timed(graphs)
+            del graphs
+            gs_s.check_status()
+            byt_layer = n * k + m * k + 2 * m * n
+            strong = {"N_layer": n, "rows_per_gpu": n_s,
+                      "gemm_only": {"us_per_gemm": t_s / K * 1e6, "GBps_job": byt_layer / (t_s / K) / 1e9},
+                      "with_gather": {"us_per_step": t_s_tp / K * 1e6,
+                                      "GBps_job": byt_layer / (t_s_tp / K) / 1e9}}
+            del rot_s, gs_s
+        tp = {"with_gather": {"us_per_step": t_tp / K * 1e6, "GBps_job": byt_job / (t_tp / K) / 1e9,
+                              "collective": "NCCL all_gather_into_tensor of the bf16 [M, N/g] slices"},
+              "strong_scaling": strong}
+
+    # ---- end to end through the public API with host buffers ----------------
     e2e = None
     if not args.no_e2e:
         hx = torch.empty((m, k), dtype=torch.uint8).pin_memory()
-        hx.copy_(qx.cpu())
+        hx.copy_(qx.view(torch.uint8).cpu() if qx.dtype != torch.uint8 else qx.cpu())
         hs = torch.empty((m, kb), dtype=torch.float32).pin_memory()
         hs.copy_(ascale.cpu())
-        hy = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
-        e2e_steps = K
+        hy = torch.empty((m, world * n), dtype=torch.bfloat16).pin_memory()
+        qx_u8 = qx.view(torch.uint8)
+
+        def e2e_step(i):
+            qx_u8.copy_(hx, non_blocking=True)
+            ascale.copy_(hs, non_blocking=True)
+            gs.launch(i, stream)
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, gs.out, group=pg)
+                hy.copy_(gathered.view(world, m, n).permute(1, 0, 2).reshape(m, world * n), non_blocking=True)
+            else:
+                hy.copy_(gs.out, non_blocking=True)
+
         with torch.cuda.stream(stream):
-            def e2e_step(i):
-                qx.copy_(hx, non_blocking=True)
-                ascale.copy_(hs, non_blocking=True)
-                step(i)
-                if world > 1:
-                    hy.copy_(gathered.view(world, m, n_loc).permute(1, 0, 2).reshape(m, n), non_blocking=True)
-                else:
-                    hy.copy_(out, non_blocking=True)
             for i in range(3):
                 e2e_step(i)
-            torch.cuda.synchronize(dev)
-            if world > 1:
-                dist.barrier()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
             e0.record(stream)
-            for i in range(e2e_steps):
+            for i in range(K):
                 e2e_step(i)
             e1.record(stream)
         torch.cuda.synchronize(dev)
-        te = e0.elapsed_time(e1) / 1e3
-        if world > 1:
-            tt = torch.tensor([te], device=dev)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            te = float(tt.item())
-        e2e = {"value": byt_job / (te / e2e_steps) / 1e9, "unit": "GB/s",
+        te = device_max(e0.elapsed_time(e1) / 1e3)
+        gs.check_status()
+        e2e = {"value": byt_job / (te / K) / 1e9, "unit": "GB/s",
                "h2d_bytes_per_step": int(hx.numel() + hs.numel() * 4),
                "d2h_bytes_per_step": int(hy.numel() * 2),
-               "us_per_step": te / e2e_steps * 1e6}
+               "us_per_step": te / K * 1e6,
+               "path": "pinned H2D of activation + scales, dg.launch_with_maps, "
+                       + ("NCCL gather, " if world > 1 else "") + "D2H of the bf16 output, every step"}
+
+    # ---- M sweep (BASELINE config 2: M in 1..128), rank-local, headline mode ----
+    sweep = None
+    if not args.no_sweep:
+        sweep = []
+        steps_s = min(K, 1000)
+        for mm in (1, 2, 4, 8, 16, 32, 64, 128):
+            qx_m, as_m, _ = act(mm)
+            cfg_m = dg.default_config(mm, n, k, layout=layout, pdl=pdl, independent_inputs=independent)
+            gs_m = GemmSetup(rot, cfg_m, mm, qx_m, wscale, as_m, dev)
+            graphs = capture(lambda i: gs_m.launch(i, stream), steps_s)
+            t_m = timed(graphs)
+            del graphs
+            gs_m.check_status()
+            b_m = n * k + mm * k + 2 * mm * n
+            gbs = b_m / (t_m / steps_s) / 1e9
+            sweep.append({"M": mm, "us_per_gemm": t_m / steps_s * 1e6, "GBps": gbs, "frac_of_peak": gbs / peak,
+                          "block": gs_m.plan.block[0], "mma_m": gs_m.plan.mma_m})
+            del gs_m
+
+    # ---- cuBLASLt FP8 (torch._scaled_mm) on the same cold weights: a reported
+    # library baseline with per-tensor scales (no 128-block scales), M padded
+    # to 16 rows.
+    cublas = None
+    if rank == 0 and world == 1 and not args.no_cublas:
+        try:
+            m16 = max(16, (m + 15) // 16 * 16)
+            a16 = torch.zeros((m16, k), dtype=torch.float8_e4m3fn, device=dev)
+            a16[:m] = qx.view(torch.float8_e4m3fn)
+            raw_sets = [qw.view(torch.float8_e4m3fn)] + [qw.view(torch.float8_e4m3fn).clone()
+                                                         for _ in range(rot.nsets - 1)]
+            sa = torch.tensor(sx, device=dev)
+            sb = torch.tensor(float(sw), device=dev)
+
+            def cub(i):
+                torch._scaled_mm(a16, raw_sets[i % len(raw_sets)].t(), scale_a=sa, scale_b=sb,
+                                 out_dtype=torch.bfloat16)
+            # Eager calls first: cuBLASLt picks its algorithm and workspace
+            # outside the graph capture.
+            with torch.cuda.stream(stream):
+                for i in range(3):
+                    cub(i)
+            torch.cuda.synchronize(dev)
+            graphs = capture(cub, K)
+            t_c = timed(graphs)
+            del graphs, raw_sets
+            cublas = {"us_per_gemm": t_c / K * 1e6, "GBps": byt_gpu / (t_c / K) / 1e9,
+                      "call": f"torch._scaled_mm e4m3 [{m16}x{k}] x [{k}x{n}] per-tensor scales, bf16 out"}
+        except Exception as exc:  # noqa: BLE001 - reported, not fatal
+            cublas = {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
 
     # ---- CPU baseline on rank 0 (N = 1 only), also the parity check -----------
     cpu = None
@@ -467,34 +607,32 @@ def b200_arm(args, rank, world, local_rank):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle
         run, kind = cpu_gemm_fn()
-        w_h = qw.cpu().numpy()
-        a_h = qx.cpu().numpy()
+        w_h = qw.view(torch.uint8).cpu().numpy()
+        a_h = qx.view(torch.uint8).cpu().numpy()
         ws_h = wscale.cpu().numpy()
         as_h = ascale.cpu().numpy()
         # parity of the benchmarked launch: one launch on set 0 against the
         # reference GEMM on the same bytes
-        out.zero_()
+        gs.out.zero_()
         with torch.cuda.stream(stream):
-            step(0, with_gather=False)
+            gs.launch(0, stream)
         torch.cuda.synchronize(dev)
-        got = out.float().cpu().numpy()
+        got = gs.out.float().cpu().numpy()
         threads = 1
         t0 = time.perf_counter()
         want = None
-        rows_done = 0
         reps = 0
         while True:
             want_i = cpu_parallel_gemm(run, a_h, as_h, w_h, ws_h, threads)
-            rows_done += n_loc
             reps += 1
             if want is None:
                 want = want_i
             if time.perf_counter() - t0 >= args.cpu_seconds:
                 break
         dt = (time.perf_counter() - t0) / reps
-        cpu_bytes = n_loc * k + m * k + 2 * m * n_loc
+        cpu_bytes = n * k + m * k + 2 * m * n
         cpu = {"value": cpu_bytes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": kind,
-               "sample": f"{reps} full GEMM(s) N={n_loc} K={k} M={m}, single thread, "
+               "sample": f"{reps} full GEMM(s) N={n} K={k} M={m}, single thread, "
                          f"{dt * 1e3:.1f} ms per GEMM"}
         ok, worst = oracle.elementwise_ok(got, want)
         parity = {"rel_l2": oracle.rel_l2(got, want), "max_rel_err_floored": worst, "ok": bool(ok)}
@@ -510,36 +648,40 @@ def b200_arm(args, rank, world, local_rank):
         "n_gpus": world,
         "steps": K,
         "warmup": args.warmup,
-        "ms_per_step": us_step / 1e3,
+        "ms_per_step": us_gemm / 1e3,
         "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "weak",
+        "scaling": "weak",
         "vs_baseline": None,
         "dtype": "fp8e4m3-in/f32-acc/bf16-out",
         "data": "synthetic",
         "config": {
             "workload": f"C2 decode GEMM N={n} K={k} M={m}, cold weights"
-                        + (f", TP={world} N-shards + NCCL all-gather" if world > 1 else ""),
+                        + (f"; x{world} GPUs, each a {n}-row shard of an N={world * n} tensor-parallel layer"
+                           if world > 1 else ""),
             "M": m, "N": n, "K": k, "layout": args.layout, "block_n": cfg.block_n, "subs": cfg.subs,
-            "stages": plan.stages, "grid": list(plan.grid), "threads_per_cta": plan.block[0],
-            "pdl": cfg.pdl, "pdl_mode": args.pdl_mode, "rotation_sets": nsets, "working_set_bytes": nsets * set_bytes,
-            "l2_bytes": l2, "cold": "inputs larger than L2 (rotated weight copies), no flush",
+            "stages": gs.plan.stages, "grid": list(gs.plan.grid), "threads_per_cta": gs.plan.block[0],
+            "pdl": cfg.pdl, "pdl_mode": args.pdl_mode, "rotation_sets": rot.nsets,
+            "working_set_bytes": rot.nsets * rot.set_bytes, "l2_bytes": rot.l2,
+            "cold": "inputs larger than L2 (rotated weight copies), no flush",
             "timing": "CUDA events around CUDA-graph replays of K launches, max over ranks",
         },
-        "us_per_gemm": us_step,
-        "gemm_only": {"us_per_gemm": us_gemm, "GBps_job": byt_job / (t_gemm / K) / 1e9},
+        "us_per_gemm": us_gemm,
         "pdl_mode": args.pdl_mode,
-        "other_pdl_mode": {"mode": "dependent" if args.pdl_mode == "independent" else "independent",
-                           "us_per_gemm": t_other / K * 1e6, "GBps_job": byt_job / (t_other / K) / 1e9},
+        "other_pdl_mode": {"mode": "dependent" if independent else "independent",
+                           "us_per_gemm": t_other / K * 1e6, "GBps_per_gpu": byt_gpu / (t_other / K) / 1e9},
         "pct_of_spec_8TBs": achieved / SPEC_HBM_GBS,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                      if peak_kind == "measured" else "fallback 6.65 TB/s",
-                     "traffic": traffic, "algorithmic_bytes_per_launch": byt_gpu},
+                     "traffic": ncu_traffic(workload_key), "algorithmic_bytes_per_launch": byt_gpu},
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": K * (1 if world == 1 else 1),
+        "gpu_launches": K,
         "clocks": clocks.summary(),
         "parity": parity,
+        "m_sweep": sweep,
+        "cublaslt_fp8": cublas,
+        "tensor_parallel": tp,
     }
     print(json.dumps(line), flush=True)
 

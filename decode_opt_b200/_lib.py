@@ -32,7 +32,7 @@ EXPORTED_SYMBOLS = (
     "dg_abi_version", "dg_plan", "dg_make_weight_map", "dg_make_activation_map",
     "dg_launch_with_maps", "dg_launch", "dg_prepack_weight", "dg_padded_n",
     "dg_packed_weight_bytes", "dg_status_string", "dg_flush_l2", "dg_probe_bulk_stream",
-    "dg_probe_naive_read", "dg_num_sms", "dg_launch_static_scratch",
+    "dg_probe_naive_read", "dg_num_sms", "dg_launch_static_scratch", "dg_probe_mma",
 )
 
 
@@ -128,6 +128,8 @@ def lib():
     L.dg_probe_naive_read.argtypes = [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_int, ctypes.c_void_p,
                                       ctypes.c_void_p]
     L.dg_num_sms.restype = ctypes.c_int
+    L.dg_probe_mma.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                               ctypes.c_void_p, ctypes.c_void_p]
     if L.dg_abi_version() != ABI_VERSION:
         raise RuntimeError(f"{LIB_PATH}: ABI version {L.dg_abi_version()} != {ABI_VERSION}")
     _LIB = L

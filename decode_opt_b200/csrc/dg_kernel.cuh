@@ -58,8 +58,11 @@
 // preceding kernel); activation loads, scale reads and every global write
 // come after it -- unless kFlagIndependentInputs declares that the inputs are
 // not produced by the preceding grid, in which case only the writes wait.  The
-// producer issues griddepcontrol.launch_dependents after its last TMA when
-// kFlagPdlTrigger is set (kernels/decode_gemm.cuh:708-713).
+// producer issues griddepcontrol.launch_dependents right after its first ring
+// pass when kFlagPdlTrigger is set -- earlier than the reference, which
+// triggers after its last TMA (kernels/decode_gemm.cuh:708-713): measured back
+// to back, a late trigger left each SM idle ~3.6 us between this grid's CTA
+// exiting and the next grid's CTA starting there.
 //
 // Failure behaviour.  Every wait is bounded (sm100::mbar_wait_bounded).  On a
 // timeout the CTA records an error code in *status, raises a CTA-wide abort
@@ -769,6 +772,12 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         mbar_arrive_expect_tx(&full_bar[i], tx_bytes);
         issue_weight(i);
       }
+      // Release the dependent grid now, not after the last copy: its CTAs
+      // take each SM the moment this grid's CTA there exits (one CTA fits
+      // per SM), instead of after the slowest CTA of this grid has issued its
+      // last copy.  Its griddepcontrol.wait still waits for this whole grid
+      // to complete and flush, so nothing it reads or writes is affected.
+      if (p.flags & kFlagPdlTrigger) griddep_launch_dependents();
       if (!(p.flags & kFlagIndependentInputs)) griddep_wait();
       for (int i = 0; i < first; ++i) issue_act(i);
       int issued = first;
@@ -783,7 +792,6 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         issue_act(i);
         issued = i + 1;
       }
-      if (p.flags & kFlagPdlTrigger) griddep_launch_dependents();
       // Nothing may still be landing in smem when the CTA exits.  In the
       // normal path every stage has been consumed and these waits return at
       // once; after an abort they bound the wait for copies still in flight.

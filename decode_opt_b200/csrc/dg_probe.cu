@@ -18,8 +18,16 @@
 // L2: it must read far above HBM speed, which shows the cold-buffer numbers
 // are not L2 hits.
 //
-// Timing is the caller's (CUDA events around the launch).  Every wait is
-// bounded; a timeout is reported through *status.
+//   dg_probe_mma          tcgen05.mma cost: one thread issues a run of
+//                         kind::f8f6f4 MMAs of one shape (zeroed smem
+//                         operands) round-robin over TMEM accumulators and
+//                         reads clock64 around the issue loop and around the
+//                         completion (tcgen05.commit -> mbarrier).  It is the
+//                         measurement behind the GEMM's operand placement.
+//
+// Timing of the two HBM probes is the caller's (CUDA events around the
+// launch).  Every wait is bounded; a timeout is reported through *status
+// (0x91 producer, 0x92 consumer, 0x93 MMA completion).
 
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -63,7 +71,7 @@ __global__ void __launch_bounds__(kProbeThreads, 1)
     for (int i = 0; i < n; ++i) {
       const int s = i % stages;
       if (i >= stages && !mbar_wait_bounded(&empty[s], static_cast<uint32_t>(((i / stages) & 1) ^ 1), abort_flag,
-                                            status, 0x71, kProbeTimeoutNs))
+                                            status, 0x91, kProbeTimeoutNs))
         break;
       mbar_arrive_expect_tx(&full[s], op_bytes);
       bulk_load(smem + static_cast<size_t>(s) * op_bytes, src + (op_begin + i) * op_bytes, op_bytes, &full[s], pol);
@@ -73,7 +81,7 @@ __global__ void __launch_bounds__(kProbeThreads, 1)
     uint32_t acc = 0;
     for (int i = 0; i < n; ++i) {
       const int s = i % stages;
-      if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((i / stages) & 1), abort_flag, status, 0x72,
+      if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((i / stages) & 1), abort_flag, status, 0x92,
                              kProbeTimeoutNs))
         break;
       acc ^= *reinterpret_cast<const volatile uint32_t*>(smem + static_cast<size_t>(s) * op_bytes);
@@ -117,6 +125,76 @@ __global__ void naive_read_kernel(const uint4* __restrict__ src, size_t n16, uns
   if (acc == 0x9e3779b9u) atomicAdd(sink, 1ull);
 }
 
+constexpr int kMmaProbeThreads = 128;
+constexpr uint32_t kMmaProbeSmem = 120u * 1024u;   // > half the SM: one CTA (and one TMEM owner) per SM
+
+// Bounded wait on `bar` completing the phase of `parity`; false (status set)
+// after kProbeTimeoutNs.
+__device__ bool probe_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > kProbeTimeoutNs) {
+      if (status != nullptr) atomicCAS(status, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+__global__ void __launch_bounds__(kMmaProbeThreads, 1)
+    mma_cost_kernel(int mma_m, int mma_n, int iters, int accumulators, long long* out, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023));
+  uint8_t* a_tile = smem;                 // 128 rows x 128 B, SWIZZLE_128B K-major
+  uint8_t* b_tile = smem + 16384;         // 256 rows x 128 B
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 16384 + 32768);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+  for (int i = threadIdx.x; i < (16384 + 32768) / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0u, 0u, 0u, 0u);
+  fence_proxy_async_shared();             // zero fill -> tensor-core operand reads
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  if (threadIdx.x < 32) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) {
+    const uint32_t idesc = make_idesc_e4m3_f32(static_cast<uint32_t>(mma_m), static_cast<uint32_t>(mma_n));
+    const uint32_t a0 = smem_addr(a_tile);
+    const uint32_t b0 = smem_addr(b_tile);
+    for (int i = 0; i < 8; ++i) mma_f8f6f4(tmem_base, make_desc_k_sw128(a0), make_desc_k_sw128(b0), idesc, 0u);
+    mma_commit(bar);
+    long long issue = -1, done = -1;
+    if (probe_wait(bar, 0u, status, 0x93)) {
+      const long long t0 = clock64();
+      for (int i = 0; i < iters; ++i) {
+        const int r = i % accumulators;
+        const uint32_t d = tmem_base + static_cast<uint32_t>(r * mma_n);
+        const uint32_t k = 32u * static_cast<uint32_t>(i & 3);
+        mma_f8f6f4(d, make_desc_k_sw128(a0 + k), make_desc_k_sw128(b0 + k), idesc, ((i / accumulators) & 3) != 0 ? 1u : 0u);
+      }
+      const long long t1 = clock64();
+      mma_commit(bar);
+      if (probe_wait(bar, 1u, status, 0x93)) {
+        issue = t1 - t0;
+        done = clock64() - t0;
+      }
+    }
+    out[2 * blockIdx.x] = issue;
+    out[2 * blockIdx.x + 1] = done;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x < 32) tmem_dealloc(tmem_base, 512);
+}
+
 int sm_count() {
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
@@ -154,5 +232,21 @@ int dg_probe_naive_read(const void* buf, unsigned long long bytes, int blocks_pe
 }
 
 int dg_num_sms(void) { return sm_count(); }
+
+// out: 2 * ctas long longs (issue cycles, completion cycles per CTA; -1 after
+// a timeout).
+int dg_probe_mma(int mma_m, int mma_n, int iters, int accumulators, int ctas, long long* out, int* status,
+                 void* stream) {
+  const int n_step = mma_m == 64 ? 8 : 16;
+  if (out == nullptr || !(mma_m == 64 || mma_m == 128) || mma_n < n_step || mma_n > 256 || mma_n % n_step != 0 ||
+      accumulators < 1 || accumulators * mma_n > 512 || iters < 1 || ctas < 1 || ctas > sm_count())
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(mma_cost_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kMmaProbeSmem));
+  if (e != cudaSuccess) return e;
+  mma_cost_kernel<<<ctas, kMmaProbeThreads, kMmaProbeSmem, static_cast<cudaStream_t>(stream)>>>(
+      mma_m, mma_n, iters, accumulators, out, status);
+  return cudaGetLastError();
+}
 
 }  // extern "C"

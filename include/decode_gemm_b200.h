@@ -36,6 +36,7 @@
  *                           L2 self-test :190-211 when run on a small buffer)
  *   dg_probe_naive_read     tools/peak_bw_probe.cu naive_read_nc :138-170
  *   dg_num_sms              (new) SM count of the current device
+ *   dg_probe_mma            (new) tcgen05.mma issue / completion cost per shape
  */
 #ifndef DECODE_GEMM_B200_H_
 #define DECODE_GEMM_B200_H_
@@ -87,8 +88,9 @@ typedef struct dg_config {
   int subs;      /* 128-K blocks per pipeline stage: 1, 2, 4 (reference SUBS_PER_STAGE)*/
   int stages;    /* smem ring depth, 0 = as many as fit in 227 KiB                     */
   int layout;    /* DG_LAYOUT_*  (reference PREPACK: false = RAW, true = PACKED)       */
-  int pdl;       /* 1: griddepcontrol.launch_dependents after the last TMA, and
-                    dg_launch sets programmatic stream serialization (reference PDL)   */
+  int pdl;       /* 1: griddepcontrol.launch_dependents once the first weight copies
+                    are issued, and dg_launch sets programmatic stream serialization
+                    (reference PDL)                                                      */
   int split_k;   /* reference SPLITK_FACTOR S >= 1, used when grid_ctas == 0            */
   int grid_ctas; /* 0: grid = ceil(N/BM) x split_k (reference schedule);
                     >0: stream-K over this many CTAs; <0: stream-K, one CTA per SM     */
@@ -193,6 +195,16 @@ int dg_probe_bulk_stream(const void* buf, unsigned long long bytes, unsigned op_
 int dg_probe_naive_read(const void* buf, unsigned long long bytes, int blocks_per_sm,
                         unsigned long long* sink, void* stream);
 int dg_num_sms(void);
+
+/* tcgen05.mma cost probe: each of `ctas` CTAs (at most one per SM) issues
+   `iters` kind::f8f6f4 MMAs of shape mma_m x mma_n x 32 (mma_m 64 or 128;
+   mma_n a multiple of 8 (M 64) or 16 (M 128), at most 256) from zeroed smem
+   operands, round-robin over `accumulators` TMEM accumulators
+   (accumulators * mma_n <= 512).  out[2c] = clock64 cycles to issue them,
+   out[2c+1] = cycles until all have completed; -1 and *status = 0x93 if a
+   completion wait timed out. */
+int dg_probe_mma(int mma_m, int mma_n, int iters, int accumulators, int ctas, long long* out, int* status,
+                 void* stream);
 
 #ifdef __cplusplus
 }
