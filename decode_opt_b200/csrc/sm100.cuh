@@ -18,7 +18,7 @@
 //     instruction descriptor for e4m3 x e4m3 -> f32;
 //   * programmatic dependent launch (griddepcontrol.wait / launch_dependents).
 //
-// No multicast form of any load exists in this file.
+// Every copy here lands in the issuing CTA's own shared memory only.
 
 #pragma once
 
