@@ -551,9 +551,9 @@ def b200_arm(args, rank, world, local_rank):
                "path": "pinned H2D of activation + scales, dg.launch_with_maps, "
                        + ("NCCL gather, " if world > 1 else "") + "D2H of the bf16 output, every step"}
 
-    # ---- M sweep (M in 1..128), rank-local, headline mode ----
+    # ---- M sweep (M in 1..128), one GPU, headline mode ----
     sweep = None
-    if not args.no_sweep:
+    if not args.no_sweep and world == 1:
         sweep = []
         steps_s = min(K, 1000)
         for mm in (1, 2, 4, 8, 16, 32, 64, 128):
