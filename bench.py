@@ -473,10 +473,30 @@ def b200_arm(args, rank, world, local_rank):
 
     # ---- multi-GPU: with the NCCL gather, and the strong-scaling layer ---------
     tp = None
+    fused = None
     if world > 1:
+        from decode_opt_b200 import tp as dg_tp
         graphs = capture(tp_step, K)
         t_tp = timed(graphs)
         del graphs
+        # The all-gather fused into the GEMM: every rank stores its slices into
+        # all ranks' gathered buffers over NVLink (two buffer sets alternate).
+        fused = dg_tp.FusedGather(m, n, device=dev)
+        fdesc = [fused.descriptor(0), fused.descriptor(1)]
+
+        def fused_step(i):
+            rc = dg.launch_gather(gs.cfg, gs.probs[i % gs.nsets], fdesc[i % 2], gs.wmaps[i % gs.nsets], gs.amap,
+                                  stream, pdl_attr=gs.cfg.pdl)
+            if rc != 0:
+                raise RuntimeError(f"fused launch failed: cudaError {rc}")
+        def fused_steps(i):
+            fused_step(i)
+            if i == K - 1:      # the last launch's gather completes inside the timed region
+                fused.wait((K - 1) % 2, stream=stream, status=gs.status)
+        graphs = capture(fused_steps, K)
+        t_fused = timed(graphs)
+        del graphs
+        gs.check_status()
         # Strong scaling: the one n x k layer N-sharded over
         # the ranks, each streaming n/world rows, then the gather.
         n_s = n // world
@@ -497,15 +517,36 @@ def b200_arm(args, rank, world, local_rank):
             graphs = capture(strong_tp, K)
             t_s_tp = timed(graphs)
             del graphs
+            fused_s = dg_tp.FusedGather(m, n_s, device=dev)
+            fdesc_s = [fused_s.descriptor(0), fused_s.descriptor(1)]
+
+            def strong_fused(i):
+                rc = dg.launch_gather(gs_s.cfg, gs_s.probs[i % gs_s.nsets], fdesc_s[i % 2],
+                                      gs_s.wmaps[i % gs_s.nsets], gs_s.amap, stream, pdl_attr=gs_s.cfg.pdl)
+                if rc != 0:
+                    raise RuntimeError(f"fused launch failed: cudaError {rc}")
+            def strong_fused_steps(i):
+                strong_fused(i)
+                if i == K - 1:
+                    fused_s.wait((K - 1) % 2, stream=stream, status=gs_s.status)
+            graphs = capture(strong_fused_steps, K)
+            t_s_fused = timed(graphs)
+            del graphs
+            fused_s.close()
             gs_s.check_status()
             byt_layer = n * k + m * k + 2 * m * n
             strong = {"N_layer": n, "rows_per_gpu": n_s,
                       "gemm_only": {"us_per_gemm": t_s / K * 1e6, "GBps_job": byt_layer / (t_s / K) / 1e9},
                       "with_gather": {"us_per_step": t_s_tp / K * 1e6,
-                                      "GBps_job": byt_layer / (t_s_tp / K) / 1e9}}
+                                      "GBps_job": byt_layer / (t_s_tp / K) / 1e9},
+                      "with_fused_gather": {"us_per_step": t_s_fused / K * 1e6,
+                                            "GBps_job": byt_layer / (t_s_fused / K) / 1e9}}
             del rot_s, gs_s
         tp = {"with_gather": {"us_per_step": t_tp / K * 1e6, "GBps_job": byt_job / (t_tp / K) / 1e9,
                               "collective": "NCCL all_gather_into_tensor of the bf16 [M, N/g] slices"},
+              "with_fused_gather": {"us_per_step": t_fused / K * 1e6, "GBps_job": byt_job / (t_fused / K) / 1e9,
+                                    "collective": "none: the GEMM stores its slices into every rank's "
+                                                  "gathered [M, g*N] buffer over NVLink (dg_launch_gather)"},
               "strong_scaling": strong}
 
     # ---- end to end through the public API with host buffers ----------------
@@ -521,11 +562,12 @@ def b200_arm(args, rank, world, local_rank):
         def e2e_step(i):
             qx_u8.copy_(hx, non_blocking=True)
             ascale.copy_(hs, non_blocking=True)
-            gs.launch(i, stream)
             if world > 1:
-                dist.all_gather_into_tensor(gathered, gs.out, group=pg)
-                hy.copy_(gathered.view(world, m, n).permute(1, 0, 2).reshape(m, world * n), non_blocking=True)
+                fused_step(i)
+                fused.wait(i % 2, stream=stream, status=gs.status)
+                hy.copy_(fused.output(i % 2, m), non_blocking=True)
             else:
+                gs.launch(i, stream)
                 hy.copy_(gs.out, non_blocking=True)
 
         with torch.cuda.stream(stream):
@@ -548,8 +590,14 @@ def b200_arm(args, rank, world, local_rank):
                "h2d_bytes_per_step": int(hx.numel() + hs.numel() * 4),
                "d2h_bytes_per_step": int(hy.numel() * 2),
                "us_per_step": te / K * 1e6,
-               "path": "pinned H2D of activation + scales, dg.launch_with_maps, "
-                       + ("NCCL gather, " if world > 1 else "") + "D2H of the bf16 output, every step"}
+               "path": "pinned H2D of activation + scales, "
+                       + ("dg.launch_gather (GEMM with the fused NVLink all-gather), D2H of the gathered "
+                          "bf16 [M, g*N] output" if world > 1 else "dg.launch_with_maps, D2H of the bf16 output")
+                       + ", every step"}
+
+    if fused is not None:
+        torch.cuda.synchronize(dev)
+        fused.close()
 
     # ---- M sweep (M in 1..128), one GPU, headline mode ----
     sweep = None
@@ -595,9 +643,40 @@ def b200_arm(args, rank, world, local_rank):
             torch.cuda.synchronize(dev)
             graphs = capture(cub, K)
             t_c = timed(graphs)
-            del graphs, raw_sets
+            del graphs
             cublas = {"us_per_gemm": t_c / K * 1e6, "GBps": byt_gpu / (t_c / K) / 1e9,
                       "call": f"torch._scaled_mm e4m3 [{m16}x{k}] x [{k}x{n}] per-tensor scales, bf16 out"}
+            # The same GEMM with this problem's block scales: 1x128 on the
+            # activation, 128x128 on the weights (cuBLASLt VEC128 / BLK128x128).
+            sa_blk = torch.full((m16, kb), sx, device=dev)
+            sb_blk = wscale.t()                     # (K/128, N/128) view
+            blk = None
+            for name, sa_v, sb_v in (("row-major scales", sa_blk.contiguous(), sb_blk.contiguous()),
+                                     ("outer-dim-major scales", sa_blk.t().contiguous().t(), sb_blk)):
+                try:
+                    torch._scaled_mm(a16, raw_sets[0].t(), scale_a=sa_v, scale_b=sb_v, out_dtype=torch.bfloat16)
+                    torch.cuda.synchronize(dev)
+                    blk = (name, sa_v, sb_v)
+                    break
+                except Exception as exc:  # noqa: BLE001 - try the next scale layout
+                    last_err = f"{type(exc).__name__}: {exc}"[:200]
+            if blk is None:
+                cublas["blockwise"] = {"unavailable": last_err}
+            else:
+                def cub_blk(i):
+                    torch._scaled_mm(a16, raw_sets[i % len(raw_sets)].t(), scale_a=blk[1], scale_b=blk[2],
+                                     out_dtype=torch.bfloat16)
+                with torch.cuda.stream(stream):
+                    for i in range(3):
+                        cub_blk(i)
+                torch.cuda.synchronize(dev)
+                graphs = capture(cub_blk, K)
+                t_b = timed(graphs)
+                del graphs
+                cublas["blockwise"] = {"us_per_gemm": t_b / K * 1e6, "GBps": byt_gpu / (t_b / K) / 1e9,
+                                       "call": f"torch._scaled_mm e4m3 1x128 activation / 128x128 weight block "
+                                               f"scales ({blk[0]}), M padded to {m16}"}
+            del raw_sets
         except Exception as exc:  # noqa: BLE001 - reported, not fatal
             cublas = {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
 

@@ -43,7 +43,7 @@ from ._lib import (ERR_INJECTED_TIMEOUT, FLAG_INDEPENDENT_INPUTS, FLAG_INJECT_TI
 
 __all__ = [
     "KernelConfig", "B200Config", "Problem", "LaunchPlan", "make_launch_plan", "make_weight_tma",
-    "make_activation_tma", "launch_with_maps", "launch", "padded_n", "packed_weight_bytes",
+    "make_activation_tma", "launch_with_maps", "launch", "launch_gather", "padded_n", "packed_weight_bytes",
     "launch_prepack_weight", "prepack_weight", "fp8_decode_gemm", "default_config", "status_string",
     "LAYOUT_RAW", "LAYOUT_PACKED", "LAYOUT_PACKED_SWIZZLED", "FLAG_INJECT_TIMEOUT", "FLAG_INDEPENDENT_INPUTS",
     "ERR_INJECTED_TIMEOUT", "STATUS_OK", "m_tile_for", "flush_l2",
@@ -435,6 +435,17 @@ def launch_with_maps(cfg, p: Problem, w_map: TensorMap, a_map: TensorMap, stream
         attr = cfg.PDL
     return _lib.lib().dg_launch_with_maps(ctypes.byref(b.to_dg()), ctypes.byref(p.to_dg()), w_map, a_map,
                                           _stream_handle(stream), int(bool(attr)))
+
+
+def launch_gather(cfg, p: Problem, gather, w_map: TensorMap, a_map: TensorMap, stream=None,
+                  pdl_attr: Optional[bool] = None) -> int:
+    """Tensor-parallel launch with the all-gather fused into the kernel
+    (``dg_launch_gather``; ``gather`` is a ``DgGather``, e.g. from
+    ``tp.FusedGather.descriptor``).  Returns a cudaError_t value."""
+    b = _b200(cfg, p)
+    attr = b.pdl if pdl_attr is None else pdl_attr
+    return _lib.lib().dg_launch_gather(ctypes.byref(b.to_dg()), ctypes.byref(p.to_dg()), ctypes.byref(gather),
+                                       w_map, a_map, _stream_handle(stream), int(bool(attr)))
 
 
 def launch(cfg, p: Problem, stream=None) -> int:

@@ -33,6 +33,7 @@ EXPORTED_SYMBOLS = (
     "dg_launch_with_maps", "dg_launch", "dg_prepack_weight", "dg_padded_n",
     "dg_packed_weight_bytes", "dg_status_string", "dg_flush_l2", "dg_probe_bulk_stream",
     "dg_probe_naive_read", "dg_num_sms", "dg_launch_static_scratch", "dg_probe_mma",
+    "dg_launch_gather", "dg_gather_wait", "dg_ipc_export", "dg_ipc_import", "dg_ipc_release",
 )
 
 
@@ -90,7 +91,23 @@ class DgPlanInfo(ctypes.Structure):
     ]
 
 
+MAX_RANKS = 8                   # DG_MAX_RANKS
+ERR_GATHER_WAIT = 0x81
+
+
+class DgGather(ctypes.Structure):
+    _fields_ = [
+        ("world", ctypes.c_int),
+        ("rank", ctypes.c_int),
+        ("ldo", ctypes.c_int),
+        ("outputs", ctypes.c_void_p * MAX_RANKS),
+        ("flags", ctypes.c_void_p * MAX_RANKS),
+        ("sync", ctypes.c_void_p),
+    ]
+
+
 TensorMap = ctypes.c_uint8 * 128
+IpcHandle = ctypes.c_uint8 * 64
 
 _LIB = None
 
@@ -128,6 +145,12 @@ def lib():
     L.dg_probe_naive_read.argtypes = [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_int, ctypes.c_void_p,
                                       ctypes.c_void_p]
     L.dg_num_sms.restype = ctypes.c_int
+    L.dg_launch_gather.argtypes = [cfgp, probp, ctypes.POINTER(DgGather), ctypes.c_void_p, ctypes.c_void_p,
+                                   ctypes.c_void_p, ctypes.c_int]
+    L.dg_gather_wait.argtypes = [ctypes.POINTER(DgGather), ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_void_p]
+    L.dg_ipc_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_ulonglong)]
+    L.dg_ipc_import.argtypes = [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_void_p)]
+    L.dg_ipc_release.argtypes = [ctypes.c_void_p]
     L.dg_probe_mma.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                ctypes.c_void_p, ctypes.c_void_p]
     if L.dg_abi_version() != ABI_VERSION:

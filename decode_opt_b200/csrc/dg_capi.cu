@@ -103,14 +103,43 @@ void fill_info(const Plan& plan, dg_plan_info* out) {
   out->sem_ints = plan.sem_ints;
 }
 
+// Fills the output copies and the fused-gather fields of `p` from `g`
+// (nullptr: one output, row stride N).
+cudaError_t apply_gather(dg::KernelParams& p, const dg_gather* g) {
+  p.outs[0] = p.output;
+  if (g == nullptr) return cudaSuccess;
+  if (g->world < 1 || g->world > DG_MAX_RANKS || g->rank < 0 || g->rank >= g->world || g->ldo < p.N)
+    return cudaErrorInvalidValue;
+  if (static_cast<long long>(g->rank + 1) * p.N > g->ldo) return cudaErrorInvalidValue;
+  for (int r = 0; r < g->world; ++r)
+    if (g->outputs[r] == nullptr || (g->world > 1 && g->flags[r] == nullptr)) return cudaErrorInvalidValue;
+  if (g->world > 1 && g->sync == nullptr) return cudaErrorInvalidValue;
+  p.ldo = g->ldo;
+  p.world = g->world;
+  p.rank = g->rank;
+  p.n_outs = g->world;
+  p.output = static_cast<__nv_bfloat16*>(g->outputs[g->rank]);
+  p.outs[0] = p.output;
+  for (int r = 0, k = 1; r < g->world; ++r) {
+    p.peer_flags[r] = g->flags[r];
+    if (r != g->rank) p.outs[k++] = static_cast<__nv_bfloat16*>(g->outputs[r]);
+  }
+  p.my_flags = g->flags[g->rank];
+  p.sync_ctr = g->sync;
+  return cudaSuccess;
+}
+
 int launch_impl(const dg_config* cfg, const dg_problem* prob, const CUtensorMap* w_map,
-                const CUtensorMap* a_map, cudaStream_t stream, bool pdl_attr) {
+                const CUtensorMap* a_map, cudaStream_t stream, bool pdl_attr, const dg_gather* g = nullptr) {
   if (cfg == nullptr || prob == nullptr) return cudaErrorInvalidValue;
   const Config c = to_config(cfg);
   Plan plan = dg::make_plan(c, prob->M, prob->N, prob->K, current_sm_count());
   if (plan.error != nullptr) return cudaErrorInvalidValue;
   dg::KernelParams& p = plan.params;
   p.output = static_cast<__nv_bfloat16*>(prob->output);
+  if (g != nullptr) p.output = static_cast<__nv_bfloat16*>(g->outputs[g->rank >= 0 && g->rank < DG_MAX_RANKS ? g->rank : 0]);
+  const cudaError_t g_err = apply_gather(p, g);
+  if (g_err != cudaSuccess) return g_err;
   p.w_scales = prob->weight_scales;
   p.a_scales = prob->activation_scales;
   p.ws = prob->splitk_ws;
@@ -173,6 +202,56 @@ cudaError_t static_scratch_on_current_device(void** out) {
   }
   *out = g_scratch_ptr[dev];
   return cudaSuccess;
+}
+
+// ------------------------------------------------------------------ IPC ---
+// cuMemGetAddressRange through the runtime's driver entry point (no libcuda
+// link): the base of the allocation that holds a pointer.
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+AddressRangeFn address_range_fn() {
+  static std::atomic<AddressRangeFn> cached{nullptr};
+  AddressRangeFn fn = cached.load(std::memory_order_acquire);
+  if (fn != nullptr) return fn;
+  void* sym = nullptr;
+  cudaDriverEntryPointQueryResult q{};
+  if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &sym, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || sym == nullptr)
+    return nullptr;
+  fn = reinterpret_cast<AddressRangeFn>(sym);
+  cached.store(fn, std::memory_order_release);
+  return fn;
+}
+
+// A peer allocation is opened once per process (a second cudaIpcOpenMemHandle
+// of the same handle fails), shared by every pointer into it.
+struct OpenedAllocation {
+  cudaIpcMemHandle_t handle;
+  char* base;
+  int refs;
+};
+std::mutex g_ipc_mutex;
+OpenedAllocation g_ipc_open[64];
+int g_ipc_count = 0;
+
+// dg_gather_wait: one thread waits (bounded) until every peer has published
+// this rank's latest epoch, i.e. the last fused launch before it on the
+// stream has all ranks' slices in this rank's buffer.
+__global__ void gather_wait_kernel(int world, int rank, const int* my_flags, int* status,
+                                   unsigned long long timeout_ns) {
+  using namespace dg::sm100;
+  if (threadIdx.x != 0) return;
+  const int epoch = load_relaxed_gpu(my_flags + rank);
+  const uint64_t start = global_timer_ns();
+  for (int r = 0; r < world; ++r) {
+    if (r == rank) continue;
+    while (load_relaxed_sys(my_flags + r) - epoch < 0) {
+      if (global_timer_ns() - start > timeout_ns) {
+        if (status != nullptr) atomicCAS(status, 0, DG_ERR_GATHER_WAIT);
+        return;
+      }
+    }
+  }
+  fence_acq_rel_sys();
 }
 
 __global__ void flush_kernel(uint4* buf, size_t n16) {
@@ -268,6 +347,77 @@ int dg_launch_static_scratch(const dg_config* cfg, const dg_problem* p, void* st
   return dg_launch(cfg, &q, stream);
 }
 
+int dg_launch_gather(const dg_config* cfg, const dg_problem* p, const dg_gather* g, const void* weight_map128,
+                     const void* activation_map128, void* stream, int pdl_attr) {
+  if (g == nullptr || weight_map128 == nullptr || activation_map128 == nullptr) return cudaErrorInvalidValue;
+  return launch_impl(cfg, p, static_cast<const CUtensorMap*>(weight_map128),
+                     static_cast<const CUtensorMap*>(activation_map128), static_cast<cudaStream_t>(stream),
+                     pdl_attr != 0, g);
+}
+
+int dg_gather_wait(const dg_gather* g, int* status, unsigned long long timeout_ns, void* stream) {
+  if (g == nullptr || g->world < 1 || g->world > DG_MAX_RANKS || g->rank < 0 || g->rank >= g->world ||
+      g->flags[g->rank] == nullptr)
+    return cudaErrorInvalidValue;
+  if (g->world == 1) return cudaSuccess;
+  gather_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      g->world, g->rank, g->flags[g->rank], status, timeout_ns ? timeout_ns : dg::kDefaultTimeoutNs);
+  return cudaGetLastError();
+}
+
+int dg_ipc_export(const void* ptr, void* handle64, unsigned long long* offset) {
+  if (ptr == nullptr || handle64 == nullptr || offset == nullptr) return cudaErrorInvalidValue;
+  AddressRangeFn range = address_range_fn();
+  if (range == nullptr) return cudaErrorInsufficientDriver;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  cudaIpcMemHandle_t h{};
+  const cudaError_t err = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (err != cudaSuccess) return err;
+  std::memcpy(handle64, &h, sizeof(h));
+  *offset = static_cast<unsigned long long>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return cudaSuccess;
+}
+
+int dg_ipc_import(const void* handle64, unsigned long long offset, void** ptr) {
+  if (handle64 == nullptr || ptr == nullptr) return cudaErrorInvalidValue;
+  cudaIpcMemHandle_t h{};
+  std::memcpy(&h, handle64, sizeof(h));
+  std::lock_guard<std::mutex> lock(g_ipc_mutex);
+  for (int i = 0; i < g_ipc_count; ++i) {
+    if (std::memcmp(&g_ipc_open[i].handle, &h, sizeof(h)) == 0) {
+      ++g_ipc_open[i].refs;
+      *ptr = g_ipc_open[i].base + offset;
+      return cudaSuccess;
+    }
+  }
+  if (g_ipc_count == 64) return cudaErrorMemoryAllocation;
+  void* base = nullptr;
+  const cudaError_t err = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (err != cudaSuccess) return err;
+  g_ipc_open[g_ipc_count] = {h, static_cast<char*>(base), 1};
+  ++g_ipc_count;
+  *ptr = static_cast<char*>(base) + offset;
+  return cudaSuccess;
+}
+
+int dg_ipc_release(void* ptr) {
+  if (ptr == nullptr) return cudaErrorInvalidValue;
+  std::lock_guard<std::mutex> lock(g_ipc_mutex);
+  // The opened allocation that holds ptr: the one with the largest base <= ptr.
+  int best = -1;
+  for (int i = 0; i < g_ipc_count; ++i)
+    if (g_ipc_open[i].base <= static_cast<char*>(ptr) && (best < 0 || g_ipc_open[i].base > g_ipc_open[best].base))
+      best = i;
+  if (best < 0) return cudaErrorInvalidValue;
+  if (--g_ipc_open[best].refs > 0) return cudaSuccess;
+  const cudaError_t err = cudaIpcCloseMemHandle(g_ipc_open[best].base);
+  g_ipc_open[best] = g_ipc_open[g_ipc_count - 1];
+  --g_ipc_count;
+  return err;
+}
+
 int dg_prepack_weight(const void* src, void* dst, int n, int k, int block_n, int layout, void* stream) {
   if (src == nullptr || dst == nullptr || n < 1 || k < 128 || k % 128 != 0 || block_n < 8 ||
       block_n > 256 || block_n % 8 != 0)
@@ -306,6 +456,7 @@ const char* dg_status_string(int code) {
     case DG_ERR_INJECTED_TIMEOUT: return "injected timeout (test hook)";
     case DG_ERR_BAD_LAUNCH_SHAPE: return "launch grid/block does not match the plan";
     case DG_ERR_REDUCE_WAIT: return "split reduction: a workspace bulk copy did not land in time";
+    case DG_ERR_GATHER_WAIT: return "fused gather: a peer's output slices did not arrive in time";
     default: return "unknown status";
   }
 }

@@ -199,6 +199,10 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms) {
   p.a_region_bytes = align1k(stages * a_stage);
   p.smem_bytes = smem_for(stages);
   p.timeout_ns = c.timeout_ns ? c.timeout_ns : kDefaultTimeoutNs;
+  p.ldo = N;
+  p.n_outs = 1;
+  p.world = 1;
+  p.rank = 0;
 
   plan.epi_warps = 4 * epw;
   plan.block = dim3(static_cast<unsigned>(block_threads(copies, epw)), 1u, 1u);

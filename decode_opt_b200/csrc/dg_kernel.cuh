@@ -86,6 +86,7 @@ constexpr uint32_t kMaxDynamicSmem = 227u * 1024u; // per CTA on sm_100
 constexpr int kMaxStages = 16;
 constexpr int kMaxAccumBuffers = 8;
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // 2 s
+constexpr int kMaxOutputs = 8;                     // output copies: one per tensor-parallel rank
 
 enum Layout : int {
   kLayoutRaw = 0,             // W[N,K], K contiguous
@@ -131,6 +132,7 @@ enum Status : int {
   kErrInjectedTimeout = 0x51,
   kErrBadLaunchShape = 0x61,
   kErrReduceWait = 0x71,      // split reduction: a workspace bulk copy did not land in time
+  kErrGatherWait = 0x81,      // fused gather: a peer's slices did not arrive in time
 };
 
 // Everything the kernel needs, computed on the host (dg_host.cuh) and passed
@@ -156,7 +158,14 @@ struct KernelParams {
   uint32_t a_region_bytes;   // stages * a_stage_bytes + pad, 1 KiB aligned
   uint32_t smem_bytes;       // total dynamic smem incl. 1 KiB alignment slack
   unsigned long long timeout_ns;
-  __nv_bfloat16* output;     // [M, N]
+  __nv_bfloat16* output;     // [M, ldo], this GEMM's N columns (= outs[0])
+  int ldo;                   // output row stride in elements (N unless gathering)
+  int n_outs;                // destinations of every output element: 1, or the TP world size
+  __nv_bfloat16* outs[kMaxOutputs];  // outs[0] = output; outs[r] another rank's gathered buffer
+  int world, rank;           // tensor-parallel group of the fused gather (world 1: none)
+  int* peer_flags[kMaxOutputs];      // rank r's flag array (one int per writer rank)
+  int* my_flags;             // this rank's flag array
+  int* sync_ctr;             // [2]: CTAs finished in this launch, launches completed (epoch)
   const float* w_scales;     // [ceil(N/128), K/128]
   const float* a_scales;     // [M, K/128]
   float* ws;                 // [slabs][M][N] fp32 (split tiles only)
@@ -255,11 +264,11 @@ __device__ __forceinline__ int active_epilogue_rank(int w, int M, int block_n) {
 }
 
 // mbarriers (ring full/empty, accumulator full/empty, drain, test hook, two
-// for the split reduction), then the TMEM address slot, the CTA abort flag
-// and the two-int mailbox of the split reduction.
+// for the split reduction), then the TMEM address slot, the CTA abort flag,
+// the two-int mailbox of the split reduction and the "stored output" flag.
 struct SmemBarriers {
   static __host__ __device__ constexpr uint32_t bytes(int stages, int bufs) {
-    return static_cast<uint32_t>((2 * stages + 2 * bufs + 4) * 8 + 16);
+    return static_cast<uint32_t>((2 * stages + 2 * bufs + 4) * 8 + 32);
   }
 };
 
@@ -394,8 +403,6 @@ __device__ __noinline__ bool reduce_row_blocks(const KernelParams& p, int tile, 
   // half the ring.
   const uint32_t block_bytes = static_cast<uint32_t>(n_c) * static_cast<uint32_t>(bn_t) * 32u;
   const bool bulk = allow_bulk && blocked && geo.m8 > 0 && block_bytes >= 32768u && block_bytes <= half;
-  __nv_bfloat16* out = p.output;
-
   auto piece = [&](int b, int s, uint32_t& bytes) -> const float* {
     const float* slab = p.ws + static_cast<size_t>(s) * slab_stride;
     if (b < geo.m8 / 8) {
@@ -406,21 +413,25 @@ __device__ __noinline__ bool reduce_row_blocks(const KernelParams& p, int tile, 
     bytes = static_cast<uint32_t>(bn_t) * 4u;
     return slab + static_cast<size_t>(m) * N + col0;
   };
-  // Output of one float4 unit: row m, columns c .. c+3 of the tile.
+  // Output of one float4 unit: row m, columns c .. c+3 of the tile, to every
+  // output copy.
   auto emit4 = [&](int m, int c, const float4& v) {
-    __nv_bfloat16* dst = out + static_cast<size_t>(m) * N + col0 + c;
-    if (out_vec) {
-      __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y);
-      __nv_bfloat162 hi = __floats2bfloat162_rn(v.z, v.w);
-      uint2 pk;
-      pk.x = *reinterpret_cast<uint32_t*>(&lo);
-      pk.y = *reinterpret_cast<uint32_t*>(&hi);
-      *reinterpret_cast<uint2*>(dst) = pk;
-    } else {
-      dst[0] = __float2bfloat16_rn(v.x);
-      dst[1] = __float2bfloat16_rn(v.y);
-      dst[2] = __float2bfloat16_rn(v.z);
-      dst[3] = __float2bfloat16_rn(v.w);
+    const size_t off = static_cast<size_t>(m) * p.ldo + col0 + c;
+    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(v.z, v.w);
+    for (int r = 0; r < p.n_outs; ++r) {
+      __nv_bfloat16* dst = p.outs[r] + off;
+      if (out_vec) {
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&lo);
+        pk.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(dst) = pk;
+      } else {
+        dst[0] = lo.x;
+        dst[1] = lo.y;
+        dst[2] = hi.x;
+        dst[3] = hi.y;
+      }
     }
   };
 
@@ -562,7 +573,9 @@ __device__ __noinline__ bool reduce_row_blocks(const KernelParams& p, int tile, 
     for (int q = 0; q < GROUPS; ++q) {
       if (g0 + q * nthreads >= g_end) continue;
       if (vec4) emit4(orow[q], ocol[q], tot[q]);
-      else out[static_cast<size_t>(orow[q]) * N + col0 + ocol[q]] = __float2bfloat16_rn(tot[q].x);
+      else
+        for (int r = 0; r < p.n_outs; ++r)
+          p.outs[r][static_cast<size_t>(orow[q]) * p.ldo + col0 + ocol[q]] = __float2bfloat16_rn(tot[q].x);
     }
   }
   return true;
@@ -654,6 +667,47 @@ __device__ __noinline__ void reduce_split_tiles(const KernelParams& p, const int
   }
 }
 
+// Fused gather (tensor parallel, world > 1), run by thread 0 of every CTA
+// after the CTA's last output store.  Every output element was stored to all
+// world ranks' gathered buffers (peer memory mapped over NVLink).  Each CTA
+// that stored output makes its stores visible at system scope (one release
+// fence) and every CTA counts itself done; the last CTA of the grid
+// publishes the launch's epoch (this rank's previous epoch + 1) into its own
+// and every peer's flag slot for this rank, then waits -- at most
+// p.timeout_ns, status kErrGatherWait otherwise -- until every peer has
+// published the same epoch here.  So the grid completes only when all ranks'
+// slices of this launch have landed in this rank's buffer, which also keeps
+// every rank within one launch of the others (the two alternating buffer
+// sets rely on it).  Flags are written and polled relaxed around one fence
+// per side: a release or acquire on every access at system scope measured
+// microseconds each on a GPU streaming at full bandwidth.  A launch that
+// recorded an error publishes nothing, so its peers' waits run out and
+// report it too.  The done count and the epoch are touched only after the
+// previous grid on the stream has completed (griddepcontrol.wait first).
+__device__ __noinline__ void gather_complete(const KernelParams& p, bool wrote_output) {
+  using namespace sm100;
+  griddep_wait();
+  if (wrote_output) fence_acq_rel_sys();   // this CTA's peer stores before its count
+  const int done = atomic_add_acq_rel_gpu(p.sync_ctr, 1);
+  if (done != p.num_ctas - 1) return;
+  store_relaxed_gpu(p.sync_ctr, 0);
+  if (p.status != nullptr && load_relaxed_gpu(p.status) != 0) return;
+  const int epoch = load_relaxed_gpu(p.my_flags + p.rank) + 1;
+  fence_acq_rel_sys();
+  for (int r = 0; r < p.world; ++r) store_relaxed_sys(p.peer_flags[r] + p.rank, epoch);
+  const uint64_t start = global_timer_ns();
+  for (int r = 0; r < p.world; ++r) {
+    if (r == p.rank) continue;
+    while (load_relaxed_sys(p.my_flags + r) - epoch < 0) {
+      if (global_timer_ns() - start > p.timeout_ns) {
+        if (p.status != nullptr) atomicCAS(p.status, 0, kErrGatherWait);
+        return;
+      }
+    }
+  }
+  fence_acq_rel_sys();
+}
+
 template <class Tr>
 __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
                                                  const CUtensorMap* w_map,
@@ -694,6 +748,7 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* red_mailbox = abort_flag + 1;   // [2]
+  volatile int* wrote_output = red_mailbox + 2; // this CTA stored output elements
 
   if (warp == Tr::kProducerWarp && lane == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -709,6 +764,7 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
     mbar_init(&red_bar[0], 1);
     mbar_init(&red_bar[1], 1);
     *abort_flag = 0;
+    *wrote_output = 0;
     fence_barrier_init();
   }
   if (warp == Tr::kMmaWarp) {
@@ -888,7 +944,8 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
       if (waited) griddep_wait();
 
       // 16-byte output and workspace rows need N and the base pointers aligned.
-      const bool out_vec = (N & 7) == 0 && (reinterpret_cast<uintptr_t>(p.output) & 15u) == 0;
+      bool out_vec = (p.ldo & 7) == 0;
+      for (int r = 0; r < p.n_outs; ++r) out_vec = out_vec && (reinterpret_cast<uintptr_t>(p.outs[r]) & 15u) == 0;
       const bool ws_vec = (N & 3) == 0 && (reinterpret_cast<uintptr_t>(p.ws) & 15u) == 0;
       const int m8 = ws_vec ? (M & ~7) : 0;   // workspace rows stored in 8-row blocks
       // Split tiles this CTA contributed to (only its first and last segments
@@ -981,9 +1038,11 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         const int contributors = static_cast<int>(c_last - c_first + 1);
         const int ncols = min(Tr::kColsPerWarp, min(bn - col0, N - n0));   // valid columns here
         if (contributors == 1) {
+          if (leader) *wrote_output = 1;
           if (row_ok && *abort_flag == 0)
-            store_row_bf16<Tr::kColsPerWarp>(p.output + static_cast<size_t>(m) * N + n0, partial, ncols,
-                                             out_vec);
+            for (int r = 0; r < p.n_outs; ++r)
+              store_row_bf16<Tr::kColsPerWarp>(p.outs[r] + static_cast<size_t>(m) * p.ldo + n0, partial, ncols,
+                                               out_vec);
         } else {
           const int slab = static_cast<int>(cta - c_first);
           const size_t slab_stride = static_cast<size_t>(M) * N;
@@ -1012,6 +1071,7 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
             last = red_mailbox[0];
             named_barrier_sync(1, epi_threads);
             if (last) {
+              if (leader) *wrote_output = 1;
               uint32_t no_phase = 0;
               reduce_row_blocks<Tr::kRedGroups>(p, tile, contributors, 0, SplitGeometry(M, ws_vec).nb, ws_vec,
                                                 out_vec, false, smem, 0, red_bar, no_phase, leader, active_tid,
@@ -1042,6 +1102,7 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
           named_barrier_sync(1, epi_threads);
         }
       }
+      if (red_work && leader) *wrote_output = 1;
       if (red_work)
         reduce_split_tiles<Tr::kRedGroups>(p, split_tile, split_contrib, n_split, completed, leader,
                                            active_tid, static_cast<int>(epi_threads), ws_vec, out_vec, smem,
@@ -1054,6 +1115,7 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   __syncthreads();
   tc_fence_after();
   if (warp == Tr::kMmaWarp) tmem_dealloc(tmem_base, Tr::kTmemCols);
+  if (p.world > 1 && threadIdx.x == 0) gather_complete(p, *wrote_output != 0);
 }
 
 template <int MMA_M, int COPIES, int EPW>

@@ -11,6 +11,12 @@ permute to [M, g, N/g] gives the row-major [M, N] result (M = 1 needs none).
 N/g must be a multiple of 128, so shard boundaries coincide with weight-scale
 groups (7168/8 = 896 = 7 x 128).
 
+The fused alternative (`FusedGather`, `dg_launch_gather`) drops the
+collective: each rank's GEMM stores every output element straight into all
+ranks' gathered [M, N] buffers over NVLink (peer memory mapped with CUDA IPC)
+and its grid completes only when every rank's slices of that launch have
+arrived, signalled through per-rank epoch flags with bounded waits.
+
 The reference is single-GPU; this module is the B200 multi-GPU extension the
 benchmark uses (`bench.py --gpus N`).
 """
@@ -101,3 +107,111 @@ class TPDecodeGemm:
         local = self.dg.fp8_decode_gemm(act, act_scales, self._weight(cfg), self.w_scales, config=cfg,
                                         n=self.n_loc, stream=stream)
         return gather_slices(local, self.group)
+
+
+def gather_descriptor(world: int, rank: int, n_loc: int, out_bases, flag_ptrs, sync_ptr):
+    """The dg_gather for rank `rank`: out_bases[q] is rank q's gathered
+    [M, world*n_loc] bf16 buffer as mapped in this process, flag_ptrs[q] its
+    int[world] flag array; this rank writes columns [rank*n_loc,
+    (rank+1)*n_loc) of every buffer."""
+    from ._lib import DgGather, MAX_RANKS
+    if not 1 <= world <= MAX_RANKS or not 0 <= rank < world:
+        raise ValueError("bad world/rank")
+    g = DgGather()
+    g.world = world
+    g.rank = rank
+    g.ldo = world * n_loc
+    for q in range(world):
+        g.outputs[q] = int(out_bases[q]) + 2 * rank * n_loc
+        g.flags[q] = int(flag_ptrs[q])
+    g.sync = int(sync_ptr)
+    return g
+
+
+class FusedGather:
+    """Gathered output buffers of a tensor-parallel group for the fused-gather
+    launch.
+
+    Every rank allocates `buffers` gathered [m_max, world*n_loc] bf16 buffers,
+    one int[world] flag array and an int[2] launch counter, exports CUDA IPC
+    handles for the buffers and flags, exchanges them with
+    `all_gather_object` over `group`, and maps every other rank's.
+    `descriptor(i)` is the dg_gather of buffer set i: alternate i between
+    consecutive launches (a rank must never overwrite slices a peer has not
+    consumed yet).  Every rank must make the same launches in the same order.
+    """
+
+    def __init__(self, m_max: int, n_loc: int, group=None, buffers: int = 2, device=None):
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        from . import _lib
+        self._lib = _lib.lib()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.n_loc = n_loc
+        self.m_max = m_max
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.buffers = [torch.zeros((m_max, self.world * n_loc), dtype=torch.bfloat16, device=dev)
+                        for _ in range(buffers)]
+        self.flags = torch.zeros(self.world, dtype=torch.int32, device=dev)
+        self.sync = torch.zeros(2, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+
+        def export(t):
+            h = _lib.IpcHandle()
+            off = ctypes.c_ulonglong()
+            rc = self._lib.dg_ipc_export(t.data_ptr(), h, ctypes.byref(off))
+            if rc != 0:
+                raise RuntimeError(f"dg_ipc_export failed: cudaError {rc}")
+            return bytes(h), off.value
+
+        mine = [export(b) for b in self.buffers] + [export(self.flags)]
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=group)
+        self._imported = []
+        self.peer_bufs = []    # [set][rank] base pointers in this process
+        self.peer_flags = []
+        for i in range(buffers):
+            row = []
+            for q in range(self.world):
+                row.append(self.buffers[i].data_ptr() if q == self.rank else self._import(*everyone[q][i]))
+            self.peer_bufs.append(row)
+        self.peer_flags = [self.flags.data_ptr() if q == self.rank else self._import(*everyone[q][buffers])
+                           for q in range(self.world)]
+
+    def _import(self, handle: bytes, offset: int) -> int:
+        import ctypes
+        from . import _lib
+        h = _lib.IpcHandle.from_buffer_copy(handle)
+        ptr = ctypes.c_void_p()
+        rc = self._lib.dg_ipc_import(h, offset, ctypes.byref(ptr))
+        if rc != 0:
+            raise RuntimeError(f"dg_ipc_import failed: cudaError {rc}")
+        self._imported.append(ptr.value)
+        return ptr.value
+
+    def descriptor(self, i: int):
+        return gather_descriptor(self.world, self.rank, self.n_loc, self.peer_bufs[i], self.peer_flags,
+                                 self.sync.data_ptr())
+
+    def wait(self, i: int, stream=None, status=None, timeout_ns: int = 0) -> None:
+        """Enqueue the completion wait for the last fused launch (buffer set i
+        is then complete on this rank)."""
+        import ctypes
+        import torch
+        d = self.descriptor(i)
+        s = (stream if stream is not None else torch.cuda.current_stream()).cuda_stream
+        rc = self._lib.dg_gather_wait(ctypes.byref(d), status.data_ptr() if status is not None else None,
+                                      timeout_ns, s)
+        if rc != 0:
+            raise RuntimeError(f"dg_gather_wait failed: cudaError {rc}")
+
+    def output(self, i: int, m: int):
+        """This rank's gathered [m, world*n_loc] result of buffer set i."""
+        return self.buffers[i][:m]
+
+    def close(self):
+        for ptr in self._imported:
+            self._lib.dg_ipc_release(ptr)
+        self._imported = []

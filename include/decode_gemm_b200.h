@@ -35,6 +35,10 @@
  *   dg_probe_bulk_stream    tools/peak_bw_probe.cu tma_stream_probe :82-134 (and the
  *                           L2 self-test :190-211 when run on a small buffer)
  *   dg_probe_naive_read     tools/peak_bw_probe.cu naive_read_nc :138-170
+ *   dg_launch_gather        (new: the reference is single-GPU) tensor-parallel launch
+ *                           with the all-gather fused into the epilogue
+ *   dg_gather_wait          (new) completion wait for the fused gather
+ *   dg_ipc_export / dg_ipc_import / dg_ipc_release  (new) peer buffers for it
  *   dg_num_sms              (new) SM count of the current device
  *   dg_probe_mma            (new) tcgen05.mma issue / completion cost per shape
  */
@@ -76,6 +80,7 @@ extern "C" {
 #define DG_ERR_INJECTED_TIMEOUT 0x51
 #define DG_ERR_BAD_LAUNCH_SHAPE 0x61
 #define DG_ERR_REDUCE_WAIT 0x71
+#define DG_ERR_GATHER_WAIT 0x81
 
 /* Runtime configuration.  Zero-initialise, then set fields. */
 typedef struct dg_config {
@@ -149,6 +154,47 @@ int dg_launch_with_maps(const dg_config* cfg, const dg_problem* p, const void* w
 
 /* Encodes both maps, then launches (attribute follows cfg->pdl). */
 int dg_launch(const dg_config* cfg, const dg_problem* p, void* stream);
+
+/* Tensor-parallel GEMM with the all-gather fused into the kernel.  Rank r of
+   `world` computes its N-shard (p->N rows of W) and stores every output element
+   into all ranks' gathered [M, ldo] bf16 buffers over NVLink (peer memory
+   mapped into this process, e.g. with dg_ipc_import), at column offset
+   r * p->N.  The grid publishes a per-launch epoch into every rank's flag
+   array after its stores and completes only after every peer has published
+   the same epoch here (bounded wait; status DG_ERR_GATHER_WAIT otherwise):
+   when it has completed, this rank's gathered [M, N] of the launch is whole.
+   After any error re-zero the flags and sync words on every rank.
+   p->output is ignored (outputs[rank] is used).
+   Consecutive launches must alternate between two sets of gathered buffers;
+   every rank must make the same sequence of launches. */
+#define DG_MAX_RANKS 8
+typedef struct dg_gather {
+  int world, rank;            /* tensor-parallel group, 1 <= world <= DG_MAX_RANKS */
+  int ldo;                    /* row stride of the gathered buffers in elements (world * N) */
+  void* outputs[DG_MAX_RANKS];/* rank q's gathered buffer + rank * N (this rank's columns)   */
+  int* flags[DG_MAX_RANKS];   /* rank q's flag array: int[world], zeroed once                  */
+  int* sync;                  /* this rank's int[2] (CTA done count, reserved), zeroed once   */
+} dg_gather;
+
+/* Replaces no reference interface (the reference is single-GPU): launch with
+   pre-built maps and the fused gather. */
+int dg_launch_gather(const dg_config* cfg, const dg_problem* p, const dg_gather* g, const void* weight_map128,
+                     const void* activation_map128, void* stream, int pdl_attr);
+
+/* Waits on `stream` (one thread, bounded by timeout_ns, 0 = 2 s) until every
+   peer has published this rank's latest epoch -- already true once the last
+   fused launch has completed; an explicit check for callers that want one.
+   status (device int, may be NULL) receives DG_ERR_GATHER_WAIT on a timeout. */
+int dg_gather_wait(const dg_gather* g, int* status, unsigned long long timeout_ns, void* stream);
+
+/* CUDA IPC for the fused gather's peer buffers (no reference counterpart).
+   dg_ipc_export: 64-byte handle of the allocation holding `ptr` and ptr's
+   offset in it.  dg_ipc_import: maps a peer's allocation (once per process,
+   reference-counted) and returns the peer pointer; dg_ipc_release drops one
+   reference (`ptr` as returned by dg_ipc_import). */
+int dg_ipc_export(const void* ptr, void* handle64, unsigned long long* offset);
+int dg_ipc_import(const void* handle64, unsigned long long offset, void** ptr);
+int dg_ipc_release(void* ptr);
 
 /* Capacity of the library's static split-K scratch (dg_launch_static_scratch):
    4096 tickets (16 KiB) + 2 Mi workspace floats (8 MiB) per device. */

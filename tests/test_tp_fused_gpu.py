@@ -1,0 +1,136 @@
+"""GPU tests of the GEMM with the tensor-parallel all-gather fused into the
+kernel (dg_launch_gather).
+
+* One GPU: the output-copy path with a row stride and a column offset (a
+  world of one writing into a wider buffer); columns outside its slice keep
+  their sentinel.
+* Two GPUs (skipped on a box with fewer): two ranks as child processes, each
+  computing its N-shard and storing into both ranks' gathered buffers over
+  NVLink; after the completion wait both gathered outputs must match the
+  oracle for the whole N over two consecutive launches (alternating buffer
+  sets), with status 0.
+"""
+
+import ctypes
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+import decode_opt_b200 as dg
+from decode_opt_b200 import _lib, tp
+
+pytestmark = pytest.mark.gpu
+
+
+def test_strided_output_at_column_offset():
+    import oracle
+    from helpers import check_against_oracle
+    n, k, m = 1024, 2048, 5
+    w, ws = oracle.gen_weight_smoke(n, k, 77)
+    a, as_ = oracle.gen_activation_smoke(m, k, 78)
+    ref = oracle.compute_reference(a, as_, w, ws, threads=8)
+    dev = "cuda"
+    cfg = dg.default_config(m, n, k, layout=dg.LAYOUT_PACKED_SWIZZLED)
+    plan = cfg.plan(m, n, k)
+    wt = dg.prepack_weight(torch.from_numpy(w).to(dev), cfg.block_n, cfg.layout)
+    ldo, col = n + 64, 32
+    wide = torch.full((m, ldo), -7.0, dtype=torch.bfloat16, device=dev)
+    ws_buf = torch.zeros(max(plan.ws_floats, 1), device=dev)
+    sem = torch.zeros(max(plan.sem_ints, 1), dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    act = torch.from_numpy(a).to(dev)
+    p = dg.Problem(m, n, k, act, wt, torch.from_numpy(ws).to(dev), torch.from_numpy(as_).to(dev), None, ws_buf,
+                   sem, status)
+    g = _lib.DgGather()
+    g.world, g.rank, g.ldo = 1, 0, ldo
+    g.outputs[0] = wide.data_ptr() + 2 * col
+    g.sync = 0
+    rc = dg.launch_gather(cfg, p, g, dg.make_weight_tma(cfg, p), dg.make_activation_tma(cfg, p))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    got = wide.float().cpu().numpy()
+    ok, rl2, worst = check_against_oracle(got[:, col:col + n], ref)
+    assert ok, (rl2, worst)
+    assert np.all(got[:, :col] == -7.0) and np.all(got[:, col + n:] == -7.0)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _rank_main(rank, world, port, m, n, k, result_dir):
+    import torch.distributed as dist
+    import oracle
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    fg = None
+    try:
+        dev = torch.device("cuda", rank)
+        w, ws = oracle.gen_weight_smoke(n, k, 91)
+        n_loc = n // world
+        lo, hi = tp.shard_rows(n, world, rank)
+        cfg = dg.default_config(m, n_loc, k, layout=dg.LAYOUT_PACKED_SWIZZLED)
+        plan = cfg.plan(m, n_loc, k)
+        wt = dg.prepack_weight(torch.from_numpy(np.ascontiguousarray(w[lo:hi])).to(dev), cfg.block_n, cfg.layout)
+        wsc = torch.from_numpy(np.ascontiguousarray(tp.shard_scales(ws, world, rank, n))).to(dev)
+        ws_buf = torch.zeros(max(plan.ws_floats, 1), device=dev)
+        sem = torch.zeros(max(plan.sem_ints, 1), dtype=torch.int32, device=dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        fg = tp.FusedGather(m, n_loc, device=dev)
+        results = []
+        for step in range(2):
+            a, as_ = oracle.gen_activation_smoke(m, k, 200 + step)
+            act = torch.from_numpy(a).to(dev)
+            p = dg.Problem(m, n_loc, k, act, wt, wsc, torch.from_numpy(as_).to(dev), None, ws_buf, sem, status)
+            dist.barrier()
+            rc = dg.launch_gather(cfg, p, fg.descriptor(step % 2), dg.make_weight_tma(cfg, p),
+                                  dg.make_activation_tma(cfg, p))
+            assert rc == 0, rc
+            fg.wait(step % 2, status=status)
+            torch.cuda.synchronize(dev)
+            assert int(status.item()) == 0, dg.status_string(int(status.item()))
+            results.append(fg.output(step % 2, m).float().cpu().numpy())
+        np.save(os.path.join(result_dir, f"rank{rank}.npy"), np.stack(results))
+        dist.barrier()
+    finally:
+        if fg is not None:
+            fg.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("m", [1, 8])
+def test_two_gpu_fused_gather_matches_oracle(tmp_path, m):
+    import torch.multiprocessing as mp
+    import oracle
+    from helpers import check_against_oracle
+    n, k, world = 2048, 4096, 2
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, m, n, k, str(tmp_path))) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.exitcode is None:
+            p.kill()
+        assert p.exitcode == 0
+    w, ws = oracle.gen_weight_smoke(n, k, 91)
+    for step in range(2):
+        a, as_ = oracle.gen_activation_smoke(m, k, 200 + step)
+        ref = oracle.compute_reference(a, as_, w, ws, threads=8)
+        for r in range(world):
+            got = np.load(os.path.join(str(tmp_path), f"rank{r}.npy"))[step]
+            ok, rl2, worst = check_against_oracle(got, ref)
+            assert ok, (r, step, rl2, worst)

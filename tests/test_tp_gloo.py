@@ -81,3 +81,20 @@ def test_assemble_layout():
     for r in range(g):
         assert torch.equal(full[:, r * n_loc:(r + 1) * n_loc], gathered[r])
     assert tp.assemble(gathered[:, :1], 1).shape == (1, g * n_loc)
+
+
+def test_gather_descriptor_pointer_table():
+    """Rank r of g writes columns [r*n_loc, (r+1)*n_loc) of every rank's
+    gathered buffer; the row stride is g*n_loc; flags and sync pass through."""
+    world, n_loc = 4, 896
+    bases = [0x10000000 * (q + 1) for q in range(world)]
+    flags = [0x7000 + 64 * q for q in range(world)]
+    for rank in range(world):
+        g = tp.gather_descriptor(world, rank, n_loc, bases, flags, 0x9000)
+        assert (g.world, g.rank, g.ldo) == (world, rank, world * n_loc)
+        for q in range(world):
+            assert g.outputs[q] == bases[q] + 2 * rank * n_loc
+            assert g.flags[q] == flags[q]
+        assert g.sync == 0x9000
+    with pytest.raises(ValueError):
+        tp.gather_descriptor(9, 0, n_loc, bases * 3, flags * 3, 0)
