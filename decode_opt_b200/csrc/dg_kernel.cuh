@@ -10,7 +10,7 @@
 // This is the hot path the reference implements as fp8_decode_gemm<Cfg>
 // (kernels/decode_gemm.cuh:574-1081).  It is a new design for Blackwell.
 //
-// Operand placement.  A tcgen05.mma takes the same ~180 cycles whatever its
+// Operand placement.  A tcgen05.mma takes the same ~161 cycles whatever its
 // M and N (measured on B200 for kind::f8f6f4, M in {64,128}, N in 16..256), so
 // the weights -- the only large operand -- go on the MMA's N side with up to
 // N = 256 rows per instruction: 8 KiB of weights per MMA, twice what an
