@@ -73,6 +73,7 @@ def parse_args():
     ap.add_argument("--graph-chunk", type=int, default=500, help="launches per captured CUDA graph")
     ap.add_argument("--no-sweep", action="store_true", help="skip the M = 1..128 sweep")
     ap.add_argument("--no-cublas", action="store_true", help="skip the cuBLASLt FP8 baseline")
+    ap.add_argument("--no-chain", action="store_true", help="skip the 61-layer dependent chain")
     return ap.parse_args()
 
 
@@ -618,6 +619,66 @@ def b200_arm(args, rank, world, local_rank):
                           "block": gs_m.plan.block[0], "mma_m": gs_m.plan.mma_m})
             del gs_m
 
+    # ---- 61-layer decode chain with a true data dependency:
+    # layers alternate N x K = 7168 x 16384 ("down", the C2 shape) and
+    # 16384 x 7168 ("up"); every layer is a GEMM launched with PDL in the
+    # dependent mode (its activation is read only after the previous grid
+    # completes, its weights are prefetched before) followed by the GPU
+    # quantiser of its bf16 output into the next layer's e4m3 activation and
+    # 1x128 block scales.  Each layer has its own weight copy (7.2 GB, cold).
+    chain = None
+    if not args.no_chain and world == 1:
+        layers = 61
+        passes = max(3, min(20, K // 500))
+        dn = (n, k)
+        up = (k, n)
+        shapes = [dn if li % 2 == 0 else up for li in range(layers)]
+        base = {}
+        for (nn, kk) in (dn, up):
+            gw = torch.Generator(device=dev).manual_seed(1000 + nn)
+            wq, ws_ = quantize_pertensor(torch.randn((nn, kk), device=dev, generator=gw), torch.float8_e4m3fn)
+            cfg_l = dg.default_config(m, nn, kk, layout=layout, pdl=pdl, independent_inputs=False)
+            packed = wq if layout == dg.LAYOUT_RAW else dg.prepack_weight(wq, cfg_l.block_n, layout)
+            base[(nn, kk)] = (packed, torch.full(((nn + 127) // 128, kk // 128), float(ws_), device=dev), cfg_l)
+        weights = [base[sh][0].clone() for sh in shapes]
+        act_in = {k: torch.zeros((m, k), dtype=torch.uint8, device=dev), n: torch.zeros((m, n), dtype=torch.uint8, device=dev)}
+        act_sc = {k: torch.zeros((m, k // 128), device=dev), n: torch.zeros((m, n // 128), device=dev)}
+        outs = {n: torch.empty((m, n), dtype=torch.bfloat16, device=dev),
+                k: torch.empty((m, k), dtype=torch.bfloat16, device=dev)}
+        q0, s0 = dg.quantize_activation(torch.randn((m, k), device=dev, generator=gx).bfloat16())
+        act_in[k].copy_(q0)
+        act_sc[k].copy_(s0)
+        plans = {sh: base[sh][2].plan(m, *sh) for sh in (dn, up)}
+        ws_c = torch.zeros(max(max(pl.ws_floats for pl in plans.values()), 1), device=dev)
+        sem_c = torch.zeros(max(max(pl.sem_ints for pl in plans.values()), 1), dtype=torch.int32, device=dev)
+        st_c = torch.zeros(1, dtype=torch.int32, device=dev)
+        steps_c = []
+        for li, (nn, kk) in enumerate(shapes):
+            cfg_l = base[(nn, kk)][2]
+            pr = dg.Problem(m, nn, kk, act_in[kk], weights[li], base[(nn, kk)][1], act_sc[kk], outs[nn], ws_c,
+                            sem_c, st_c)
+            steps_c.append((cfg_l, pr, dg.make_weight_tma(cfg_l, pr), dg.make_activation_tma(cfg_l, pr), nn))
+
+        def chain_step(i):
+            cfg_l, pr, wm_, am_, nn = steps_c[i % layers]
+            rc = dg.launch_with_maps(cfg_l, pr, wm_, am_, stream, pdl_attr=cfg_l.pdl)
+            if rc != 0:
+                raise RuntimeError(f"chain launch failed: cudaError {rc}")
+            dg.quantize_activation(outs[nn], out=act_in[nn], scales=act_sc[nn], stream=stream, pdl_attr=True)
+        graphs = capture(chain_step, layers * passes)
+        t_chain = timed(graphs)
+        del graphs
+        if int(st_c.item()) != 0:
+            raise RuntimeError(f"chain status {dg.status_string(int(st_c.item()))}")
+        per_layer = t_chain / (layers * passes)
+        bytes_layer = sum(nn * kk + m * kk + 2 * m * nn for (nn, kk) in shapes) / layers
+        chain = {"layers": layers, "passes_timed": passes, "shapes": "alternating 7168x16384 / 16384x7168",
+                 "us_per_layer": per_layer * 1e6, "GBps": bytes_layer / per_layer / 1e9,
+                 "frac_of_peak": bytes_layer / per_layer / 1e9 / peak,
+                 "per_layer": "GEMM (PDL, dependent: weights before griddepcontrol.wait, activation after) "
+                              "+ GPU bf16->e4m3 block quantiser of its output (PDL)"}
+        del weights, steps_c
+
     # ---- cuBLASLt FP8 (torch._scaled_mm) on the same cold weights: a reported
     # library baseline with per-tensor scales (no 128-block scales), M padded
     # to 16 rows.
@@ -761,6 +822,7 @@ def b200_arm(args, rank, world, local_rank):
         "m_sweep": sweep,
         "cublaslt_fp8": cublas,
         "tensor_parallel": tp,
+        "chain_61": chain,
     }
     print(json.dumps(line), flush=True)
 

@@ -43,7 +43,8 @@ from ._lib import (ERR_INJECTED_TIMEOUT, FLAG_INDEPENDENT_INPUTS, FLAG_INJECT_TI
 
 __all__ = [
     "KernelConfig", "B200Config", "Problem", "LaunchPlan", "make_launch_plan", "make_weight_tma",
-    "make_activation_tma", "launch_with_maps", "launch", "launch_gather", "padded_n", "packed_weight_bytes",
+    "make_activation_tma", "launch_with_maps", "launch", "launch_gather", "quantize_activation", "padded_n",
+    "packed_weight_bytes",
     "launch_prepack_weight", "prepack_weight", "fp8_decode_gemm", "default_config", "status_string",
     "LAYOUT_RAW", "LAYOUT_PACKED", "LAYOUT_PACKED_SWIZZLED", "FLAG_INJECT_TIMEOUT", "FLAG_INDEPENDENT_INPUTS",
     "ERR_INJECTED_TIMEOUT", "STATUS_OK", "m_tile_for", "flush_l2",
@@ -446,6 +447,25 @@ def launch_gather(cfg, p: Problem, gather, w_map: TensorMap, a_map: TensorMap, s
     attr = b.pdl if pdl_attr is None else pdl_attr
     return _lib.lib().dg_launch_gather(ctypes.byref(b.to_dg()), ctypes.byref(p.to_dg()), ctypes.byref(gather),
                                        w_map, a_map, _stream_handle(stream), int(bool(attr)))
+
+
+def quantize_activation(x, out=None, scales=None, stream=None, pdl_attr: bool = False):
+    """bf16 [M, K] (row stride >= K) -> (e4m3 [M, K] as uint8, fp32 scales
+    [M, K/128]) on the GPU: the reference's block quantisation
+    (bench/bench_decode.cu:459-467)."""
+    import torch
+    m, k = x.shape
+    if x.dtype != torch.bfloat16 or x.stride(1) != 1:
+        raise ValueError("x must be bf16 with unit column stride")
+    if out is None:
+        out = torch.empty((m, k), dtype=torch.uint8, device=x.device)
+    if scales is None:
+        scales = torch.empty((m, k // 128), dtype=torch.float32, device=x.device)
+    rc = _lib.lib().dg_quantize_act(x.data_ptr(), x.stride(0), m, k, out.data_ptr(), scales.data_ptr(),
+                                    _stream_handle(stream), int(bool(pdl_attr)))
+    if rc != 0:
+        raise RuntimeError(f"dg_quantize_act failed: cudaError {rc}")
+    return out, scales
 
 
 def launch(cfg, p: Problem, stream=None) -> int:

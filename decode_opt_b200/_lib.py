@@ -34,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "dg_packed_weight_bytes", "dg_status_string", "dg_flush_l2", "dg_probe_bulk_stream",
     "dg_probe_naive_read", "dg_num_sms", "dg_launch_static_scratch", "dg_probe_mma",
     "dg_launch_gather", "dg_gather_wait", "dg_ipc_export", "dg_ipc_import", "dg_ipc_release",
+    "dg_quantize_act",
 )
 
 
@@ -147,6 +148,8 @@ def lib():
     L.dg_num_sms.restype = ctypes.c_int
     L.dg_launch_gather.argtypes = [cfgp, probp, ctypes.POINTER(DgGather), ctypes.c_void_p, ctypes.c_void_p,
                                    ctypes.c_void_p, ctypes.c_int]
+    L.dg_quantize_act.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
     L.dg_gather_wait.argtypes = [ctypes.POINTER(DgGather), ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_void_p]
     L.dg_ipc_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_ulonglong)]
     L.dg_ipc_import.argtypes = [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_void_p)]

@@ -22,7 +22,7 @@ LIB_NAME = "libdecode_gemm_b200.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ("dg_capi.cu", "dg_probe.cu")
+SOURCES = ("dg_capi.cu", "dg_probe.cu", "dg_quant.cu")
 
 
 def nvcc() -> str:

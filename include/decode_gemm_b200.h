@@ -31,6 +31,8 @@
  *   dg_padded_n             prepack::padded_n   kernels/weight_prepack.cuh:45-47
  *   dg_packed_weight_bytes  prepack::packed_weight_bytes kernels/weight_prepack.cuh:50-52
  *   dg_status_string        (new) text of the kernel's device status codes
+ *   dg_quantize_act         host block quantisation of bench/bench_decode.cu:459-467
+ *                           (make_activation), as a GPU kernel
  *   dg_flush_l2             bench helper flush_l2_kernel bench/bench_decode.cu:473-476
  *   dg_probe_bulk_stream    tools/peak_bw_probe.cu tma_stream_probe :82-134 (and the
  *                           L2 self-test :190-211 when run on a small buffer)
@@ -227,6 +229,15 @@ int dg_padded_n(int n, int block_n);
 unsigned long long dg_packed_weight_bytes(int n, int k, int block_n);
 
 const char* dg_status_string(int code);
+
+/* Activation quantiser: bf16 x[M, K] (row stride ldx >= K, e.g. a gathered
+   [M, N] GEMM output feeding the next layer) -> e4m3 q[M, K] and fp32
+   scales[M, K/128], per row and 128-column block scale = max(amax, 1e-4)/448,
+   q = e4m3_rn(clamp(x / scale, +-448)) -- the reference's host quantisation
+   (bench/bench_decode.cu:459-467) on the GPU.  K % 128 == 0, q 4-byte
+   aligned.  pdl_attr: launch with programmatic stream serialization (the
+   kernel releases its dependents at once and waits for the producer of x). */
+int dg_quantize_act(const void* x, int ldx, int M, int K, void* q, float* scales, void* stream, int pdl_attr);
 
 /* Writes `bytes` of `buf` (device) to evict L2 between timed launches. */
 int dg_flush_l2(void* buf, unsigned long long bytes, void* stream);

@@ -80,6 +80,7 @@ def load():
     pk = [_u8p, _u8p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
     lib.orc_prepack.argtypes = pk
     lib.orc_prepack_swizzled.argtypes = pk
+    lib.orc_quantize_rows.argtypes = [ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int, _u8p, _f32p]
     _LIB = lib
     return lib
 
@@ -148,6 +149,17 @@ def gen_activation_bench(rows: int, k: int, seed: int):
     s = np.zeros((rows, k // 128), np.float32)
     load().orc_gen_activation_bench(rows, k, seed, _ptr(a, _u8p), _ptr(s, _f32p))
     return a, s
+
+
+def quantize_rows(x: np.ndarray):
+    """fp32 rows [M, K] -> (e4m3 bytes [M, K], scales [M, K/128]): the block
+    quantisation of bench/bench_decode.cu:459-467."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    m, k = x.shape
+    q = np.zeros((m, k), np.uint8)
+    s = np.zeros((m, k // 128), np.float32)
+    load().orc_quantize_rows(m, k, _ptr(x, _f32p), k, _ptr(q, _u8p), _ptr(s, _f32p))
+    return q, s
 
 
 def gen_pertensor(rows: int, k: int, seed: int, scale_rows: int | None = None, threads: int = 1):

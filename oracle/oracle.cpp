@@ -24,6 +24,8 @@
 //   orc_gen_activation_smoke         smoke_test.cu generate_activation
 //   orc_gen_weight_bench             bench_decode.cu make_weights
 //   orc_gen_activation_bench         bench_decode.cu make_activation
+//   orc_quantize_rows                bench_decode.cu:459-467, the block quantisation
+//                                    of make_activation, on given rows
 //   orc_gen_pertensor                per-tensor-scaled N(0,1) inputs (BASELINE mode)
 //   orc_compute_reference            smoke_test.cu compute_reference
 //   orc_compute_reference_mt         same, N split over threads (bit-identical)
@@ -204,6 +206,26 @@ void orc_gen_activation_bench(int rows, int K, uint64_t seed, uint8_t* act, floa
       const float scale = std::max(amax, kQuantEps) / kFp8Max;
       scales[static_cast<size_t>(m) * kb + kbi] = scale;
       uint8_t* dst = act + static_cast<size_t>(m) * K + static_cast<size_t>(kbi) * 128;
+      for (int c = 0; c < 128; ++c) dst[c] = quant(row[kbi * 128 + c], scale);
+    }
+  }
+}
+
+// The block quantisation of make_activation (bench/bench_decode.cu:459-467)
+// applied to given fp32 rows (row stride ldx): per row and 128-column block,
+// amax = max |v| (std::max order), scale = max(amax, 1e-4) / 448,
+// q = e4m3(clamp(v / scale, +-448)).  The GPU activation quantiser is checked
+// against it.
+void orc_quantize_rows(int rows, int K, const float* x, int ldx, uint8_t* q, float* scales) {
+  const int kb = K / kKBlock;
+  for (int m = 0; m < rows; ++m) {
+    const float* row = x + static_cast<size_t>(m) * ldx;
+    for (int kbi = 0; kbi < kb; ++kbi) {
+      float amax = 0.0f;
+      for (int c = 0; c < 128; ++c) amax = std::max(amax, std::abs(row[kbi * 128 + c]));
+      const float scale = std::max(amax, kQuantEps) / kFp8Max;
+      scales[static_cast<size_t>(m) * kb + kbi] = scale;
+      uint8_t* dst = q + static_cast<size_t>(m) * K + static_cast<size_t>(kbi) * 128;
       for (int c = 0; c < 128; ++c) dst[c] = quant(row[kbi * 128 + c], scale);
     }
   }

@@ -177,3 +177,24 @@ def test_elementwise_check_floor():
     assert ok
     ok, _ = oracle.elementwise_ok(want * 1.05, want)
     assert not ok
+
+
+def test_quantize_rows_matches_reference_formula_and_torch_e4m3():
+    """orc_quantize_rows (bench/bench_decode.cu:459-467): scale =
+    max(amax, 1e-4)/448 per row and 128-block, bytes = RN e4m3 of the clamped
+    quotient -- cross-checked against torch's float8_e4m3fn conversion, with a
+    zero block (scale = 1e-4/448) and large magnitudes."""
+    import torch
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((6, 512)).astype(np.float32) * np.float32(3.0)
+    x[1, 128:256] = 0.0
+    x[2, :128] *= np.float32(1e4)
+    x = torch.from_numpy(x).bfloat16().float().numpy()
+    q, s = oracle.quantize_rows(x)
+    blocks = x.reshape(6, 4, 128)
+    amax = np.abs(blocks).max(-1)
+    assert np.array_equal(s, (np.maximum(amax, np.float32(1e-4)) / np.float32(448)).astype(np.float32))
+    assert s[1, 1] == np.float32(np.float32(1e-4) / np.float32(448))
+    want = torch.from_numpy(np.clip(blocks / s[..., None], -448, 448).astype(np.float32)) \
+        .to(torch.float8_e4m3fn).view(torch.uint8).numpy().reshape(6, 512)
+    assert np.array_equal(q, want)
