@@ -37,7 +37,6 @@ import argparse
 import json
 import math
 import os
-import statistics
 import sys
 import threading
 import time
@@ -99,67 +98,6 @@ def ncu_traffic(workload_key):
             return json.load(f).get(workload_key)
     except (OSError, ValueError):
         return None
-
-
-class ClockSampler:
-    """Samples SM clock and throttle reasons with NVML every ~20 ms."""
-
-    REASONS = {  # nvmlClocksEventReason* bits
-        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
-        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
-        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
-    }
-
-    def __init__(self, device_index: int):
-        self.samples = []
-        self.max_mhz = None
-        self._stop = threading.Event()
-        self._thread = None
-        self._marks = []
-        try:
-            import pynvml
-            pynvml.nvmlInit()
-            self._nvml = pynvml
-            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
-        except Exception:  # noqa: BLE001 - NVML missing: report no clocks
-            self._nvml = None
-
-    def _run(self):
-        nv = self._nvml
-        while not self._stop.is_set():
-            try:
-                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
-                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                self.samples.append((time.perf_counter(), mhz, reasons))
-            except Exception:  # noqa: BLE001
-                pass
-            self._stop.wait(0.02)
-
-    def start(self):
-        if self._nvml is not None:
-            self._thread = threading.Thread(target=self._run, daemon=True)
-            self._thread.start()
-
-    def mark(self):
-        self._marks.append(time.perf_counter())
-
-    def stop(self):
-        self._stop.set()
-        if self._thread is not None:
-            self._thread.join(timeout=1.0)
-
-    def summary(self):
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
-        lo, hi = (self._marks[0], self._marks[-1]) if len(self._marks) >= 2 else (-1e30, 1e30)
-        inside = [s for s in self.samples if lo <= s[0] <= hi] or self.samples
-        mhz = statistics.median(s[1] for s in inside)
-        bits = 0
-        for s in inside:
-            bits |= s[2]
-        reasons = sorted(name for bit, name in self.REASONS.items() if bits & bit and name != "gpu_idle")
-        return {"sm_mhz": mhz, "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(inside)}
 
 
 def quantize_pertensor(x, fp8):
@@ -447,6 +385,7 @@ def b200_arm(args, rank, world, local_rank):
     gs.check_status()
 
     graphs = capture(gemm_step, K)
+    from decode_opt_b200.clocks import ClockSampler
     clocks = ClockSampler(local_rank)
     clocks.start()
     time.sleep(0.05)
