@@ -38,8 +38,8 @@ from dataclasses import dataclass, field
 from typing import Optional
 
 from . import _lib
-from ._lib import (ERR_INJECTED_TIMEOUT, FLAG_INDEPENDENT_INPUTS, FLAG_INJECT_TIMEOUT, LAYOUT_PACKED, LAYOUT_PACKED_SWIZZLED,
-                   LAYOUT_RAW, STATUS_OK, DgConfig, DgPlanInfo, DgProblem, TensorMap)
+from ._lib import (ERR_INJECTED_TIMEOUT, FLAG_INDEPENDENT_INPUTS, FLAG_INJECT_TIMEOUT, GRID_CLUSTER, LAYOUT_PACKED,
+                   LAYOUT_PACKED_SWIZZLED, LAYOUT_RAW, STATUS_OK, DgConfig, DgPlanInfo, DgProblem, TensorMap)
 
 __all__ = [
     "KernelConfig", "B200Config", "Problem", "LaunchPlan", "make_launch_plan", "make_weight_tma",
@@ -47,7 +47,7 @@ __all__ = [
     "packed_weight_bytes",
     "launch_prepack_weight", "prepack_weight", "fp8_decode_gemm", "default_config", "status_string",
     "LAYOUT_RAW", "LAYOUT_PACKED", "LAYOUT_PACKED_SWIZZLED", "FLAG_INJECT_TIMEOUT", "FLAG_INDEPENDENT_INPUTS",
-    "ERR_INJECTED_TIMEOUT", "STATUS_OK", "m_tile_for", "flush_l2",
+    "ERR_INJECTED_TIMEOUT", "STATUS_OK", "m_tile_for", "flush_l2", "GRID_CLUSTER",
 ]
 
 CUDA_SUCCESS = 0
@@ -112,25 +112,61 @@ class B200Config:
     def validate(self, m: int, n: int, k: int) -> Optional[str]:
         return self.plan(m, n, k).error
 
+    def max_active_clusters(self, m: int, n: int, k: int) -> int:
+        """Clusters of this plan's size the current GPU holds at once
+        (``dg_max_active_clusters``)."""
+        out = ctypes.c_int()
+        rc = _lib.lib().dg_max_active_clusters(ctypes.byref(self.to_dg()), m, n, k, ctypes.byref(out))
+        if rc != 0:
+            raise RuntimeError(f"dg_max_active_clusters failed: cudaError {rc}")
+        return out.value
+
     @property
     def prepacked(self) -> bool:
         return self.layout != LAYOUT_RAW
 
 
 def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool = True,
-                   independent_inputs: bool = False) -> B200Config:
+                   independent_inputs: bool = False, schedule: str = "cluster") -> B200Config:
     """The B200 schedule used by :func:`fp8_decode_gemm` and the benchmark.
 
-    256-row weight tiles (the widest tcgen05 N: 8 KiB of weights per MMA
-    instruction), two 128-K blocks per stage in a two-deep ring (64 KiB per
-    bulk copy; deeper rings measured no faster), and a stream-K grid of one
-    CTA per SM so every SM streams the same number of weight bytes whatever
-    the tile count.  `independent_inputs` sets FLAG_INDEPENDENT_INPUTS (see
+    Two 128-K blocks per stage in a two-deep ring (64 KiB per bulk copy at
+    256 rows; deeper rings measured no faster) and weight tiles on the
+    tcgen05 N side, 256 rows (8 KiB of weights per MMA instruction):
+
+    * ``schedule="cluster"`` (default): cluster split-K (``GRID_CLUSTER``):
+      each tile's K range split over the CTAs of one thread-block cluster,
+      reduced through distributed shared memory; the library picks the split
+      from the device's cluster occupancy (one wave of clusters: the most
+      SMs for dependent launches, 32 CTAs for independent inputs).  For a
+      large matrix under dependent launches, 224-row tiles when they let at
+      least 10% more SMs stream in one wave (7168 rows: 32 tiles x 4 = 128
+      CTAs instead of 28 x 4 = 112).  Falls back to stream-K where the
+      cluster plan does not apply.
+    * ``schedule="stream_k"``: a stream-K grid of one CTA per SM with the
+      workspace reduction.
+
+    `independent_inputs` sets FLAG_INDEPENDENT_INPUTS (see
     include/decode_gemm_b200.h).
     """
-    return B200Config(m_tile=m_tile_for(m), block_n=256, subs=2, stages=2, layout=layout, pdl=pdl,
-                      split_k=1, grid_ctas=-1,
-                      flags=FLAG_INDEPENDENT_INPUTS if independent_inputs else 0)
+    from dataclasses import replace
+    flags = FLAG_INDEPENDENT_INPUTS if independent_inputs else 0
+    stream_k = B200Config(m_tile=m_tile_for(m), block_n=256, subs=2, stages=2, layout=layout, pdl=pdl,
+                          split_k=1, grid_ctas=-1, flags=flags)
+    if schedule == "stream_k":
+        return stream_k
+    if schedule != "cluster":
+        raise ValueError("schedule must be 'cluster' or 'stream_k'")
+    base = replace(stream_k, grid_ctas=GRID_CLUSTER)
+    p256 = base.plan(m, n, k)
+    if p256.error is not None or p256.cluster < 2:
+        return stream_k
+    if not independent_inputs and n * k >= 512 * 1024 * p256.num_ctas:
+        alt = replace(base, block_n=224)
+        p224 = alt.plan(m, n, k)
+        if p224.error is None and p224.cluster >= 2 and p224.num_ctas * 10 >= p256.num_ctas * 11:
+            return alt
+    return base
 
 
 @dataclass(frozen=True)
@@ -376,6 +412,7 @@ class LaunchPlan:
     max_slabs: int = 1
     ws_floats: int = 0
     sem_ints: int = 0
+    cluster: int = 1
 
     @classmethod
     def _from_info(cls, info: DgPlanInfo) -> "LaunchPlan":
@@ -384,7 +421,8 @@ class LaunchPlan:
                    smem_bytes=info.smem_bytes, num_output_tiles=info.num_output_tiles,
                    padded_n=info.padded_n, error=err, stages=info.stages, n_mma=info.n_mma,
                    a_rows=info.a_rows, mma_m=info.mma_m, epi_warps=info.epi_warps, num_ctas=info.num_ctas,
-                   max_slabs=info.max_slabs, ws_floats=info.ws_floats, sem_ints=info.sem_ints)
+                   max_slabs=info.max_slabs, ws_floats=info.ws_floats, sem_ints=info.sem_ints,
+                   cluster=info.cluster)
 
 
 def _b200(cfg, p: Problem) -> B200Config:

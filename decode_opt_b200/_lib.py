@@ -13,11 +13,12 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libdecode_gemm_b200.so")
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 LAYOUT_RAW = 0
 LAYOUT_PACKED = 1
 LAYOUT_PACKED_SWIZZLED = 2
+GRID_CLUSTER = -2              # DG_GRID_CLUSTER
 
 FLAG_INJECT_TIMEOUT = 2
 FLAG_INDEPENDENT_INPUTS = 4
@@ -34,7 +35,7 @@ EXPORTED_SYMBOLS = (
     "dg_packed_weight_bytes", "dg_status_string", "dg_flush_l2", "dg_probe_bulk_stream",
     "dg_probe_naive_read", "dg_num_sms", "dg_launch_static_scratch", "dg_probe_mma",
     "dg_launch_gather", "dg_gather_wait", "dg_ipc_export", "dg_ipc_import", "dg_ipc_release",
-    "dg_quantize_act",
+    "dg_quantize_act", "dg_max_active_clusters",
 )
 
 
@@ -88,6 +89,7 @@ class DgPlanInfo(ctypes.Structure):
         ("max_slabs", ctypes.c_int),
         ("ws_floats", ctypes.c_ulonglong),
         ("sem_ints", ctypes.c_int),
+        ("cluster", ctypes.c_int),
         ("error", ctypes.c_char * 96),
     ]
 
@@ -127,6 +129,8 @@ def lib():
     probp = ctypes.POINTER(DgProblem)
     L.dg_abi_version.restype = ctypes.c_int
     L.dg_plan.argtypes = [cfgp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(DgPlanInfo)]
+    L.dg_max_active_clusters.argtypes = [cfgp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                         ctypes.POINTER(ctypes.c_int)]
     L.dg_make_weight_map.argtypes = [cfgp, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
     L.dg_make_activation_map.argtypes = [cfgp, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
     L.dg_launch_with_maps.argtypes = [cfgp, probp, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,

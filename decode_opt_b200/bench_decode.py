@@ -21,9 +21,18 @@ B200 step):
       kernel with the reference's schedule (one CTA per BM-row output tile,
       times the split-K factor); the ring depth WG*STG is reduced when it
       does not fit in shared memory (STAGES_SM100 in the config column);
-  6 b200_streamk
-      the B200 schedule: 256-row tiles, the descriptor-ready swizzled weight
-      layout, a stream-K grid of one CTA per SM, the early PDL trigger.
+  6 b200
+      the B200 schedule for dependent launches (``default_config``): cluster
+      split-K -- each tile's K range split over one thread-block cluster and
+      reduced through distributed shared memory, as many clusters as one
+      wave holds -- with the descriptor-ready swizzled weight layout and the
+      early PDL trigger; activations are read after griddepcontrol.wait;
+  7 b200_indep
+      the B200 schedule for independent inputs (FLAG_INDEPENDENT_INPUTS:
+      activations read before griddepcontrol.wait, writes after; fewer CTAs
+      per GEMM), under which back-to-back GEMMs of the PDL protocol stream
+      side by side -- the reference kernel, which never waits on the grid
+      dependency, is timed the same way.
 
 S5 turns 2-way split-K on where the reference's rule says it pays: M >= 8 and
 the tile count in [ceil(SMs/2), SMs) (bench/configs.cuh:398-406), with this
@@ -75,8 +84,9 @@ K_BLOCK = 128
 FP8_MAX = 448.0
 QUANT_EPS = 1.0e-4
 
-STEP_NAMES = ("baseline", "pdl", "blockk", "prepack", "tile_stage", "splitk", "b200_streamk")
+STEP_NAMES = ("baseline", "pdl", "blockk", "prepack", "tile_stage", "splitk", "b200", "b200_indep")
 STEP_B200 = 6
+STEP_B200_INDEP = 7
 PROTOCOLS = ("ISO", "B2B", "PDL")
 
 CSV_HEADER = ("model,N,K,M,m_tile,step,step_name,protocol,latency_us_p50,latency_us_p30,"
@@ -236,7 +246,7 @@ class Options:
 USAGE = """usage: python -m decode_opt_b200.bench_decode [options]
   --models all|id,...        model ids (default all; see --list)
   --models-json PATH         model table in the models.json schema
-  --steps all|0-6            ladder steps (0..5 the reference's, 6 the B200 schedule)
+  --steps all|0-7            ladder steps (0..5 the reference's, 6 and 7 the B200 schedule)
   --ms all|1,2,4,...         batch sizes in [1, 128] (default 1,2,4,8,16,32,64,128)
   --protocols ISO,B2B,PDL    protocols to time (default all three)
   --reps R                   repetitions (default 3)
@@ -286,7 +296,7 @@ def parse_args(argv: Sequence[str]) -> Options:
         if a == "--models":
             o.models = parse_csv_strings(need())
         elif a == "--steps":
-            o.steps = parse_int_ranges(need(), 0, 6)
+            o.steps = parse_int_ranges(need(), 0, 7)
         elif a == "--ms":
             o.ms = parse_int_ranges(need(), 1, 128)
         elif a == "--tune":
@@ -371,7 +381,7 @@ def parse_args(argv: Sequence[str]) -> Options:
         sys.stderr.write(f"[bench] unknown protocol(s): {','.join(bad)}\n")
         raise SystemExit(2)
     if not o.steps:
-        o.steps = list(range(0, 7))
+        o.steps = list(range(0, 8))
     if not o.ms:
         o.ms = [1, 2, 4, 8, 16, 32, 64, 128]
     if o.demo:
@@ -488,7 +498,7 @@ LAYOUT_NAMES = {0: "raw", 1: "packed", 2: "swizzled"}
 
 
 def b200_config_string(b: dict) -> str:
-    grid = {0: "tiles", -1: "streamk"}.get(b["grid_ctas"], str(b["grid_ctas"]))
+    grid = {0: "tiles", -1: "streamk", -2: "cluster"}.get(b["grid_ctas"], str(b["grid_ctas"]))
     s = (f"B200;M_TILE={b['m_tile']};BN={b['block_n']};SUBS={b['subs']};STAGES={b['stages']};"
          f"LAYOUT={LAYOUT_NAMES[b['layout']]};GRID={grid};PDL={int(b['pdl'])};SK={b['split_k']}")
     if b.get("flags", 0) & 4:
@@ -496,21 +506,23 @@ def b200_config_string(b: dict) -> str:
     return s
 
 
-def b200_step_config(m: int, n: int, k: int) -> dict:
-    """Step 6: the library's default schedule with the swizzled layout."""
+def b200_step_config(m: int, n: int, k: int, independent: bool = False) -> dict:
+    """Steps 6 and 7: the library's default schedule with the swizzled layout."""
     from . import LAYOUT_PACKED_SWIZZLED, default_config
-    return dict(default_config(m, n, k, layout=LAYOUT_PACKED_SWIZZLED, pdl=True).__dict__)
+    return dict(default_config(m, n, k, layout=LAYOUT_PACKED_SWIZZLED, pdl=True,
+                               independent_inputs=independent).__dict__)
 
 
 TUNE_BLOCK_N = (64, 128, 192, 256)
 TUNE_SUBS = (1, 2, 4)
 TUNE_STAGES = (2, 3, 4)
-TUNE_GRIDS = (0, -1)
+TUNE_GRIDS = (0, -1, -2)
 
 
 def tune_grid(m: int) -> List[dict]:
-    """The B200 tune grid: BN x SUBS x ring depth x schedule (reference tiles
-    or stream-K), swizzled layout, PDL trigger on.  It replaces the reference's
+    """The B200 tune grid: BN x SUBS x ring depth x schedule (reference tiles,
+    stream-K, or cluster split-K with the library's split), swizzled layout,
+    PDL trigger on.  It replaces the reference's
     SM90 grid (bench/configs.cuh:466-486), whose WG/REG/TILES knobs do not
     exist on the sm_100a kernel."""
     from . import LAYOUT_PACKED_SWIZZLED
@@ -1138,8 +1150,8 @@ class Session:
 
 def canonical_variants(step: int, m: int, n: int, k: int, sms: int) -> StepVariant:
     mt = m_tile_for(m)
-    if step == STEP_B200:
-        return StepVariant(step, mt, b200=b200_step_config(m, n, k))
+    if step in (STEP_B200, STEP_B200_INDEP):
+        return StepVariant(step, mt, b200=b200_step_config(m, n, k, independent=step == STEP_B200_INDEP))
     return StepVariant(step, mt, kernel_config=canonical_kernel_config(step, mt, n, k, m, sms))
 
 
@@ -1166,7 +1178,7 @@ def print_list(o: Options, models: Sequence[ModelShape], note: str, sms: int = 1
             for step in range(6):
                 kc = canonical_kernel_config(step, mt, m.N, m.K, mt, sms)
                 print(f"    S{step} {STEP_NAMES[step]:<11s} {config_string(kc)}")
-    print(f"tune grid: BN {TUNE_BLOCK_N} x SUBS {TUNE_SUBS} x STAGES {TUNE_STAGES} x GRID tiles/streamk = "
+    print(f"tune grid: BN {TUNE_BLOCK_N} x SUBS {TUNE_SUBS} x STAGES {TUNE_STAGES} x GRID tiles/streamk/cluster = "
           f"{len(TUNE_BLOCK_N) * len(TUNE_SUBS) * len(TUNE_STAGES) * len(TUNE_GRIDS)} configurations")
 
 

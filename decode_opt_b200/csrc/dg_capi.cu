@@ -61,13 +61,15 @@ struct KernelEntry {
   KernelFn fn;
   std::atomic<int> smem_high_water;
   cudaError_t pool_check;   // register pool covers the setmaxnreg split
+  std::atomic<int> nonportable_cluster;   // cudaFuncAttributeNonPortableClusterSizeAllowed set
 };
 
 template <int MMA_M, int COPIES, int EPW>
 KernelEntry* entry() {
   static KernelEntry e{dg::kernel_ptr<MMA_M, COPIES, EPW>(), {0},
                        dg::check_register_pool(reinterpret_cast<const void*>(dg::kernel_ptr<MMA_M, COPIES, EPW>()),
-                                               COPIES, EPW)};
+                                               COPIES, EPW),
+                       {0}};
   return &e;
 }
 
@@ -77,6 +79,60 @@ KernelEntry* select_kernel(int mma_m, int copies, int epw) {
   if (mma_m == 128 && copies == 2 && epw == 2) return entry<128, 2, 2>();
   if (mma_m == 128 && copies == 1 && epw == 2) return entry<128, 1, 2>();
   return nullptr;
+}
+
+// Cluster occupancy of the current device: occ[S] clusters of S CTAs at one
+// CTA per SM (every batch-class kernel holds an SM alone: its registers
+// exceed half the register file), from cudaOccupancyMaxActiveClusters, asked
+// once per device; the measured B200 table when no device answers.
+constexpr int kMaxOccDevices = 64;
+std::mutex g_occ_mutex;
+int g_occ[kMaxOccDevices][dg::kMaxClusterSplit + 1];
+bool g_occ_ready[kMaxOccDevices] = {};
+
+const int* device_cluster_occupancy() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxOccDevices) {
+    cudaGetLastError();
+    return dg::kB200ClusterOccupancy;
+  }
+  std::lock_guard<std::mutex> lock(g_occ_mutex);
+  if (g_occ_ready[dev]) return g_occ[dev];
+  KernelEntry* k = entry<64, 4, 1>();
+  const void* fn = reinterpret_cast<const void*>(k->fn);
+  bool ok = dg::ensure_smem(fn, dg::kMaxDynamicSmem, &k->smem_high_water) == cudaSuccess &&
+            cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+  if (ok) k->nonportable_cluster.store(1, std::memory_order_release);
+  g_occ[dev][0] = 0;
+  for (int S = 1; ok && S <= dg::kMaxClusterSplit; ++S) {
+    cudaLaunchConfig_t lc{};
+    cudaLaunchAttribute attr[1]{};
+    lc.gridDim = dim3(1u, static_cast<unsigned>(S), 1u);
+    lc.blockDim = dim3(static_cast<unsigned>(dg::block_threads(4, 1)), 1u, 1u);
+    lc.dynamicSmemBytes = dg::kMaxDynamicSmem;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = static_cast<unsigned>(S);
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    int n = 0;
+    ok = cudaOccupancyMaxActiveClusters(&n, fn, &lc) == cudaSuccess;
+    g_occ[dev][S] = n;
+  }
+  if (!ok) {
+    cudaGetLastError();
+    return dg::kB200ClusterOccupancy;
+  }
+  g_occ_ready[dev] = true;
+  return g_occ[dev];
+}
+
+// The plan every entry point launches: cluster split-K with split_k <= 1
+// takes its split from the device's cluster occupancy.
+Plan plan_for(const Config& c, int M, int N, int K) {
+  const bool ask = c.grid_ctas == dg::kGridCluster && c.split_k <= 1;
+  return dg::make_plan(c, M, N, K, current_sm_count(), ask ? device_cluster_occupancy() : dg::kB200ClusterOccupancy);
 }
 
 void fill_info(const Plan& plan, dg_plan_info* out) {
@@ -101,6 +157,7 @@ void fill_info(const Plan& plan, dg_plan_info* out) {
   out->max_slabs = plan.max_slabs;
   out->ws_floats = plan.ws_floats;
   out->sem_ints = plan.sem_ints;
+  out->cluster = plan.cluster;
 }
 
 // Fills the output copies and the fused-gather fields of `p` from `g`
@@ -133,7 +190,7 @@ int launch_impl(const dg_config* cfg, const dg_problem* prob, const CUtensorMap*
                 const CUtensorMap* a_map, cudaStream_t stream, bool pdl_attr, const dg_gather* g = nullptr) {
   if (cfg == nullptr || prob == nullptr) return cudaErrorInvalidValue;
   const Config c = to_config(cfg);
-  Plan plan = dg::make_plan(c, prob->M, prob->N, prob->K, current_sm_count());
+  Plan plan = plan_for(c, prob->M, prob->N, prob->K);
   if (plan.error != nullptr) return cudaErrorInvalidValue;
   dg::KernelParams& p = plan.params;
   p.output = static_cast<__nv_bfloat16*>(prob->output);
@@ -154,6 +211,12 @@ int launch_impl(const dg_config* cfg, const dg_problem* prob, const CUtensorMap*
   const cudaError_t attr_err =
       dg::ensure_smem(reinterpret_cast<const void*>(k->fn), plan.smem_bytes, &k->smem_high_water);
   if (attr_err != cudaSuccess) return attr_err;
+  if (plan.cluster > 8 && k->nonportable_cluster.load(std::memory_order_acquire) == 0) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(reinterpret_cast<const void*>(k->fn), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    k->nonportable_cluster.store(1, std::memory_order_release);
+  }
   return dg::launch_kernel(k->fn, plan, p, *w_map, *a_map, stream, pdl_attr);
 }
 
@@ -268,9 +331,37 @@ int dg_abi_version(void) { return DG_ABI_VERSION; }
 
 int dg_plan(const dg_config* cfg, int M, int N, int K, dg_plan_info* out) {
   if (cfg == nullptr || out == nullptr) return cudaErrorInvalidValue;
-  const Plan plan = dg::make_plan(to_config(cfg), M, N, K, current_sm_count());
+  const Plan plan = plan_for(to_config(cfg), M, N, K);
   fill_info(plan, out);
   return plan.error == nullptr ? 0 : static_cast<int>(cudaErrorInvalidValue);
+}
+
+int dg_max_active_clusters(const dg_config* cfg, int M, int N, int K, int* out) {
+  if (cfg == nullptr || out == nullptr) return cudaErrorInvalidValue;
+  *out = 0;
+  const Plan plan = plan_for(to_config(cfg), M, N, K);
+  if (plan.error != nullptr) return cudaErrorInvalidValue;
+  KernelEntry* k = select_kernel(plan.mma_m, plan.copies, plan.epw);
+  if (k == nullptr) return cudaErrorInvalidValue;
+  cudaError_t err = dg::ensure_smem(reinterpret_cast<const void*>(k->fn), plan.smem_bytes, &k->smem_high_water);
+  if (err != cudaSuccess) return err;
+  if (plan.cluster > 8 && k->nonportable_cluster.load(std::memory_order_acquire) == 0) {
+    err = cudaFuncSetAttribute(reinterpret_cast<const void*>(k->fn), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (err != cudaSuccess) return err;
+    k->nonportable_cluster.store(1, std::memory_order_release);
+  }
+  cudaLaunchConfig_t lc{};
+  cudaLaunchAttribute attr[1]{};
+  lc.gridDim = plan.grid;
+  lc.blockDim = plan.block;
+  lc.dynamicSmemBytes = plan.smem_bytes;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = static_cast<unsigned>(plan.cluster);
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  return cudaOccupancyMaxActiveClusters(out, reinterpret_cast<const void*>(k->fn), &lc);
 }
 
 int dg_make_weight_map(const dg_config* cfg, const void* weight, int N, int K, void* map128) {
@@ -315,7 +406,7 @@ int dg_launch_static_scratch(const dg_config* cfg, const dg_problem* p, void* st
   if (info != nullptr) std::memset(info, 0, sizeof(*info));
   if (cfg == nullptr || p == nullptr) return cudaErrorInvalidValue;
   const Config c = to_config(cfg);
-  const Plan plan = dg::make_plan(c, p->M, p->N, p->K, current_sm_count());
+  const Plan plan = plan_for(c, p->M, p->N, p->K);
   if (plan.error != nullptr) {
     if (info != nullptr) fill_info(plan, info);
     return cudaErrorInvalidValue;

@@ -40,13 +40,46 @@ struct Config {
   int stages = 0;         // smem ring depth; 0 = as many as fit
   int layout = kLayoutRaw;
   int pdl = 0;            // 1: trigger dependents + programmatic serialization
-  int split_k = 1;        // reference S (grid_ctas == 0 only): 1, 2, 4, 8, ...
+  int split_k = 1;        // reference S (grid_ctas == 0), or the cluster split
+                          // (grid_ctas == kGridCluster; 1 = choose)
   int grid_ctas = 0;      // 0: grid = tiles x split_k; > 0: stream-K over this
-                          // many CTAs; < 0: stream-K over one CTA per SM
+                          // many CTAs; -1: stream-K over one CTA per SM;
+                          // kGridCluster: cluster split-K
   int epi_warps = 0;      // informational; the tile width fixes the epilogue warps
   unsigned long long timeout_ns = 0;  // bounded-wait limit; 0 = 2 s
   int flags = 0;          // extra kernel flags (kFlagInjectTimeout: tests only)
 };
+
+// grid_ctas value selecting cluster split-K: grid (tiles, S), cluster
+// (1, S, 1), the tile's S partials reduced through distributed shared memory.
+constexpr int kGridCluster = -2;
+
+// Clusters of S CTAs (one CTA per SM) a B200 holds at once, S = 0..16, as
+// cudaOccupancyMaxActiveClusters reports on this pool's 148-SM parts: SMs
+// come in GPCs that a cluster may not straddle, so the count falls faster
+// than 148/S.  Used when no device can be asked.
+constexpr int kB200ClusterOccupancy[kMaxClusterSplit + 1] = {0,  148, 74, 45, 33, 26, 22, 15, 15,
+                                                             15, 11,  7,  7,  7,  7,  7,  7};
+
+// The planner's cluster split for T tiles of C chunks, given occ[S] = the
+// clusters of S CTAs that fit at once (portable sizes only, S <= 8; every
+// CTA gets a chunk, S <= C).  A grid that needs a second wave of clusters
+// measured 40-70% slower, so only one-wave splits are taken:
+//   dependent launches (each GEMM waits for the previous one before reading
+//   its activation): the largest S whose T clusters fit at once, i.e. as
+//   many SMs streaming as one wave allows;
+//   independent inputs (consecutive GEMMs may overlap): the smallest S that
+//   still gives 32 CTAs, so that more GEMMs stream side by side.
+// 1 (no split) when not even clusters of two fit in one wave.
+inline int choose_cluster_split(int T, int C, bool independent, const int* occ) {
+  const int s_max = std::min(8, C);
+  if (independent)
+    for (int s = 2; s <= s_max; ++s)
+      if (T <= occ[s] && static_cast<long long>(T) * s >= 32) return s;
+  for (int s = s_max; s >= 2; --s)
+    if (T <= occ[s]) return s;
+  return 1;
+}
 
 struct Plan {
   KernelParams params{};
@@ -61,6 +94,7 @@ struct Plan {
   size_t ws_floats = 0;     // max_slabs * M * N when max_slabs > 1
   int sem_ints = 0;         // num_tiles when max_slabs > 1
   int padded_n = 0;
+  int cluster = 1;          // CTAs per cluster along grid y (cluster split-K)
   const char* error = nullptr;
 };
 
@@ -112,7 +146,8 @@ inline const char* check_config(const Config& c) {
 
 // Full plan for one (M, N, K); `num_sms` sizes the stream-K grid when
 // grid_ctas < 0.  On failure plan.error names the violated rule.
-inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms) {
+inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms,
+                      const int* cluster_occupancy = kB200ClusterOccupancy) {
   Plan plan;
   if ((plan.error = check_config(c)) != nullptr) return plan;
   if (M < 1 || M > c.m_tile) return plan.error = "M out of [1, m_tile]", plan;
@@ -152,7 +187,23 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms) {
   if (smem_for(stages) > kMaxDynamicSmem) return plan.error = "dynamic shared memory exceeds 227 KiB", plan;
 
   long long G;
-  if (c.grid_ctas > 0) {
+  int cluster = 1;
+  if (c.grid_ctas == kGridCluster) {
+    const int S = c.split_k > 1 ? c.split_k
+                                : choose_cluster_split(T, C, (c.flags & kFlagIndependentInputs) != 0,
+                                                       cluster_occupancy);
+    if (S > kMaxClusterSplit) return plan.error = "cluster split: split_k must be <= 16", plan;
+    if (S > C) return plan.error = "cluster split: more splits than (K/128)/subs chunks", plan;
+    if (S > 1 && c.block_n % 32 != 0) return plan.error = "cluster split: block_n must be a multiple of 32", plan;
+    // The fp32 partial [M][block_n] goes to the drained pipeline ring.
+    if (S > 1 && static_cast<uint64_t>(M) * c.block_n * 4u >
+                     static_cast<uint64_t>(align1k(stages * w_stage + w_pad)) + align1k(stages * a_stage))
+      return plan.error = "cluster split: the M x block_n fp32 partial exceeds the pipeline's shared memory", plan;
+    G = static_cast<long long>(T) * S;
+    if (T > 0x7fffffff) return plan.error = "grid too large", plan;
+    plan.grid = dim3(static_cast<unsigned>(T), static_cast<unsigned>(S), 1u);
+    cluster = S;
+  } else if (c.grid_ctas > 0) {
     G = std::min<long long>(c.grid_ctas, U);
     plan.grid = dim3(static_cast<unsigned>(G), 1u, 1u);
   } else if (c.grid_ctas < 0) {
@@ -165,7 +216,7 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms) {
     plan.grid = dim3(static_cast<unsigned>(T), static_cast<unsigned>(c.split_k), 1u);
   }
   int max_slabs = 1;
-  for (int t = 0; t < T; ++t) {
+  for (int t = 0; cluster == 1 && t < T; ++t) {
     const long long first = cta_of_unit(static_cast<long long>(t) * C, G, U);
     const long long last = cta_of_unit(static_cast<long long>(t) * C + C - 1, G, U);
     max_slabs = std::max(max_slabs, static_cast<int>(last - first + 1));
@@ -189,8 +240,8 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms) {
   // Contributors of a split tile may wait (bounded) for one another only when
   // the whole grid fits on the device at once: one CTA per SM always fits.
   const bool coop = num_sms > 0 && G <= num_sms;
-  p.flags = (c.pdl ? kFlagPdlTrigger : 0) | (coop ? kFlagCoopReduce : 0) |
-            (c.flags & ~(kFlagPdlTrigger | kFlagCoopReduce));
+  p.flags = (c.pdl ? kFlagPdlTrigger : 0) | (coop ? kFlagCoopReduce : 0) | (cluster > 1 ? kFlagCluster : 0) |
+            (c.flags & ~(kFlagPdlTrigger | kFlagCoopReduce | kFlagCluster));
   p.total_units = U;
   p.w_stage_bytes = w_stage;
   p.a_stage_bytes = a_stage;
@@ -214,6 +265,7 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms) {
   plan.ws_floats = max_slabs > 1 ? static_cast<size_t>(max_slabs) * M * static_cast<size_t>(N) : 0;
   plan.sem_ints = max_slabs > 1 ? T : 0;
   plan.padded_n = T * c.block_n;
+  plan.cluster = cluster;
   return plan;
 }
 
@@ -344,7 +396,7 @@ inline cudaError_t check_buffers(const Plan& plan, const KernelParams& p) {
 inline cudaError_t launch_kernel(KernelFn fn, const Plan& plan, const KernelParams& p, const CUtensorMap& w,
                                  const CUtensorMap& a, cudaStream_t stream, bool pdl_attr) {
   cudaLaunchConfig_t cfg{};
-  cudaLaunchAttribute attr[1]{};
+  cudaLaunchAttribute attr[2]{};
   cfg.gridDim = plan.grid;
   cfg.blockDim = plan.block;
   cfg.dynamicSmemBytes = plan.smem_bytes;
@@ -352,9 +404,16 @@ inline cudaError_t launch_kernel(KernelFn fn, const Plan& plan, const KernelPara
   cfg.attrs = attr;
   cfg.numAttrs = 0;
   if (pdl_attr) {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.numAttrs = 1;
+    attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+    ++cfg.numAttrs;
+  }
+  if (plan.cluster > 1) {
+    attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+    attr[cfg.numAttrs].val.clusterDim.x = 1;
+    attr[cfg.numAttrs].val.clusterDim.y = static_cast<unsigned>(plan.cluster);
+    attr[cfg.numAttrs].val.clusterDim.z = 1;
+    ++cfg.numAttrs;
   }
   return cudaLaunchKernelEx(&cfg, fn, p, w, a);
 }

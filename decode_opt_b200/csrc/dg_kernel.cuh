@@ -53,6 +53,19 @@
 // (gridDim.y = S, kernels/decode_gemm.cuh:1015-1077) is the special case
 // G = tiles*S, where every range is one S-th of one tile.
 //
+// Cluster split-K (kFlagCluster).  The grid is (tiles, S) as in the
+// reference's split-K, and the S CTAs of a tile form one thread-block cluster
+// (cluster dims (1, S, 1)), so CTA s owns K range [s*C/S, (s+1)*C/S) of its
+// tile.  Each CTA writes its fp32 partial [M][BN] into its own shared memory
+// (the drained ring; float4 columns XOR-swizzled by row so that the rows of a
+// warp hit distinct banks); after one cluster barrier, cluster rank r sums
+// the r-th S-th of the tile's elements over the S partials, read through
+// distributed shared memory in rank order 0..S-1 (run-to-run bit-identical),
+// and stores bf16; a second cluster barrier keeps every CTA's partial alive
+// until all its readers are done.  No workspace, semaphore or global atomic:
+// the reduction never waits on L2, whose round trips take 1-2 us while the
+// GPU streams weights at full bandwidth.
+//
 // Programmatic dependent launch.  Weight tiles for the first ring pass are
 // requested before griddepcontrol.wait (weights are never written by a
 // preceding kernel); activation loads, scale reads and every global write
@@ -104,7 +117,13 @@ enum Flags : int {
   // Set by the planner when the whole grid can be resident at once: every
   // contributor of a split tile helps reduce it (bounded wait for the others).
   kFlagCoopReduce = 8,
+  // Cluster split-K (set by the planner): grid (tiles, S) with cluster
+  // (1, S, 1); the S CTAs of a tile reduce through distributed shared memory
+  // instead of the workspace.
+  kFlagCluster = 16,
 };
+
+constexpr int kMaxClusterSplit = 16;   // CTAs per cluster (above 8: non-portable size)
 
 // State word of a split tile (one int per tile, zero between launches):
 //   bits  0..9   contributors that have stored their slab (arrivals)
@@ -667,6 +686,69 @@ __device__ __noinline__ void reduce_split_tiles(const KernelParams& p, const int
   }
 }
 
+// Cluster split-K reduction of tile `tile` (kFlagCluster), run by the active
+// epilogue threads of every CTA of the tile's cluster between the two
+// cluster barriers.  `buf` is the shared::cta address of this CTA's partial
+// [M][block_n] fp32 (float4 column c4 of row m stored at c4 ^ (m & 7)); the
+// same offset holds each peer's.  Cluster rank r sums float4 units
+// [r*Q/S, (r+1)*Q/S) of the Q = M * ceil(bn_t/4) units, peers in rank order.
+__device__ __forceinline__ void cluster_reduce_tile(const KernelParams& p, uint32_t buf, int tile, int tid,
+                                                    int nthreads, bool out_vec) {
+  using namespace sm100;
+  const int S = static_cast<int>(gridDim.y);
+  const int r = static_cast<int>(cluster_ctarank());
+  const int bn = p.block_n;
+  const int bn_t = min(bn, p.N - tile * bn);
+  const int u4 = (bn_t + 3) / 4;
+  const long long q_all = static_cast<long long>(p.M) * u4;
+  const long long lo = r * q_all / S;
+  const long long hi = (r + 1) * q_all / S;
+  const int col_base = tile * bn;
+  for (long long u = lo + tid; u < hi; u += nthreads) {
+    const int m = static_cast<int>(u / u4);
+    const int c4 = static_cast<int>(u - static_cast<long long>(m) * u4);
+    const uint32_t off = buf + static_cast<uint32_t>((m * bn + 4 * (c4 ^ (m & 7))) * 4);
+    // Eight peers' loads in flight at a time, summed in rank order.
+    float4 tot = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int q0 = 0; q0 < kMaxClusterSplit; q0 += 8) {
+      if (q0 >= S) break;
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (q0 + j < S) v[j] = ld_shared_cluster_f4(map_shared_rank(off, static_cast<uint32_t>(q0 + j)));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (q0 + j >= S) continue;
+        if (q0 + j == 0) {
+          tot = v[j];
+        } else {
+          tot.x += v[j].x;
+          tot.y += v[j].y;
+          tot.z += v[j].z;
+          tot.w += v[j].w;
+        }
+      }
+    }
+    const int c = 4 * c4;
+    const int valid = min(4, bn_t - c);
+    const __nv_bfloat162 lo2 = __floats2bfloat162_rn(tot.x, tot.y);
+    const __nv_bfloat162 hi2 = __floats2bfloat162_rn(tot.z, tot.w);
+    for (int o = 0; o < p.n_outs; ++o) {
+      __nv_bfloat16* dst = p.outs[o] + static_cast<size_t>(m) * p.ldo + col_base + c;
+      if (out_vec && valid == 4) {
+        uint2 pk;
+        pk.x = *reinterpret_cast<const uint32_t*>(&lo2);
+        pk.y = *reinterpret_cast<const uint32_t*>(&hi2);
+        *reinterpret_cast<uint2*>(dst) = pk;
+      } else {
+        const __nv_bfloat16 e[4] = {lo2.x, lo2.y, hi2.x, hi2.y};
+        for (int j = 0; j < valid; ++j) dst[j] = e[j];
+      }
+    }
+  }
+}
+
 // Fused gather (tensor parallel, world > 1), run by thread 0 of every CTA
 // after the CTA's last output store.  Every output element was stored to all
 // world ranks' gathered buffers (peer memory mapped over NVLink).  Each CTA
@@ -916,6 +998,12 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
     }
     __syncwarp();
   }
+  // Control warps take part in the epilogue's two cluster barriers.
+  if (p.flags & kFlagCluster) {
+    __syncwarp();
+    cluster_sync_acq_rel();
+    cluster_sync_acq_rel();
+  }
   } else {
     // ======================================================== EPILOGUE ====
     if constexpr (Tr::kRegRealloc) regs_increase<kEpiRegs>();
@@ -1037,7 +1125,20 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         const long long c_last = cta_of_unit(tile_first + C - 1, G, U);
         const int contributors = static_cast<int>(c_last - c_first + 1);
         const int ncols = min(Tr::kColsPerWarp, min(bn - col0, N - n0));   // valid columns here
-        if (contributors == 1) {
+        if (p.flags & kFlagCluster) {
+          // This CTA's partial of its one tile -> its shared memory, reduced
+          // by the cluster after the loop.
+          if (row_ok && *abort_flag == 0) {
+            float* row = reinterpret_cast<float*>(w_region) + static_cast<size_t>(m) * bn;
+#pragma unroll
+            for (int j4 = 0; j4 < Tr::kColsPerWarp / 4; ++j4) {
+              const int c4 = (col0 >> 2) + j4;
+              if (4 * c4 < bn)
+                *reinterpret_cast<float4*>(row + 4 * (c4 ^ (m & 7))) =
+                    make_float4(partial[4 * j4], partial[4 * j4 + 1], partial[4 * j4 + 2], partial[4 * j4 + 3]);
+            }
+          }
+        } else if (contributors == 1) {
           if (leader) *wrote_output = 1;
           if (row_ok && *abort_flag == 0)
             for (int r = 0; r < p.n_outs; ++r)
@@ -1107,6 +1208,19 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         reduce_split_tiles<Tr::kRedGroups>(p, split_tile, split_contrib, n_split, completed, leader,
                                            active_tid, static_cast<int>(epi_threads), ws_vec, out_vec, smem,
                                            p.w_region_bytes + p.a_region_bytes, red_bar, red_mailbox, abort_flag);
+      if (p.flags & kFlagCluster) {
+        if (!waited) griddep_wait();   // a CTA without units still stores its share
+        cluster_sync_acq_rel();        // every partial of the tile is in place
+        if (*abort_flag == 0) {
+          if (leader) *wrote_output = 1;
+          cluster_reduce_tile(p, smem_addr(w_region), static_cast<int>(blockIdx.x), active_tid,
+                              static_cast<int>(epi_threads), out_vec);
+        }
+        cluster_sync_acq_rel();        // no peer reads this CTA's partial any more
+      }
+    } else if (p.flags & kFlagCluster) {
+      cluster_sync_acq_rel();
+      cluster_sync_acq_rel();
     }
   }
 

@@ -344,5 +344,34 @@ __device__ __forceinline__ void regs_decrease() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
 }
 
+// ------------------------------------------------- thread-block clusters --
+// Cluster-wide barrier: every thread of every CTA of the cluster arrives
+// (release: its earlier shared-memory writes become visible to the cluster)
+// and waits for all the others (acquire).  A hardware barrier: it completes
+// once every non-exited thread of the cluster has arrived.
+__device__ __forceinline__ void cluster_sync_acq_rel() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of offset `saddr` (a shared::cta address of
+// this CTA) in the shared memory of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t map_shared_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+  return d;
+}
+__device__ __forceinline__ float4 ld_shared_cluster_f4(uint32_t caddr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(caddr)
+               : "memory");
+  return v;
+}
+
 }  // namespace sm100
 }  // namespace dg

@@ -53,7 +53,7 @@
 extern "C" {
 #endif
 
-#define DG_ABI_VERSION 2
+#define DG_ABI_VERSION 3
 
 /* Weight layouts. */
 #define DG_LAYOUT_RAW 0             /* W[N,K], K contiguous (checkpoint layout) */
@@ -61,6 +61,9 @@ extern "C" {
                                        (the reference's prepack layout) */
 #define DG_LAYOUT_PACKED_SWIZZLED 2 /* same order, each 8-row group pre-swizzled for the
                                        tcgen05 SWIZZLE_128B operand layout (B200 native) */
+
+/* dg_config.grid_ctas value of the cluster split-K schedule (new). */
+#define DG_GRID_CLUSTER (-2)
 
 /* Kernel flags (dg_config.flags). */
 #define DG_FLAG_INJECT_TIMEOUT 2     /* tests: one wait can never complete, so the bounded
@@ -98,9 +101,13 @@ typedef struct dg_config {
   int pdl;       /* 1: griddepcontrol.launch_dependents once the first weight copies
                     are issued, and dg_launch sets programmatic stream serialization
                     (reference PDL)                                                      */
-  int split_k;   /* reference SPLITK_FACTOR S >= 1, used when grid_ctas == 0            */
+  int split_k;   /* reference SPLITK_FACTOR S >= 1 (grid_ctas == 0), or the cluster
+                    split (grid_ctas == DG_GRID_CLUSTER; 1 = as many as fit, <= 16)    */
   int grid_ctas; /* 0: grid = ceil(N/BM) x split_k (reference schedule);
-                    >0: stream-K over this many CTAs; <0: stream-K, one CTA per SM     */
+                    >0: stream-K over this many CTAs; -1: stream-K, one CTA per SM;
+                    DG_GRID_CLUSTER: cluster split-K (new): grid ceil(N/BM) x S,
+                    the S CTAs of a tile form a thread-block cluster and reduce
+                    through distributed shared memory -- no workspace          */
   int epi_warps; /* 0 (or the value block_n implies: 4 per 64 tile columns)            */
   int flags;     /* DG_FLAG_* (tests only)                                              */
   unsigned long long timeout_ns; /* bounded-wait limit per wait; 0 = 2 s               */
@@ -136,6 +143,7 @@ typedef struct dg_plan_info {
   int max_slabs;                   /* workspace slabs a split tile needs (1 = none) */
   unsigned long long ws_floats;    /* required splitk_ws size in floats             */
   int sem_ints;                    /* required splitk_sem size in ints              */
+  int cluster;                     /* CTAs per cluster along grid y (1 = none)      */
   char error[96];                  /* empty when usable                             */
 } dg_plan_info;
 
@@ -143,6 +151,12 @@ int dg_abi_version(void);
 
 /* Validates (cfg, M, N, K) and fills *out.  Returns 0, or 1 with out->error set. */
 int dg_plan(const dg_config* cfg, int M, int N, int K, dg_plan_info* out);
+
+/* (new) How many clusters of the plan's size (dg_plan_info.cluster) can be
+   resident on the current device at once, one CTA per SM
+   (cudaOccupancyMaxActiveClusters); grids of cluster split-K above that run
+   in more than one wave.  Returns a cudaError_t value. */
+int dg_max_active_clusters(const dg_config* cfg, int M, int N, int K, int* out);
 
 /* Encodes the tensor maps the kernel reads (opaque 128-byte CUtensorMap
    blobs).  The weight map is all zero for DG_LAYOUT_PACKED_SWIZZLED. */

@@ -78,8 +78,25 @@ def test_status_strings():
 
 
 @pytest.mark.parametrize("m", [1, 8, 16, 32, 64, 128])
+def test_default_plan_c2_cluster(m):
+    """Default schedule (no GPU: the measured B200 cluster occupancy): cluster
+    split-K, 224-row tiles x 4 K-splits = 128 CTAs in one wave for dependent
+    launches; 256-row tiles x 2 for independent inputs; no workspace."""
+    c = dg.default_config(m, 7168, 16384)
+    p = c.plan(m, 7168, 16384)
+    assert p.error is None and c.grid_ctas == dg.GRID_CLUSTER and c.block_n == 224
+    assert p.cluster == 4 and p.grid == (32, 4, 1) and p.num_ctas == 128 and p.n_mma == 224
+    assert p.ws_floats == 0 and p.sem_ints == 0 and p.max_slabs == 1
+    ci = dg.default_config(m, 7168, 16384, independent_inputs=True)
+    pi = ci.plan(m, 7168, 16384)
+    assert ci.block_n == 256 and pi.cluster == 2 and pi.num_ctas == 56
+    small = dg.default_config(m, 2048, 4096).plan(m, 2048, 4096)
+    assert small.cluster == 8 and small.num_ctas == 64
+
+
+@pytest.mark.parametrize("m", [1, 8, 16, 32, 64, 128])
 def test_default_plan_c2(m):
-    p = dg.default_config(m, 7168, 16384).plan(m, 7168, 16384)
+    p = dg.default_config(m, 7168, 16384, schedule="stream_k").plan(m, 7168, 16384)
     assert p.error is None
     # weights on the MMA N side (256 rows per tile), batch on M: 64 rows (4
     # copies of 16) up to M = 16, else 128 rows holding 4, 2 or 1 copies

@@ -11,7 +11,7 @@ from decode_opt_b200 import bench_decode as bd
 
 
 def test_parse_int_ranges():
-    assert bd.parse_int_ranges("all", 0, 6) == list(range(7))
+    assert bd.parse_int_ranges("all", 0, 7) == list(range(8))
     assert bd.parse_int_ranges("", 1, 3) == [1, 2, 3]
     assert bd.parse_int_ranges("0-3,5", 0, 6) == [0, 1, 2, 3, 5]
     assert bd.parse_int_ranges("3-1", 0, 6) == [1, 2, 3]
@@ -22,7 +22,7 @@ def test_parse_int_ranges():
 
 def test_parse_args_defaults_and_flags():
     o = bd.parse_args([])
-    assert o.steps == list(range(7)) and o.ms == [1, 2, 4, 8, 16, 32, 64, 128]
+    assert o.steps == list(range(8)) and o.ms == [1, 2, 4, 8, 16, 32, 64, 128]
     assert o.reps == 3 and o.iso_samples == 0 and o.b2b_batch == 0 and o.out_dir == "results"
     assert bd.wanted_protocols(o) == ["ISO", "B2B", "PDL"]
     o = bd.parse_args(["--protocols", "iso,pdl", "--models", "qwen36,glm52", "--ms", "1-4", "--reps", "0"])
@@ -106,7 +106,7 @@ def test_b200_config_string():
                flags=4, timeout_ns=0)
     assert bd.b200_config_string(cfg) == ("B200;M_TILE=8;BN=256;SUBS=2;STAGES=2;LAYOUT=swizzled;GRID=streamk;"
                                           "PDL=1;SK=1;ACT_EARLY=1")
-    assert len(bd.tune_grid(1)) == 72 and all(c["m_tile"] == 8 for c in bd.tune_grid(3))
+    assert len(bd.tune_grid(1)) == 108 and all(c["m_tile"] == 8 for c in bd.tune_grid(3))
 
 
 def test_number_formats_and_fields():
@@ -119,14 +119,14 @@ def test_number_formats_and_fields():
 
 
 def test_row_main_and_detail():
-    r = bd.CsvRow(model="deepseek_v4_pro", N=7168, K=16384, M=1, m_tile=8, step=6, step_name="b200_streamk",
+    r = bd.CsvRow(model="deepseek_v4_pro", N=7168, K=16384, M=1, m_tile=8, step=6, step_name="b200",
                   config="B200;BN=256", rel_l2=1.1e-3, passed="1", clocks_mhz=1965, reps=3, iso_samples=20,
                   b2b_batch=50, pdl_batch=50)
     r.fill_stats("PDL", bd.TimingStats(23.5, 23.4, 23.3, 23.45, 3))
     line = bd.row_main(r)
     f = line.split(",")
     assert bd.CSV_HEADER.count(",") + 1 == 16 == len(f)
-    assert f[:9] == ["deepseek_v4_pro", "7168", "16384", "1", "8", "6", "b200_streamk", "PDL", "23.5000"]
+    assert f[:9] == ["deepseek_v4_pro", "7168", "16384", "1", "8", "6", "b200", "PDL", "23.5000"]
     bw = (7168 * 16384 + 16384 + 2 * 7168) / 23.5e-6 / 1e9
     assert f[10] == f"{bw:.3f}" and f[11] == f"{bw / 8000.0:.6f}"
     assert f[12:] == ["1965", "1.100000e-03", "1", "B200;BN=256"]
@@ -214,5 +214,5 @@ def test_block_quantize_matches_formula():
 def test_list_runs_without_gpu(capsys):
     assert bd.main(["--list", "--models", "qwen36"]) == 0
     out = capsys.readouterr().out
-    assert "qwen36" in out and "S6 b200_streamk" in out and "72 configurations" in out
+    assert "qwen36" in out and "S6 b200" in out and "S7 b200_indep" in out and "108 configurations" in out
     assert bd.main(["--list", "--models", "nope"]) == 2

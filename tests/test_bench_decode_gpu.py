@@ -21,14 +21,14 @@ def _rows(path):
 
 def test_sweep_rows_pass_and_resume(tmp_path):
     out = str(tmp_path)
-    args = ["--models", "qwen36", "--ms", "1,8,128", "--steps", "0,3,5,6", "--reps", "2", "--iso-samples", "3",
+    args = ["--models", "qwen36", "--ms", "1,8,128", "--steps", "0,3,5,6,7", "--reps", "2", "--iso-samples", "3",
             "--b2b-batch", "6", "--out", out, "--splitk-factor-sweep", "--pdl-placement", "--check-launcher",
             "--weight-cache-gb", "3"]
     assert bd.main(args) == 0
     csv = bd.newest_csv(out, "bench_")
     header, rows = _rows(csv)
     assert header == bd.CSV_HEADER
-    assert len(rows) == 3 * 4 * 3
+    assert len(rows) == 3 * 5 * 3
     col = {h: i for i, h in enumerate(header.split(","))}
     for r in rows:
         assert r[col["pass"]] == "1", r
@@ -38,7 +38,8 @@ def test_sweep_rows_pass_and_resume(tmp_path):
         bw = float(r[col["bandwidth_gbps"]])
         assert bw == pytest.approx(bd.modeled_bytes(2048, 4096, int(r[col["M"]])) / (lat * 1e-6) / 1e9, rel=1e-3)
     assert {(r[col["step"]], r[col["step_name"]]) for r in rows} == {("0", "baseline"), ("3", "prepack"),
-                                                                     ("5", "splitk"), ("6", "b200_streamk")}
+                                                                     ("5", "splitk"), ("6", "b200"),
+                                                                     ("7", "b200_indep")}
     dh, drows = _rows(bd.detail_path_of(csv))
     assert dh == bd.DETAIL_HEADER and len(drows) == len(rows)
     dcol = {h: i for i, h in enumerate(dh.split(","))}
@@ -57,7 +58,7 @@ def test_sweep_rows_pass_and_resume(tmp_path):
     assert all(r[col["pass"]] == "1" for r in prows)
 
     # resume: every canonical row is already there, nothing is re-measured
-    assert bd.main(["--models", "qwen36", "--ms", "1,8,128", "--steps", "0,3,5,6", "--reps", "2",
+    assert bd.main(["--models", "qwen36", "--ms", "1,8,128", "--steps", "0,3,5,6,7", "--reps", "2",
                     "--iso-samples", "3", "--b2b-batch", "6", "--out", out, "--resume"]) == 0
     _, rows2 = _rows(csv)
     assert rows2 == rows
@@ -71,7 +72,7 @@ def test_tune_best_table(tmp_path):
     assert len(tune) == 1
     header, rows = _rows(os.path.join(out, tune[0]))
     assert header == bd.TUNE_BEST_HEADER
-    assert 1 <= len(rows) <= 72
+    assert 1 <= len(rows) <= 108
     ranks = [int(r[7]) for r in rows]
     assert ranks == list(range(1, len(rows) + 1)) and rows[0][8] == "1"
     lat = [float(r[10]) for r in rows]

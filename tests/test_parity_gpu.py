@@ -244,7 +244,7 @@ def test_split_workspace_layouts(m, ws_offset):
     a, as_ = oracle.gen_activation_smoke(m, k, 42 + m)
     ref = oracle.compute_reference(a, as_, w, ws, threads=8)
     dc = DeviceCase(w, ws, a, as_, n)
-    c = dg.default_config(m, n, k, layout=dg.LAYOUT_PACKED_SWIZZLED)
+    c = dg.default_config(m, n, k, layout=dg.LAYOUT_PACKED_SWIZZLED, schedule="stream_k")
     assert c.plan(m, n, k).max_slabs > 1
     first = None
     for _ in range(3):
@@ -312,17 +312,19 @@ def test_pdl_back_to_back_split_k_stays_correct():
     assert np.array_equal(final.view(np.uint32), got.view(np.uint32))
 
 
+@pytest.mark.parametrize("schedule", ["stream_k", "cluster"])
 @pytest.mark.parametrize("independent", [False, True])
-def test_pdl_back_to_back_stream_k_both_modes(independent):
-    """Back-to-back stream-K launches with programmatic serialization, with and
-    without FLAG_INDEPENDENT_INPUTS: correct, tickets clean, bit-identical."""
+def test_pdl_back_to_back_both_modes(independent, schedule):
+    """Back-to-back launches (stream-K and cluster split-K) with programmatic
+    serialization, with and without FLAG_INDEPENDENT_INPUTS: correct, tickets
+    clean, bit-identical."""
     import torch
     n, k, m = 2048, 4096, 2
     w, ws = oracle.gen_weight_smoke(n, k, 81)
     a, as_ = oracle.gen_activation_smoke(m, k, 82)
     ref = oracle.compute_reference(a, as_, w, ws)
     dc = DeviceCase(w, ws, a, as_, n)
-    c = dg.default_config(m, n, k, layout=dg.LAYOUT_RAW, independent_inputs=independent)
+    c = dg.default_config(m, n, k, layout=dg.LAYOUT_RAW, independent_inputs=independent, schedule=schedule)
     rc, got, status = dc.run(c)
     assert rc == 0 and status == 0
     assert check_against_oracle(got, ref)[0]

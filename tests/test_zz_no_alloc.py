@@ -61,7 +61,7 @@ def _close(got, want):
                                       (32, dg.LAYOUT_PACKED_SWIZZLED)])
 def test_static_scratch_matches_dg_launch_twice(m, layout):
     import torch
-    cfg = dg.default_config(m, N, K, layout=layout)
+    cfg = dg.default_config(m, N, K, layout=layout, schedule="stream_k")
     w_dev, w_s = _weight(layout)
     inputs = [_inputs(m, 100 + m), _inputs(m, 200 + m)]
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
@@ -88,7 +88,7 @@ def test_static_scratch_matches_dg_launch_twice(m, layout):
 def test_static_scratch_rejects_plans_over_the_limit():
     import torch
     m, n, k = 128, 7168, 16384
-    cfg = dg.default_config(m, n, k, layout=dg.LAYOUT_RAW)
+    cfg = dg.default_config(m, n, k, layout=dg.LAYOUT_RAW, schedule="stream_k")
     plan = cfg.plan(m, n, k)
     assert plan.error is None and plan.ws_floats > _lib.STATIC_WS_FLOATS
     act = torch.zeros(m, k, dtype=torch.uint8, device="cuda")
