@@ -138,13 +138,15 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
       each tile's K range split over the CTAs of one thread-block cluster,
       reduced through distributed shared memory; the library picks the split
       from the device's cluster occupancy (one wave of clusters: the most
-      SMs for dependent launches, 32 CTAs for independent inputs).  For a
-      large matrix under dependent launches, 224-row tiles when they let at
-      least 10% more SMs stream in one wave (7168 rows: 32 tiles x 4 = 128
-      CTAs instead of 28 x 4 = 112).  Falls back to stream-K where the
-      cluster plan does not apply.
+      SMs for dependent launches, 32 CTAs for independent inputs) and the
+      ring as deep as shared memory allows.  224-row tiles instead of 256
+      when 224 divides N and they allow a deeper ring (M <= 16: three 56 KiB
+      stages in flight instead of two of 64 KiB) or, for dependent launches
+      of a large matrix, at least 10% more CTAs in one wave (7168 rows:
+      32 x 4 = 128 CTAs instead of 28 x 4 = 112).  Falls back to stream-K
+      where the cluster plan does not apply.
     * ``schedule="stream_k"``: a stream-K grid of one CTA per SM with the
-      workspace reduction.
+      workspace reduction (two 64 KiB stages).
 
     `independent_inputs` sets FLAG_INDEPENDENT_INPUTS (see
     include/decode_gemm_b200.h).
@@ -157,15 +159,19 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
         return stream_k
     if schedule != "cluster":
         raise ValueError("schedule must be 'cluster' or 'stream_k'")
-    base = replace(stream_k, grid_ctas=GRID_CLUSTER)
+    base = replace(stream_k, grid_ctas=GRID_CLUSTER, stages=0)
     p256 = base.plan(m, n, k)
     if p256.error is not None or p256.cluster < 2:
         return stream_k
-    if not independent_inputs and n * k >= 512 * 1024 * p256.num_ctas:
+    if n % 224 == 0:
         alt = replace(base, block_n=224)
         p224 = alt.plan(m, n, k)
-        if p224.error is None and p224.cluster >= 2 and p224.num_ctas * 10 >= p256.num_ctas * 11:
-            return alt
+        if p224.error is None and p224.cluster >= 2:
+            deeper = p224.stages > p256.stages
+            wider = (not independent_inputs and n * k >= 512 * 1024 * p256.num_ctas
+                     and p224.num_ctas * 10 >= p256.num_ctas * 11)
+            if deeper or wider:
+                return alt
     return base
 
 

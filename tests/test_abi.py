@@ -81,15 +81,18 @@ def test_status_strings():
 def test_default_plan_c2_cluster(m):
     """Default schedule (no GPU: the measured B200 cluster occupancy): cluster
     split-K, 224-row tiles x 4 K-splits = 128 CTAs in one wave for dependent
-    launches; 256-row tiles x 2 for independent inputs; no workspace."""
+    launches; for independent inputs 2 K-splits, 224-row tiles where they
+    allow three ring stages (M <= 16), else 256; no workspace."""
     c = dg.default_config(m, 7168, 16384)
     p = c.plan(m, 7168, 16384)
     assert p.error is None and c.grid_ctas == dg.GRID_CLUSTER and c.block_n == 224
     assert p.cluster == 4 and p.grid == (32, 4, 1) and p.num_ctas == 128 and p.n_mma == 224
+    assert p.stages == (3 if m <= 16 else 2)
     assert p.ws_floats == 0 and p.sem_ints == 0 and p.max_slabs == 1
     ci = dg.default_config(m, 7168, 16384, independent_inputs=True)
     pi = ci.plan(m, 7168, 16384)
-    assert ci.block_n == 256 and pi.cluster == 2 and pi.num_ctas == 56
+    assert ci.block_n == (224 if m <= 16 else 256) and pi.cluster == 2
+    assert pi.num_ctas == (64 if m <= 16 else 56)
     small = dg.default_config(m, 2048, 4096).plan(m, 2048, 4096)
     assert small.cluster == 8 and small.num_ctas == 64
 
