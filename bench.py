@@ -383,8 +383,10 @@ def b200_arm(args, rank, world, local_rank):
         gs.launch(i, stream)
 
     def tp_step(i):
-        gs.launch(i, stream)
-        dist.all_gather_into_tensor(gathered, gs.out, group=pg)
+        # An NCCL collective between GEMMs serialises them: the dependent
+        # (latency) schedule is the best one for this baseline.
+        gs_dep.launch(i, stream)
+        dist.all_gather_into_tensor(gathered, gs_dep.out, group=pg)
 
     K = args.steps
     # ---- warm-up: eager launches, then every graph once (in timed()) ------------
@@ -441,9 +443,9 @@ def b200_arm(args, rank, world, local_rank):
         fused = dg_tp.FusedGather(m, n, device=dev)
         fdesc = [fused.descriptor(0), fused.descriptor(1)]
 
-        def fused_step(i):
-            rc = dg.launch_gather(gs.cfg, gs.probs[i % gs.nsets], fdesc[i % 2], gs.wmaps[i % gs.nsets], gs.amap,
-                                  stream, pdl_attr=gs.cfg.pdl)
+        def fused_step(i, setup=gs):
+            rc = dg.launch_gather(setup.cfg, setup.probs[i % setup.nsets], fdesc[i % 2],
+                                  setup.wmaps[i % setup.nsets], setup.amap, stream, pdl_attr=setup.cfg.pdl)
             if rc != 0:
                 raise RuntimeError(f"fused launch failed: cudaError {rc}")
         def fused_steps(i):
@@ -468,9 +470,18 @@ def b200_arm(args, rank, world, local_rank):
             t_s = timed(graphs)
             del graphs
 
+            cfg_sd = dg.default_config(m, n_s, k, layout=layout, pdl=pdl, independent_inputs=False)
+            gs_sd = gs_s if cfg_sd == cfg_s else GemmSetup(
+                Rotation(q_s, layout, cfg_sd.block_n, dev) if cfg_sd.block_n != cfg_s.block_n else rot_s,
+                cfg_sd, m, qx, wscale[: n_s // 128].contiguous(), ascale, dev)
+            with torch.cuda.stream(stream):
+                for i in range(3):
+                    gs_sd.launch(i, stream)
+            torch.cuda.synchronize(dev)
+
             def strong_tp(i):
-                gs_s.launch(i, stream)
-                dist.all_gather_into_tensor(gathered_s, gs_s.out, group=pg)
+                gs_sd.launch(i, stream)
+                dist.all_gather_into_tensor(gathered_s, gs_sd.out, group=pg)
             graphs = capture(strong_tp, K)
             t_s_tp = timed(graphs)
             del graphs
@@ -520,8 +531,8 @@ def b200_arm(args, rank, world, local_rank):
             qx_u8.copy_(hx, non_blocking=True)
             ascale.copy_(hs, non_blocking=True)
             if world > 1:
-                fused_step(i)
-                fused.wait(i % 2, stream=stream, status=gs.status)
+                fused_step(i, gs_dep)
+                fused.wait(i % 2, stream=stream, status=gs_dep.status)
                 hy.copy_(fused.output(i % 2, m), non_blocking=True)
             else:
                 gs_dep.launch(i, stream)
@@ -815,6 +826,9 @@ def main():
         import torch.distributed as dist
         backend = "nccl" if args.impl == "b200" else "gloo"
         if backend == "nccl":
+            # NCCL writes its debug lines (the version banner included) to
+            # stdout, which carries exactly one JSON line: send them to stderr.
+            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
             import torch
             torch.cuda.set_device(local_rank)
         dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120))
