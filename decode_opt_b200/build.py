@@ -5,6 +5,11 @@
 links the CUDA runtime statically and resolves ``cuTensorMapEncodeTiled``
 through the runtime's driver entry-point query, so it loads on hosts without a
 GPU (the CPU test suite checks its exported symbols there).
+
+It then compiles ``tests/cpp/dg_drop_in_check.cu`` against the C++ headers
+(``include/decode_gemm.cuh``, ``include/weight_prepack.cuh``) and the
+library into ``decode_opt_b200/dg_drop_in_check``, the program the GPU tests
+run to check the C++ interface.
 """
 
 from __future__ import annotations
@@ -20,6 +25,8 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB_NAME = "libdecode_gemm_b200.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
+DROP_IN_SRC = os.path.join(ROOT, "tests", "cpp", "dg_drop_in_check.cu")
+DROP_IN_BIN = os.path.join(HERE, "dg_drop_in_check")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 SOURCES = ("dg_capi.cu", "dg_probe.cu", "dg_quant.cu")
@@ -36,14 +43,34 @@ def _sources():
         os.path.join(INCLUDE, f) for f in sorted(os.listdir(INCLUDE))]
 
 
-def needs_build(target: str = LIB_PATH) -> bool:
+def needs_build(target: str = LIB_PATH, extra=()) -> bool:
     if not os.path.exists(target):
         return True
     t = os.path.getmtime(target)
-    return any(os.path.getmtime(s) > t for s in _sources())
+    return any(os.path.getmtime(s) > t for s in list(_sources()) + list(extra))
 
 
 def build(verbose: bool = False, ptxas_verbose: bool = False, force: bool = False) -> str:
+    lib = build_library(verbose, ptxas_verbose, force)
+    build_drop_in_check(verbose, force)
+    return lib
+
+
+def build_drop_in_check(verbose: bool = False, force: bool = False) -> str:
+    """The C++-interface check program, linked to the in-tree library (found
+    next to it at run time)."""
+    if not force and not needs_build(DROP_IN_BIN, (DROP_IN_SRC, LIB_PATH)):
+        return DROP_IN_BIN
+    cmd = [nvcc(), "-std=c++17", "-O3", "-lineinfo", *ARCH_FLAGS, "-I", INCLUDE, "-I", CSRC, DROP_IN_SRC,
+           "-o", DROP_IN_BIN + ".tmp", "-L", HERE, "-ldecode_gemm_b200", "-Xlinker", "-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(DROP_IN_BIN + ".tmp", DROP_IN_BIN)
+    return DROP_IN_BIN
+
+
+def build_library(verbose: bool = False, ptxas_verbose: bool = False, force: bool = False) -> str:
     if not force and not needs_build():
         return LIB_PATH
     cmd = [nvcc(), "-std=c++17", "-O3", "-lineinfo", *ARCH_FLAGS,

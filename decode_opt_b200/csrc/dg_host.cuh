@@ -71,8 +71,8 @@ constexpr int kB200ClusterOccupancy[kMaxClusterSplit + 1] = {0,  148, 74, 45, 33
 //   independent inputs (consecutive GEMMs may overlap): the smallest S that
 //   still gives 32 CTAs, so that more GEMMs stream side by side.
 // 1 (no split) when not even clusters of two fit in one wave.
-inline int choose_cluster_split(int T, int C, bool independent, const int* occ) {
-  const int s_max = std::min(8, C);
+__host__ __device__ inline int choose_cluster_split(int T, int C, bool independent, const int* occ) {
+  const int s_max = C < 8 ? C : 8;
   if (independent)
     for (int s = 2; s <= s_max; ++s)
       if (T <= occ[s] && static_cast<long long>(T) * s >= 32) return s;
@@ -111,27 +111,44 @@ struct BatchClass {
   int epw;
 };
 
-inline BatchClass batch_class_for(int M) {
+__host__ __device__ inline BatchClass batch_class_for(int M) {
   if (M <= 16) return {64, 4, 1};
   if (M <= 32) return {128, 4, 1};
   if (M <= 64) return {128, 2, 2};
   return {128, 1, 2};
 }
 
-inline int mma_m_for(int M) { return batch_class_for(M).mma_m; }
+__host__ __device__ inline int mma_m_for(int M) { return batch_class_for(M).mma_m; }
 
 constexpr int kAccumBuffers = 2;
 
-inline int padded_n(int n, int block_n) { return ((n + block_n - 1) / block_n) * block_n; }
+__host__ __device__ inline int padded_n(int n, int block_n) { return ((n + block_n - 1) / block_n) * block_n; }
 
 inline size_t packed_weight_bytes(int n, int k, int block_n) {
   return static_cast<size_t>(padded_n(n, block_n)) * static_cast<size_t>(k);
 }
 
-inline uint32_t align1k(uint32_t v) { return (v + 1023u) & ~1023u; }
+__host__ __device__ constexpr uint32_t align1k(uint32_t v) { return (v + 1023u) & ~1023u; }
+
+// Dynamic shared memory of a plan: 1 KiB alignment slack, the weight ring
+// (stages x subs x block_n x 128 bytes, plus the MMA's read-ahead pad when
+// block_n is not a multiple of 16), the activation ring (stages x subs x
+// MMA-M rows x 128 bytes) and the barrier block.
+__host__ __device__ constexpr uint32_t pipeline_smem_bytes(int stages, int subs, int block_n, int mma_m) {
+  return 1024u +
+         align1k(static_cast<uint32_t>(stages * subs * block_n * kKBlock + (((block_n + 15) / 16) * 16 - block_n) * kKBlock)) +
+         align1k(static_cast<uint32_t>(stages * subs * mma_m * kKBlock)) + SmemBarriers::bytes(stages, kAccumBuffers);
+}
+
+// The deepest ring up to `desired` stages (at least 1) that fits 227 KiB.
+__host__ __device__ constexpr int fitted_stages(int desired, int subs, int block_n, int mma_m) {
+  int s = desired > kMaxStages ? kMaxStages : (desired < 1 ? 1 : desired);
+  while (s > 1 && pipeline_smem_bytes(s, subs, block_n, mma_m) > kMaxDynamicSmem) --s;
+  return s;
+}
 
 // Static configuration checks (no shape).
-inline const char* check_config(const Config& c) {
+__host__ __device__ inline const char* check_config(const Config& c) {
   if (!(c.m_tile == 8 || c.m_tile == 16 || c.m_tile == 32 || c.m_tile == 64 || c.m_tile == 128))
     return "m_tile must be 8, 16, 32, 64 or 128";
   if (c.block_n < 8 || c.block_n > 256 || c.block_n % 8 != 0)
@@ -145,9 +162,14 @@ inline const char* check_config(const Config& c) {
 }
 
 // Full plan for one (M, N, K); `num_sms` sizes the stream-K grid when
-// grid_ctas < 0.  On failure plan.error names the violated rule.
-inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms,
-                      const int* cluster_occupancy = kB200ClusterOccupancy) {
+// grid_ctas < 0; `cluster_occupancy` (clusters of S CTAs that fit at once,
+// S = 0..16) chooses the cluster split when split_k <= 1 -- null: the
+// measured B200 table on the host (device code must give split_k).  Host
+// and device code compute the same plan (the header-only kernel entry
+// rebuilds it on the device).  On failure plan.error names the violated
+// rule.
+__host__ __device__ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms,
+                                          const int* cluster_occupancy = nullptr) {
   Plan plan;
   if ((plan.error = check_config(c)) != nullptr) return plan;
   if (M < 1 || M > c.m_tile) return plan.error = "M out of [1, m_tile]", plan;
@@ -160,7 +182,9 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms,
   const long long U = static_cast<long long>(T) * C;
   if (U > (1ll << 40)) return plan.error = "problem too large", plan;
 
-  const BatchClass bc = batch_class_for(M);
+  // kFlagClassFromMTile: the class of m_tile rather than of M (the C++
+  // header's kernel entry is compiled for its KernelConfig's M_TILE).
+  const BatchClass bc = batch_class_for((c.flags & kFlagClassFromMTile) ? c.m_tile : M);
   const int mma_m = bc.mma_m;
   const int epw = bc.epw;
   const int copies = bc.copies;
@@ -175,10 +199,8 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms,
   // loaded come from the next block or this tail pad and only feed output
   // columns that are never stored.
   const uint32_t w_pad = static_cast<uint32_t>((n_mma - c.block_n) * kKBlock);
-  auto smem_for = [&](int stages) -> uint32_t {
-    return 1024u + align1k(stages * w_stage + w_pad) + align1k(stages * a_stage) +
-           SmemBarriers::bytes(stages, bufs);
-  };
+  (void)bufs;
+  auto smem_for = [&](int stages) -> uint32_t { return pipeline_smem_bytes(stages, c.subs, c.block_n, mma_m); };
   int stages = c.stages;
   if (stages == 0) {
     stages = 1;
@@ -189,9 +211,14 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms,
   long long G;
   int cluster = 1;
   if (c.grid_ctas == kGridCluster) {
+#if defined(__CUDA_ARCH__)
+    const int* occ = cluster_occupancy;
+#else
+    const int* occ = cluster_occupancy != nullptr ? cluster_occupancy : kB200ClusterOccupancy;
+#endif
+    if (c.split_k <= 1 && occ == nullptr) return plan.error = "cluster split: give split_k", plan;
     const int S = c.split_k > 1 ? c.split_k
-                                : choose_cluster_split(T, C, (c.flags & kFlagIndependentInputs) != 0,
-                                                       cluster_occupancy);
+                                : choose_cluster_split(T, C, (c.flags & kFlagIndependentInputs) != 0, occ);
     if (S > kMaxClusterSplit) return plan.error = "cluster split: split_k must be <= 16", plan;
     if (S > C) return plan.error = "cluster split: more splits than (K/128)/subs chunks", plan;
     if (S > 1 && c.block_n % 32 != 0) return plan.error = "cluster split: block_n must be a multiple of 32", plan;
@@ -204,10 +231,11 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms,
     plan.grid = dim3(static_cast<unsigned>(T), static_cast<unsigned>(S), 1u);
     cluster = S;
   } else if (c.grid_ctas > 0) {
-    G = std::min<long long>(c.grid_ctas, U);
+    G = c.grid_ctas < U ? c.grid_ctas : U;
     plan.grid = dim3(static_cast<unsigned>(G), 1u, 1u);
   } else if (c.grid_ctas < 0) {
-    G = std::min<long long>(num_sms > 0 ? num_sms : 148, U);
+    const long long sms = num_sms > 0 ? num_sms : 148;
+    G = sms < U ? sms : U;
     plan.grid = dim3(static_cast<unsigned>(G), 1u, 1u);
   } else {
     if (C % c.split_k != 0) return plan.error = "split-K: (K/128)/subs must be a multiple of split_k", plan;
@@ -215,11 +243,13 @@ inline Plan make_plan(const Config& c, int M, int N, int K, int num_sms,
     if (T > 0x7fffffff || c.split_k > 65535) return plan.error = "grid too large", plan;
     plan.grid = dim3(static_cast<unsigned>(T), static_cast<unsigned>(c.split_k), 1u);
   }
-  int max_slabs = 1;
-  for (int t = 0; cluster == 1 && t < T; ++t) {
+  // Slabs of a split tile: the reference schedule gives every tile exactly
+  // split_k contributors (C % split_k == 0); stream-K counts them.
+  int max_slabs = (cluster == 1 && c.grid_ctas == 0) ? c.split_k : 1;
+  for (int t = 0; cluster == 1 && c.grid_ctas != 0 && t < T; ++t) {
     const long long first = cta_of_unit(static_cast<long long>(t) * C, G, U);
     const long long last = cta_of_unit(static_cast<long long>(t) * C + C - 1, G, U);
-    max_slabs = std::max(max_slabs, static_cast<int>(last - first + 1));
+    max_slabs = max_slabs > static_cast<int>(last - first + 1) ? max_slabs : static_cast<int>(last - first + 1);
   }
   if (max_slabs > kMaxContributors) return plan.error = "split too fine: more than 1023 CTAs share one tile", plan;
 

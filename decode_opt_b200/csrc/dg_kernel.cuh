@@ -121,6 +121,8 @@ enum Flags : int {
   // (1, S, 1); the S CTAs of a tile reduce through distributed shared memory
   // instead of the workspace.
   kFlagCluster = 16,
+  // Host planning only: take the batch class from m_tile instead of M.
+  kFlagClassFromMTile = 32,
 };
 
 constexpr int kMaxClusterSplit = 16;   // CTAs per cluster (above 8: non-portable size)
