@@ -768,7 +768,8 @@ __device__ __forceinline__ void cluster_reduce_tile(const KernelParams& p, uint3
 // recorded an error publishes nothing, so its peers' waits run out and
 // report it too.  The done count and the epoch are touched only after the
 // previous grid on the stream has completed (griddepcontrol.wait first).
-__device__ __noinline__ void gather_complete(const KernelParams& p, bool wrote_output) {
+// inline: one definition however many translation units include this header.
+__device__ __noinline__ inline void gather_complete(const KernelParams& p, bool wrote_output) {
   using namespace sm100;
   griddep_wait();
   if (wrote_output) fence_acq_rel_sys();   // this CTA's peer stores before its count

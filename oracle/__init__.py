@@ -48,7 +48,7 @@ def smoke_act_seed(shape_seed: int, m: int) -> int:
 
 def build() -> None:
     """Compile liboracle.so (and the reference build when its source exists)."""
-    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    subprocess.run(["make", "-s", "-j", str(max(1, min(8, os.cpu_count() or 1))), "-C", _HERE], check=True)
 
 
 def _ptr(a: np.ndarray, t):
