@@ -75,7 +75,7 @@ KernelEntry* entry() {
 
 KernelEntry* select_kernel(int mma_m, int copies, int epw) {
   if (mma_m == 64 && copies == 4 && epw == 1) return entry<64, 4, 1>();
-  if (mma_m == 128 && copies == 4 && epw == 1) return entry<128, 4, 1>();
+  if (mma_m == 64 && copies == 2 && epw == 2) return entry<64, 2, 2>();
   if (mma_m == 128 && copies == 2 && epw == 2) return entry<128, 2, 2>();
   if (mma_m == 128 && copies == 1 && epw == 2) return entry<128, 1, 2>();
   return nullptr;

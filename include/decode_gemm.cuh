@@ -23,7 +23,7 @@
 // shared memory gets the C ABI's results bit for bit.
 //
 // Mapping of the reference's configuration (B200 semantics):
-//   M_TILE              batch class of the kernel (MMA M 64 for 8/16, else 128)
+//   M_TILE              batch class of the kernel (MMA M 64 up to 32, else 128)
 //   OUTPUT_ROWS_PER_CTA weight rows per tile, the MMA's N side: multiple of 8
 //                       in [8, 256] (the reference allows <= 64)
 //   SUBS_PER_STAGE      128-K blocks per pipeline stage: 1, 2 or 4
@@ -70,7 +70,7 @@ namespace detail {
 template <int M_TILE> struct ClassOf;
 template <> struct ClassOf<8> { using type = dg::KernelTraits<64, 4, 1>; };
 template <> struct ClassOf<16> { using type = dg::KernelTraits<64, 4, 1>; };
-template <> struct ClassOf<32> { using type = dg::KernelTraits<128, 4, 1>; };
+template <> struct ClassOf<32> { using type = dg::KernelTraits<64, 2, 2>; };
 template <> struct ClassOf<64> { using type = dg::KernelTraits<128, 2, 2>; };
 template <> struct ClassOf<128> { using type = dg::KernelTraits<128, 1, 2>; };
 

@@ -74,8 +74,9 @@ extern "C" {
                                         dependent launch they are read before
                                         griddepcontrol.wait; global writes still wait */
 #define DG_FLAG_CLASS_FROM_M_TILE 32 /* the kernel instantiation follows cfg.m_tile
-                                        instead of M (8/16: MMA M 64; 32, 64, 128:
-                                        MMA M 128 with 4, 2, 1 batch copies), as the
+                                        instead of M (8/16, 32: MMA M 64 with 4, 2
+                                        batch copies; 64, 128: MMA M 128 with 2, 1),
+                                        as the
                                         C++ header's fp8_decode_gemm<Cfg> is compiled */
 
 /* Device status codes written to dg_problem.status (first error wins). */

@@ -82,17 +82,17 @@ def test_default_plan_c2_cluster(m):
     """Default schedule (no GPU: the measured B200 cluster occupancy): cluster
     split-K, 224-row tiles x 4 K-splits = 128 CTAs in one wave for dependent
     launches; for independent inputs 2 K-splits, 224-row tiles where they
-    allow three ring stages (M <= 16), else 256; no workspace."""
+    allow three ring stages (M <= 32, MMA M 64), else 256; no workspace."""
     c = dg.default_config(m, 7168, 16384)
     p = c.plan(m, 7168, 16384)
     assert p.error is None and c.grid_ctas == dg.GRID_CLUSTER and c.block_n == 224
     assert p.cluster == 4 and p.grid == (32, 4, 1) and p.num_ctas == 128 and p.n_mma == 224
-    assert p.stages == (3 if m <= 16 else 2)
+    assert p.stages == (3 if m <= 32 else 2)
     assert p.ws_floats == 0 and p.sem_ints == 0 and p.max_slabs == 1
     ci = dg.default_config(m, 7168, 16384, independent_inputs=True)
     pi = ci.plan(m, 7168, 16384)
-    assert ci.block_n == (224 if m <= 16 else 256) and pi.cluster == 2
-    assert pi.num_ctas == (64 if m <= 16 else 56)
+    assert ci.block_n == (224 if m <= 32 else 256) and pi.cluster == 2
+    assert pi.num_ctas == (64 if m <= 32 else 56)
     small = dg.default_config(m, 2048, 4096).plan(m, 2048, 4096)
     assert small.cluster == 8 and small.num_ctas == 64
 
@@ -102,10 +102,10 @@ def test_default_plan_c2(m):
     p = dg.default_config(m, 7168, 16384, schedule="stream_k").plan(m, 7168, 16384)
     assert p.error is None
     # weights on the MMA N side (256 rows per tile), batch on M: 64 rows (4
-    # copies of 16) up to M = 16, else 128 rows holding 4, 2 or 1 copies
-    assert p.mma_m == (64 if m <= 16 else 128) and p.n_mma == 256 and p.num_output_tiles == 28
-    assert p.block[0] == {1: 192, 8: 192, 16: 192, 32: 192, 64: 320, 128: 384}[m]
-    assert p.epi_warps == {1: 4, 8: 4, 16: 4, 32: 4, 64: 8, 128: 8}[m]
+    # copies of 16 or 2 of 32) up to M = 32, else 128 rows (2 copies of 64, 1)
+    assert p.mma_m == (64 if m <= 32 else 128) and p.n_mma == 256 and p.num_output_tiles == 28
+    assert p.block[0] == {1: 192, 8: 192, 16: 192, 32: 320, 64: 320, 128: 384}[m]
+    assert p.epi_warps == {1: 4, 8: 4, 16: 4, 32: 8, 64: 8, 128: 8}[m]
     assert p.a_rows == -(-m // 8) * 8
     assert p.smem_bytes <= 227 * 1024
     assert p.grid[0] == 148 or p.grid[0] > 0
