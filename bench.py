@@ -21,9 +21,11 @@ output slices, and the strong-scaling layer (the single N x K matrix
 N-sharded g ways, with and without the gather).
 
 Metric: algorithmic bytes (N*K + M*K + 2*M*N) per GEMM / time, GB/s, and
-us per GEMM.  `e2e` repeats the measurement through the public API with the
-step's activation and scales copied in from pinned host memory and the
-output copied back, inside the timed region.
+us per GEMM.  `e2e` repeats the measurement through the public API with
+every step's activation and scales copied in from pinned host memory and its
+output copied back, inside the timed region: a serving loop with
+--e2e-depth requests in flight (one stream each, captured in CUDA graphs),
+and beside it one request at a time on one stream.
 
 `--impl reference` times the reference's own CPU implementation of the path
 (the host scalar GEMM of kernels/smoke_test.cu, compiled from the reference
@@ -66,6 +68,9 @@ def parse_args():
                          "the previous grid before reading its activation (a layer chain). Both are "
                          "timed; this picks the headline.")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-depth", type=int, default=4, help="requests in flight in the e2e loop (1 GPU)")
+    ap.add_argument("--e2e-schedule", choices=["independent", "dependent"], default="independent",
+                    help="schedule of the e2e loop's GEMMs (they do not feed each other)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU work the rank-0 cpu_baseline sample is sized to")
@@ -543,21 +548,73 @@ def b200_arm(args, rank, world, local_rank):
                 gs_e2e.launch(i, stream)
                 hy.copy_(gs_e2e.out, non_blocking=True)
 
-        with torch.cuda.stream(stream):
-            for i in range(3):
-                e2e_step(i)
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for i in range(K):
-                e2e_step(i)
-            e1.record(stream)
-        torch.cuda.synchronize(dev)
-        te = device_max(e0.elapsed_time(e1) / 1e3)
+        def timed_serial(steps):
+            with torch.cuda.stream(stream):
+                for i in range(3):
+                    e2e_step(i)
+            torch.cuda.synchronize(dev)
+            if world > 1:
+                dist.barrier()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                e0.record(stream)
+                for i in range(steps):
+                    e2e_step(i)
+                e1.record(stream)
+            torch.cuda.synchronize(dev)
+            return device_max(e0.elapsed_time(e1) / 1e3)
+
+        pipe = None
+        if world == 1:
+            # A serving loop keeps `depth` requests in flight: request i runs
+            # on stream i % depth with that slot's own device input, output and
+            # pinned host output -- its H2D copy, GEMM and D2H copy in stream
+            # order -- so one request's copies overlap the others' GEMMs.  The
+            # GEMMs do not feed each other: the independent-inputs schedule.
+            depth = max(1, args.e2e_depth)
+            cfg_p = dg.default_config(m, n, k, layout=layout, pdl=pdl,
+                                      independent_inputs=args.e2e_schedule == "independent")
+            slots = []
+            for _ in range(depth):
+                d_in = torch.empty(in_bytes, dtype=torch.uint8, device=dev)
+                g_p = GemmSetup(rotation(cfg_p.block_n), cfg_p, m, d_in[: m * k].view(m, k), wscale,
+                                d_in[m * k:].view(torch.float32).view(m, kb), dev)
+                slots.append((d_in, g_p, torch.empty((m, n), dtype=torch.bfloat16).pin_memory(),
+                              torch.cuda.Stream(device=dev)))
+
+            def pipe_step(i):
+                d_in, g_p, h_out, st = slots[i % depth]
+                with torch.cuda.stream(st):
+                    d_in.copy_(hin, non_blocking=True)
+                    g_p.launch(i, st)
+                    h_out.copy_(g_p.out, non_blocking=True)
+
+            for i in range(3 * depth):
+                pipe_step(i)
+            torch.cuda.synchronize(dev)
+            # The loop is captured in CUDA graphs (graph_chunk requests each,
+            # forked to the slot streams and joined back), as a decode server
+            # replays its step: the copy nodes still move every request's
+            # bytes over PCIe at replay time, but no Python runs per request.
+            graphs = []
+            with torch.cuda.stream(stream):
+                for base in range(0, K, args.graph_chunk):
+                    gr = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gr, stream=stream):
+                        for _, _, _, st in slots:
+                            st.wait_stream(stream)
+                        for i in range(base, min(K, base + args.graph_chunk)):
+                            pipe_step(i)
+                        for _, _, _, st in slots:
+                            stream.wait_stream(st)
+                    graphs.append(gr)
+            t_pipe = timed(graphs)
+            del graphs
+            pipe = {"t": t_pipe, "depth": depth, "cfg": cfg_p,
+                    "plan": slots[0][1].plan, "outs": [sl[2] for sl in slots], "setups": [sl[1] for sl in slots]}
+
+        te_serial = timed_serial(K)
         gs.check_status()
         gs_e2e.check_status()
         e2e_ok = True
@@ -566,18 +623,29 @@ def b200_arm(args, rank, world, local_rank):
             with torch.cuda.stream(stream):
                 gs_dep.launch(0, stream)
             torch.cuda.synchronize(dev)
-            e2e_ok = bool(torch.equal(hy.view(torch.int16), gs_dep.out.cpu().view(torch.int16)))
+            want = gs_dep.out.cpu().view(torch.int16)
+            e2e_ok = bool(torch.equal(hy.view(torch.int16), want))
+            for h_out, g_p in zip(pipe["outs"], pipe["setups"]):
+                g_p.check_status()
+                e2e_ok = e2e_ok and bool(torch.equal(h_out.view(torch.int16), want))
+        te = pipe["t"] if pipe is not None else te_serial
+        sched = pipe["plan"] if pipe is not None else gs_e2e.plan
         e2e = {"value": byt_job / (te / K) / 1e9, "unit": "GB/s",
                "output_matches_device_path": e2e_ok,
                "h2d_bytes_per_step": int(hin.numel()),
                "d2h_bytes_per_step": int(hy.numel() * 2),
                "us_per_step": te / K * 1e6,
-               "schedule": {"block_n": gs_e2e.cfg.block_n, "grid": list(gs_e2e.plan.grid),
-                            "cluster": gs_e2e.plan.cluster, "pdl_mode": "dependent"},
+               "requests_in_flight": pipe["depth"] if pipe is not None else 1,
+               "serial": {"us_per_step": te_serial / K * 1e6,
+                          "note": "one request at a time on one stream, dependent schedule"},
+               "schedule": {"block_n": (pipe["cfg"] if pipe is not None else gs_e2e.cfg).block_n,
+                            "grid": list(sched.grid), "cluster": sched.cluster,
+                            "pdl_mode": args.e2e_schedule if pipe is not None else "dependent"},
                "path": "one pinned H2D copy of activation + scales, "
                        + ("dg.launch_gather (GEMM with the fused NVLink all-gather), D2H of the gathered "
                           "bf16 [M, g*N] output" if world > 1 else "dg.launch_with_maps, D2H of the bf16 output")
-                       + ", every step"}
+                       + ", every step" + (f"; {pipe['depth']} requests in flight on as many streams"
+                                           if pipe is not None else "")}
 
     if fused is not None:
         torch.cuda.synchronize(dev)
