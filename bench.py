@@ -47,6 +47,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "cold-weight HBM GB/s & % of peak per B200 at M=1..128; µs per GEMM"
+# Where the one JSON line goes (the process's stdout; see main()).
+JSON_OUT = sys.stdout
 SPEC_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 
@@ -226,7 +228,7 @@ def reference_arm(args, rank, world):
         "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    print(json.dumps(line), file=JSON_OUT, flush=True)
 
 
 # ---------------------------------------------------------------------------
@@ -549,21 +551,16 @@ def b200_arm(args, rank, world, local_rank):
                 hy.copy_(gs_e2e.out, non_blocking=True)
 
         def timed_serial(steps):
+            """One request at a time on one stream (H2D, GEMM -- with the fused
+            gather on N GPUs -- D2H), captured in CUDA graphs."""
             with torch.cuda.stream(stream):
-                for i in range(3):
+                for i in range(4):
                     e2e_step(i)
             torch.cuda.synchronize(dev)
-            if world > 1:
-                dist.barrier()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(stream):
-                e0.record(stream)
-                for i in range(steps):
-                    e2e_step(i)
-                e1.record(stream)
-            torch.cuda.synchronize(dev)
-            return device_max(e0.elapsed_time(e1) / 1e3)
+            graphs = capture(lambda i: e2e_step(i + 4), steps)
+            t = timed(graphs)
+            del graphs
+            return t
 
         pipe = None
         if world == 1:
@@ -637,7 +634,7 @@ def b200_arm(args, rank, world, local_rank):
                "us_per_step": te / K * 1e6,
                "requests_in_flight": pipe["depth"] if pipe is not None else 1,
                "serial": {"us_per_step": te_serial / K * 1e6,
-                          "note": "one request at a time on one stream, dependent schedule"},
+                          "note": "one request at a time on one stream, dependent schedule, CUDA graphs"},
                "schedule": {"block_n": (pipe["cfg"] if pipe is not None else gs_e2e.cfg).block_n,
                             "grid": list(sched.grid), "cluster": sched.cluster,
                             "pdl_mode": args.e2e_schedule if pipe is not None else "dependent"},
@@ -891,7 +888,7 @@ def b200_arm(args, rank, world, local_rank):
         "tensor_parallel": tp,
         "chain_61": chain,
     }
-    print(json.dumps(line), flush=True)
+    print(json.dumps(line), file=JSON_OUT, flush=True)
 
 
 def main():
@@ -903,13 +900,17 @@ def main():
         if world == 1 and args.gpus > 1:
             raise SystemExit("run N>1 under torch.distributed.run (one rank per GPU)")
     if world > 1:
+        # stdout carries exactly one JSON line: keep the real stdout for it and
+        # point file descriptor 1 at stderr, so that whatever libraries print
+        # there (NCCL's version banner, for one) goes to stderr.
+        global JSON_OUT
+        sys.stdout.flush()
+        JSON_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
         import datetime
         import torch.distributed as dist
         backend = "nccl" if args.impl == "b200" else "gloo"
         if backend == "nccl":
-            # NCCL writes its debug lines (the version banner included) to
-            # stdout, which carries exactly one JSON line: send them to stderr.
-            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
             import torch
             torch.cuda.set_device(local_rank)
         dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120))
