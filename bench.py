@@ -25,8 +25,9 @@ us per GEMM.  `e2e` repeats the measurement through the public API with
 every step's activation and scales copied in from pinned host memory and its
 output copied back, inside the timed region: a serving loop with
 --e2e-depth requests in flight (one stream each, captured in CUDA graphs;
-on N GPUs the fused GEMMs stay on one stream and only the copies overlap
-them), and beside it one request at a time on one stream.
+on N GPUs the fused GEMMs stay on one stream in groups of --e2e-group that
+chain under PDL, and the copies overlap them), and beside it one request at
+a time on one stream.
 
 `--impl reference` times the reference's own CPU implementation of the path
 (the host scalar GEMM of kernels/smoke_test.cu, compiled from the reference
@@ -72,8 +73,10 @@ def parse_args():
                          "timed; this picks the headline.")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-depth", type=int, default=4,
-                    help="e2e loop: requests in flight (1 GPU, one stream each) or input slots of the "
-                         "copy/compute pipeline (N GPUs); 1 = one request at a time")
+                    help="e2e loop on 1 GPU: requests in flight, one stream each (1: no pipelined loop)")
+    ap.add_argument("--e2e-group", type=int, default=16,
+                    help="e2e loop on N GPUs: fused GEMMs per group that chain under PDL, the group's "
+                         "first waiting on the copy streams (1: no pipelined loop)")
     ap.add_argument("--e2e-schedule", choices=["independent", "dependent"], default="independent",
                     help="schedule of the e2e loop's GEMMs (they do not feed each other)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -613,86 +616,87 @@ def b200_arm(args, rank, world, local_rank):
             del graphs
             pipe = {"t": t_pipe, "depth": depth, "cfg": cfg_p,
                     "plan": slots[0][1].plan, "outs": [sl[2] for sl in slots], "setups": [sl[1] for sl in slots]}
-        elif args.e2e_depth > 1:
-            # Requests pipelined on N GPUs.  A fused launch waits for its
-            # peers' launches, so every rank issues the fused GEMMs on ONE
-            # stream in the same order (two of them in flight on one GPU from
-            # different streams could wait on each other across GPUs); the H2D
-            # copy of the next request and the D2H copy of the previous one
-            # run beside the GEMM on two copy streams.  `nset` gathered buffer
-            # sets rotate: GEMM i starts after the D2H copy of request
-            # i-(nset-1), and a peer's GEMM i+1 -- the first to write that
-            # request's set again -- starts storing only after this rank
-            # completed GEMM i, so no set is overwritten while it is being
-            # copied out.  The input slots rotate the same way (H2D i waits for
-            # GEMM i-depth).  Every edge is captured in the CUDA graphs; each
-            # graph forks and joins the copy streams, so events never cross a
-            # graph boundary.
-            # The dependent schedule: the cross-stream edges into every GEMM
-            # node leave the captured graph without programmatic edges between
-            # consecutive GEMMs, so each runs alone, and alone the dependent
-            # schedule (S = 4) is the faster one (37 us per step against 50 us
-            # for the independent schedule on 2 GPUs).
-            depth = max(2, args.e2e_depth)
-            nset = max(3, depth)
-            cfg_p = gs_dep.cfg
+        elif args.e2e_group > 1:
+            # Requests pipelined on N GPUs, in groups of `grp`.  A fused launch
+            # waits for its peers' launches, so every rank issues the fused
+            # GEMMs on ONE stream in the same order (two of them in flight on
+            # one GPU from different streams could wait on each other across
+            # GPUs); the H2D copies of a group and the D2H copy after every
+            # GEMM run on two copy streams beside them.  Only the group's first
+            # GEMM waits on the copy streams (its group's H2D copies and the
+            # D2H copy of the previous group's first request): a captured GEMM
+            # node with cross-stream edges loses its programmatic edge, and
+            # the other GEMMs of the group keep theirs, so they overlap under
+            # PDL.  2*grp input slots and 2*grp gathered buffer sets rotate:
+            # H2D j waits for GEMM j-2*grp; set j % (2*grp) was last copied out
+            # by D2H j-2*grp, which completed before the GEMM group holding j-1
+            # began (a peer's first store into that set follows this rank's
+            # GEMM j-1).  Each graph forks and joins the copy streams, so events
+            # never cross a graph boundary.
+            grp = args.e2e_group
+            nset = 2 * grp
+            depth = nset
+            cfg_p = dg.default_config(m, n, k, layout=layout, pdl=pdl,
+                                      independent_inputs=args.e2e_schedule == "independent")
             fused_p = dg_tp.FusedGather(m, n, buffers=nset, device=dev)
             pdesc = [fused_p.descriptor(j) for j in range(nset)]
             slots = []
-            for _ in range(depth):
+            for _ in range(nset):
                 d_in = torch.empty(in_bytes, dtype=torch.uint8, device=dev)
                 slots.append((d_in, GemmSetup(rotation(cfg_p.block_n), cfg_p, m, d_in[: m * k].view(m, k),
                                               wscale, d_in[m * k:].view(torch.float32).view(m, kb), dev)))
             h_outs = [torch.empty((m, world * n), dtype=torch.bfloat16).pin_memory() for _ in range(nset)]
             h2d_st = torch.cuda.Stream(device=dev)
             d2h_st = torch.cuda.Stream(device=dev)
-            ring = 2 * depth + 4
-            ev_h2d = [torch.cuda.Event() for _ in range(ring)]
+            ring = 2 * nset + 2
+            ev_h2d = torch.cuda.Event()
             ev_gemm = [torch.cuda.Event() for _ in range(ring)]
             ev_d2h = [torch.cuda.Event() for _ in range(ring)]
 
-            def mg_step(i, base):
-                d_in, g_p = slots[i % depth]
-                if i - base >= depth:
-                    h2d_st.wait_event(ev_gemm[(i - depth) % ring])
-                with torch.cuda.stream(h2d_st):
-                    d_in.copy_(hin, non_blocking=True)
-                ev_h2d[i % ring].record(h2d_st)
-                stream.wait_event(ev_h2d[i % ring])
-                if i - base >= nset - 1:
-                    stream.wait_event(ev_d2h[(i - nset + 1) % ring])
-                rc = dg.launch_gather(g_p.cfg, g_p.probs[i % g_p.nsets], pdesc[i % nset], g_p.wmaps[i % g_p.nsets],
-                                      g_p.amap, stream, pdl_attr=g_p.cfg.pdl)
-                if rc != 0:
-                    raise RuntimeError(f"fused launch failed: cudaError {rc}")
-                # No dg_gather_wait node: a fused grid completes only after its
-                # last CTA saw every peer's epoch for this launch (each peer
-                # publishes after a system-scope fence over its slice stores),
-                # so the copy that follows the grid reads the whole gathered
-                # output; and consecutive fused GEMMs keep their PDL edge.
-                ev_gemm[i % ring].record(stream)
-                d2h_st.wait_event(ev_gemm[i % ring])
-                with torch.cuda.stream(d2h_st):
-                    h_outs[i % nset].copy_(fused_p.output(i % nset, m), non_blocking=True)
-                ev_d2h[i % ring].record(d2h_st)
+            def mg_group(g0, g1, base):
+                for j in range(g0, g1):
+                    if j - base >= nset:
+                        h2d_st.wait_event(ev_gemm[(j - nset) % ring])
+                    with torch.cuda.stream(h2d_st):
+                        slots[j % nset][0].copy_(hin, non_blocking=True)
+                ev_h2d.record(h2d_st)
+                stream.wait_event(ev_h2d)
+                if g0 - grp >= base:
+                    stream.wait_event(ev_d2h[(g0 - grp) % ring])
+                for j in range(g0, g1):
+                    g_p = slots[j % nset][1]
+                    rc = dg.launch_gather(g_p.cfg, g_p.probs[j % g_p.nsets], pdesc[j % nset],
+                                          g_p.wmaps[j % g_p.nsets], g_p.amap, stream, pdl_attr=g_p.cfg.pdl)
+                    if rc != 0:
+                        raise RuntimeError(f"fused launch failed: cudaError {rc}")
+                    # No dg_gather_wait node: a fused grid completes only after
+                    # its last CTA saw every peer's epoch for this launch (each
+                    # peer publishes after a system-scope fence over its slice
+                    # stores), so the copy that follows reads the whole output.
+                    ev_gemm[j % ring].record(stream)
+                    d2h_st.wait_event(ev_gemm[j % ring])
+                    with torch.cuda.stream(d2h_st):
+                        h_outs[j % nset].copy_(fused_p.output(j % nset, m), non_blocking=True)
+                    ev_d2h[j % ring].record(d2h_st)
 
             def mg_chunk(base, count):
                 h2d_st.wait_stream(stream)
                 d2h_st.wait_stream(stream)
-                for i in range(base, base + count):
-                    mg_step(i, base)
+                for g0 in range(base, base + count, grp):
+                    mg_group(g0, min(base + count, g0 + grp), base)
                 stream.wait_stream(h2d_st)
                 stream.wait_stream(d2h_st)
 
             with torch.cuda.stream(stream):
-                mg_chunk(0, 3 * depth)
+                mg_chunk(0, 3 * nset)
             torch.cuda.synchronize(dev)
+            chunk = max(grp, args.graph_chunk - args.graph_chunk % grp)
             graphs = []
             with torch.cuda.stream(stream):
-                for base in range(0, K, args.graph_chunk):
+                for base in range(0, K, chunk):
                     gr = torch.cuda.CUDAGraph()
                     with torch.cuda.graph(gr, stream=stream):
-                        mg_chunk(base, min(K, base + args.graph_chunk) - base)
+                        mg_chunk(base, min(K, base + chunk) - base)
                     graphs.append(gr)
             t_pipe = timed(graphs)
             del graphs
@@ -732,16 +736,16 @@ def b200_arm(args, rank, world, local_rank):
                           "note": "one request at a time on one stream, dependent schedule, CUDA graphs"},
                "schedule": {"block_n": (pipe["cfg"] if pipe is not None else gs_e2e.cfg).block_n,
                             "grid": list(sched.grid), "cluster": sched.cluster,
-                            "pdl_mode": args.e2e_schedule if pipe is not None and world == 1 else "dependent"},
+                            "pdl_mode": args.e2e_schedule if pipe is not None else "dependent"},
                "path": "one pinned H2D copy of activation + scales, "
                        + ("dg.launch_gather (GEMM with the fused NVLink all-gather), D2H of the gathered "
                           "bf16 [M, g*N] output" if world > 1 else "dg.launch_with_maps, D2H of the bf16 output")
                        + ", every step" + ("" if pipe is None else
                                            f"; {pipe['depth']} requests in flight on as many streams" if world == 1 else
                                            "; pipelined: the fused GEMMs on one stream in the same order on every "
-                                           "rank, the next request's H2D and the previous one's D2H on two copy "
-                                           f"streams beside it ({pipe['depth']} input slots and gathered buffer "
-                                           "sets)")}
+                                           f"rank in groups of {pipe['depth'] // 2} (PDL inside a group), H2D and "
+                                           "D2H copies on two copy streams beside them "
+                                           f"({pipe['depth']} input slots and gathered buffer sets)")}
 
     if fused is not None:
         torch.cuda.synchronize(dev)

@@ -132,9 +132,10 @@ class FusedGather:
     """Gathered output buffers of a tensor-parallel group for the fused-gather
     launch.
 
-    Every rank allocates `buffers` gathered [m_max, world*n_loc] bf16 buffers,
-    one int[world] flag array and an int[2] launch counter, exports CUDA IPC
-    handles for the buffers and flags, exchanges them with
+    Every rank allocates `buffers` gathered [m_max, world*n_loc] bf16 buffers
+    (slices of one allocation, so a peer opens one IPC mapping for all of
+    them), one int[world] flag array and an int[2] launch counter, exports
+    CUDA IPC handles for the buffers and flags, exchanges them with
     `all_gather_object` over `group`, and maps every other rank's.
     `descriptor(i)` is the dg_gather of buffer set i: alternate i between
     consecutive launches (a rank must never overwrite slices a peer has not
@@ -152,8 +153,8 @@ class FusedGather:
         self.n_loc = n_loc
         self.m_max = m_max
         dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-        self.buffers = [torch.zeros((m_max, self.world * n_loc), dtype=torch.bfloat16, device=dev)
-                        for _ in range(buffers)]
+        self.storage = torch.zeros((buffers, m_max, self.world * n_loc), dtype=torch.bfloat16, device=dev)
+        self.buffers = [self.storage[i] for i in range(buffers)]
         self.flags = torch.zeros(self.world, dtype=torch.int32, device=dev)
         self.sync = torch.zeros(2, dtype=torch.int32, device=dev)
         torch.cuda.synchronize(dev)
