@@ -617,22 +617,19 @@ def b200_arm(args, rank, world, local_rank):
             pipe = {"t": t_pipe, "depth": depth, "cfg": cfg_p,
                     "plan": slots[0][1].plan, "outs": [sl[2] for sl in slots], "setups": [sl[1] for sl in slots]}
         elif args.e2e_group > 1:
-            # Requests pipelined on N GPUs, in groups of `grp`.  A fused launch
-            # waits for its peers' launches, so every rank issues the fused
-            # GEMMs on ONE stream in the same order (two of them in flight on
-            # one GPU from different streams could wait on each other across
-            # GPUs); the H2D copies of a group and the D2H copy after every
-            # GEMM run on two copy streams beside them.  Only the group's first
-            # GEMM waits on the copy streams (its group's H2D copies and the
-            # D2H copy of the previous group's first request): a captured GEMM
-            # node with cross-stream edges loses its programmatic edge, and
-            # the other GEMMs of the group keep theirs, so they overlap under
-            # PDL.  2*grp input slots and 2*grp gathered buffer sets rotate:
-            # H2D j waits for GEMM j-2*grp; set j % (2*grp) was last copied out
-            # by D2H j-2*grp, which completed before the GEMM group holding j-1
-            # began (a peer's first store into that set follows this rank's
-            # GEMM j-1).  Each graph forks and joins the copy streams, so events
-            # never cross a graph boundary.
+            # Requests pipelined on N GPUs, in groups of `grp`
+            # (decode_opt_b200.tp.serving_schedule: which operation waits on
+            # which).  A fused launch waits for its peers' launches, so every
+            # rank issues the fused GEMMs on ONE stream in the same order (two
+            # of them in flight on one GPU from different streams could wait on
+            # each other across GPUs); the H2D copies and the D2H copy after
+            # every GEMM run on two copy streams beside them.  Only a group's
+            # first GEMM waits on the copy streams: a captured GEMM node with
+            # cross-stream edges loses its programmatic edge, and the other
+            # GEMMs of the group keep theirs, so they overlap under PDL.
+            # 2*grp input slots and gathered buffer sets rotate.  Each graph
+            # forks and joins the copy streams, so events never cross a graph
+            # boundary.
             grp = args.e2e_group
             nset = 2 * grp
             depth = nset
@@ -649,21 +646,17 @@ def b200_arm(args, rank, world, local_rank):
             h2d_st = torch.cuda.Stream(device=dev)
             d2h_st = torch.cuda.Stream(device=dev)
             ring = 2 * nset + 2
-            ev_h2d = torch.cuda.Event()
-            ev_gemm = [torch.cuda.Event() for _ in range(ring)]
-            ev_d2h = [torch.cuda.Event() for _ in range(ring)]
+            op_stream = {"h2d": h2d_st, "gemm": stream, "d2h": d2h_st}
+            op_done = {kind: [torch.cuda.Event() for _ in range(ring)] for kind in op_stream}
 
-            def mg_group(g0, g1, base):
-                for j in range(g0, g1):
-                    if j - base >= nset:
-                        h2d_st.wait_event(ev_gemm[(j - nset) % ring])
-                    with torch.cuda.stream(h2d_st):
+            def run_op(kind, j, waits):
+                st = op_stream[kind]
+                for w_kind, w_j in waits:
+                    st.wait_event(op_done[w_kind][w_j % ring])
+                if kind == "h2d":
+                    with torch.cuda.stream(st):
                         slots[j % nset][0].copy_(hin, non_blocking=True)
-                ev_h2d.record(h2d_st)
-                stream.wait_event(ev_h2d)
-                if g0 - grp >= base:
-                    stream.wait_event(ev_d2h[(g0 - grp) % ring])
-                for j in range(g0, g1):
+                elif kind == "gemm":
                     g_p = slots[j % nset][1]
                     rc = dg.launch_gather(g_p.cfg, g_p.probs[j % g_p.nsets], pdesc[j % nset],
                                           g_p.wmaps[j % g_p.nsets], g_p.amap, stream, pdl_attr=g_p.cfg.pdl)
@@ -673,17 +666,16 @@ def b200_arm(args, rank, world, local_rank):
                     # its last CTA saw every peer's epoch for this launch (each
                     # peer publishes after a system-scope fence over its slice
                     # stores), so the copy that follows reads the whole output.
-                    ev_gemm[j % ring].record(stream)
-                    d2h_st.wait_event(ev_gemm[j % ring])
-                    with torch.cuda.stream(d2h_st):
+                else:
+                    with torch.cuda.stream(st):
                         h_outs[j % nset].copy_(fused_p.output(j % nset, m), non_blocking=True)
-                    ev_d2h[j % ring].record(d2h_st)
+                op_done[kind][j % ring].record(st)
 
             def mg_chunk(base, count):
                 h2d_st.wait_stream(stream)
                 d2h_st.wait_stream(stream)
-                for g0 in range(base, base + count, grp):
-                    mg_group(g0, min(base + count, g0 + grp), base)
+                for op in dg_tp.serving_schedule(base, count, grp):
+                    run_op(*op)
                 stream.wait_stream(h2d_st)
                 stream.wait_stream(d2h_st)
 

@@ -128,6 +128,47 @@ def gather_descriptor(world: int, rank: int, n_loc: int, out_bases, flag_ptrs, s
     return g
 
 
+def serving_schedule(base: int, count: int, group: int):
+    """The operations of the N-GPU serving loop for requests base .. base+count-1,
+    in issue order, as (kind, j, waits).
+
+    kind: "h2d" (request j's inputs host -> input slot j % (2*group), copy
+    stream A), "gemm" (the fused GEMM + gather of request j into gathered set
+    j % (2*group), the compute stream) or "d2h" (set j % (2*group) -> host,
+    copy stream B).  waits: (kind, index) operations of OTHER streams this one
+    must follow; each stream also runs its own operations in order, and waits
+    never reach before `base` (a CUDA graph of one chunk starts after the
+    previous chunk's graph has completed).
+
+    Requests go in groups of `group`: the group's H2D copies are issued first,
+    then its GEMMs, each followed by its D2H copy.  Only the group's first GEMM
+    waits on a copy stream -- for its group's last H2D copy and for the D2H
+    copy of the previous group's first request -- so the other GEMMs of the
+    group keep their programmatic (PDL) edge to the GEMM before them.  H2D j
+    waits for GEMM j - 2*group (the previous reader of its slot).  With that,
+    D2H j - 2*group (the previous reader of set j % (2*group)) finishes before
+    this rank's GEMM j - 1, after which a peer's GEMM j may store into the set.
+    """
+    if group < 1 or count < 0:
+        raise ValueError("group must be >= 1 and count >= 0")
+    nset = 2 * group
+    ops = []
+    end = base + count
+    for g0 in range(base, end, group):
+        g1 = min(end, g0 + group)
+        for j in range(g0, g1):
+            ops.append(("h2d", j, [("gemm", j - nset)] if j - nset >= base else []))
+        for j in range(g0, g1):
+            waits = []
+            if j == g0:
+                waits.append(("h2d", g1 - 1))
+                if g0 - group >= base:
+                    waits.append(("d2h", g0 - group))
+            ops.append(("gemm", j, waits))
+            ops.append(("d2h", j, [("gemm", j)]))
+    return ops
+
+
 class FusedGather:
     """Gathered output buffers of a tensor-parallel group for the fused-gather
     launch.
