@@ -9,6 +9,11 @@ kernel (dg_launch_gather).
   NVLink; after the completion wait both gathered outputs must match the
   oracle for the whole N over two consecutive launches (alternating buffer
   sets), with status 0.
+* Two GPUs: the serving loop's schedule (decode_opt_b200.tp.serving_schedule)
+  run for 24 requests in groups of 4 -- H2D copies, fused GEMMs and D2H
+  copies on three streams, input slots and gathered sets reused -- with five
+  different activations cycling, so that a reuse hazard would corrupt a
+  request; every request's gathered output must match the oracle.
 """
 
 import ctypes
@@ -134,3 +139,109 @@ def test_two_gpu_fused_gather_matches_oracle(tmp_path, m):
             got = np.load(os.path.join(str(tmp_path), f"rank{r}.npy"))[step]
             ok, rl2, worst = check_against_oracle(got, ref)
             assert ok, (r, step, rl2, worst)
+
+
+def _serve_main(rank, world, port, m, n, k, group, count, distinct, result_dir):
+    """One rank of the N-GPU serving loop (decode_opt_b200.tp.serving_schedule,
+    executed as bench.py executes it, eagerly): request j copies activation
+    j % distinct in from pinned host memory, runs the fused GEMM into
+    gathered set j % (2*group) and copies its output to its own pinned host
+    buffer."""
+    import torch.distributed as dist
+    import oracle
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    fg = None
+    try:
+        dev = torch.device("cuda", rank)
+        w, ws = oracle.gen_weight_smoke(n, k, 91)
+        n_loc = n // world
+        lo, hi = tp.shard_rows(n, world, rank)
+        cfg = dg.default_config(m, n_loc, k, layout=dg.LAYOUT_PACKED_SWIZZLED, independent_inputs=True)
+        plan = cfg.plan(m, n_loc, k)
+        wt = dg.prepack_weight(torch.from_numpy(np.ascontiguousarray(w[lo:hi])).to(dev), cfg.block_n, cfg.layout)
+        wsc = torch.from_numpy(np.ascontiguousarray(tp.shard_scales(ws, world, rank, n))).to(dev)
+        ws_buf = torch.zeros(max(plan.ws_floats, 1), device=dev)
+        sem = torch.zeros(max(plan.sem_ints, 1), dtype=torch.int32, device=dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        nset = 2 * group
+        fg = tp.FusedGather(m, n_loc, buffers=nset, device=dev)
+        kb = k // 128
+        in_bytes = m * k + m * kb * 4
+        hins = []
+        for r in range(distinct):
+            a, as_ = oracle.gen_activation_smoke(m, k, 300 + r)
+            h = torch.empty(in_bytes, dtype=torch.uint8).pin_memory()
+            h[: m * k].copy_(torch.from_numpy(a.reshape(-1)))
+            h[m * k:].copy_(torch.from_numpy(as_.reshape(-1)).view(torch.uint8))
+            hins.append(h)
+        slots, probs = [], []
+        for _ in range(nset):
+            d_in = torch.empty(in_bytes, dtype=torch.uint8, device=dev)
+            p = dg.Problem(m, n_loc, k, d_in[: m * k].view(m, k), wt, wsc,
+                           d_in[m * k:].view(torch.float32).view(m, kb), None, ws_buf, sem, status)
+            slots.append(d_in)
+            probs.append((p, dg.make_activation_tma(cfg, p)))
+        w_map = dg.make_weight_tma(cfg, probs[0][0])
+        descs = [fg.descriptor(i) for i in range(nset)]
+        h_outs = [torch.empty((m, world * n_loc), dtype=torch.bfloat16).pin_memory() for _ in range(count)]
+        compute = torch.cuda.Stream(device=dev)
+        streams = {"h2d": torch.cuda.Stream(device=dev), "gemm": compute, "d2h": torch.cuda.Stream(device=dev)}
+        ring = 2 * nset + 2
+        done = {kind: [torch.cuda.Event() for _ in range(ring)] for kind in streams}
+        dist.barrier()
+        for kind, j, waits in tp.serving_schedule(0, count, group):
+            st = streams[kind]
+            for wk, wj in waits:
+                st.wait_event(done[wk][wj % ring])
+            with torch.cuda.stream(st):
+                if kind == "h2d":
+                    slots[j % nset].copy_(hins[j % distinct], non_blocking=True)
+                elif kind == "gemm":
+                    p, a_map = probs[j % nset]
+                    rc = dg.launch_gather(cfg, p, descs[j % nset], w_map, a_map, st, pdl_attr=cfg.pdl)
+                    assert rc == 0, rc
+                else:
+                    h_outs[j].copy_(fg.output(j % nset, m), non_blocking=True)
+            done[kind][j % ring].record(st)
+        torch.cuda.synchronize(dev)
+        assert int(status.item()) == 0, dg.status_string(int(status.item()))
+        np.save(os.path.join(result_dir, f"serve{rank}.npy"), np.stack([h.float().numpy() for h in h_outs]))
+        dist.barrier()
+    finally:
+        if fg is not None:
+            fg.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("m", [1, 8])
+def test_two_gpu_serving_schedule_matches_oracle(tmp_path, m):
+    import torch.multiprocessing as mp
+    import oracle
+    from helpers import check_against_oracle
+    n, k, world, group, count, distinct = 2048, 4096, 2, 4, 24, 5
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_serve_main, args=(r, world, port, m, n, k, group, count, distinct, str(tmp_path)))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.exitcode is None:
+            p.kill()
+        assert p.exitcode == 0
+    w, ws = oracle.gen_weight_smoke(n, k, 91)
+    refs = []
+    for r in range(distinct):
+        a, as_ = oracle.gen_activation_smoke(m, k, 300 + r)
+        refs.append(oracle.compute_reference(a, as_, w, ws, threads=8))
+    for r in range(world):
+        got = np.load(os.path.join(str(tmp_path), f"serve{r}.npy"))
+        for j in range(count):
+            ok, rl2, worst = check_against_oracle(got[j], refs[j % distinct])
+            assert ok, (r, j, rl2, worst)
