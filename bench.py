@@ -82,6 +82,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU work the rank-0 cpu_baseline sample is sized to")
+    ap.add_argument("--ref-seconds", type=float, default=60.0,
+                    help="--impl reference: CPU time its warm-up and timed steps are sized to")
     ap.add_argument("--graph-chunk", type=int, default=500, help="launches per captured CUDA graph")
     ap.add_argument("--no-sweep", action="store_true", help="skip the M = 1..128 sweep")
     ap.add_argument("--no-cublas", action="store_true", help="skip the cuBLASLt FP8 baseline")
@@ -208,12 +210,13 @@ def reference_arm(args, rank, world):
     threads = os.cpu_count() or 1
     n, k, m = args.n, args.k, args.m
     w, ws, a, as_ = host_inputs(n, k, m)
-    # Size each step's sample so the timed K steps take about a minute.
+    # Size each step's sample so the warm-up and timed steps take about
+    # --ref-seconds (a minute by default).
     rows_probe = min(n, 1024)
     t0 = time.perf_counter()
     cpu_parallel_gemm(run, a, as_, w[:rows_probe], ws[: (rows_probe + 127) // 128], threads)
     per_row = (time.perf_counter() - t0) / rows_probe
-    budget = 60.0 / max(args.steps + args.warmup, 1)
+    budget = args.ref_seconds / max(args.steps + args.warmup, 1)
     rows = int(max(128, min(n, budget / max(per_row, 1e-12))) // 128 * 128)
     w_s, ws_s = w[:rows], ws[: rows // 128]
     for _ in range(args.warmup):
