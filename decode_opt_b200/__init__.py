@@ -130,9 +130,8 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
                    independent_inputs: bool = False, schedule: str = "cluster") -> B200Config:
     """The B200 schedule used by :func:`fp8_decode_gemm` and the benchmark.
 
-    Two 128-K blocks per stage in a two-deep ring (64 KiB per bulk copy at
-    256 rows; deeper rings measured no faster) and weight tiles on the
-    tcgen05 N side, 256 rows (8 KiB of weights per MMA instruction):
+    Two 128-K blocks per stage and weight tiles on the tcgen05 N side, 256
+    rows (8 KiB of weights per MMA instruction) unless 224 serves better:
 
     * ``schedule="cluster"`` (default): cluster split-K (``GRID_CLUSTER``):
       each tile's K range split over the CTAs of one thread-block cluster,
@@ -189,7 +188,8 @@ class KernelConfig:
       (the ring depth, reduced if it does not fit in 227 KiB);
     * ``PREPACK`` -> weight layout packed (True) or raw (False);
     * ``PDL`` or ``EPI_OVERLAP`` -> ``griddepcontrol.launch_dependents`` after
-      the producer's last TMA (the sm_100a kernel has one trigger point);
+      the producer's first ring pass (the sm_100a kernel has one trigger
+      point, earlier than the reference's after-the-last-TMA trigger);
       ``launch`` sets programmatic stream serialization when ``PDL``;
     * ``SPLIT_K_CTA`` / ``SPLITK_FACTOR`` -> ``split_k`` = kSplitKFactor with the
       reference's normalisation (0: follow the bool, 1: off, 2/4/8: S);
