@@ -59,9 +59,9 @@ int current_sm_count() {
 // quarter); everything else is runtime.
 struct KernelEntry {
   KernelFn fn;
-  std::atomic<int> smem_high_water;
-  cudaError_t pool_check;   // register pool covers the setmaxnreg split
-  std::atomic<int> nonportable_cluster;   // cudaFuncAttributeNonPortableClusterSizeAllowed set
+  std::atomic<unsigned long long> smem_set;          // per device: dynamic smem limit raised
+  cudaError_t pool_check;                            // register pool covers the setmaxnreg split
+  std::atomic<unsigned long long> nonportable_set;   // per device: cluster sizes above 8 allowed
 };
 
 template <int MMA_M, int COPIES, int EPW>
@@ -100,9 +100,9 @@ const int* device_cluster_occupancy() {
   if (g_occ_ready[dev]) return g_occ[dev];
   KernelEntry* k = entry<64, 4, 1>();
   const void* fn = reinterpret_cast<const void*>(k->fn);
-  bool ok = dg::ensure_smem(fn, dg::kMaxDynamicSmem, &k->smem_high_water) == cudaSuccess &&
-            cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
-  if (ok) k->nonportable_cluster.store(1, std::memory_order_release);
+  bool ok = dg::ensure_smem(fn, &k->smem_set) == cudaSuccess &&
+            dg::set_func_attribute_once(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1,
+                                        &k->nonportable_set) == cudaSuccess;
   g_occ[dev][0] = 0;
   for (int S = 1; ok && S <= dg::kMaxClusterSplit; ++S) {
     cudaLaunchConfig_t lc{};
@@ -208,14 +208,13 @@ int launch_impl(const dg_config* cfg, const dg_problem* prob, const CUtensorMap*
   KernelEntry* k = select_kernel(plan.mma_m, plan.copies, plan.epw);
   if (k == nullptr) return cudaErrorInvalidValue;
   if (k->pool_check != cudaSuccess) return k->pool_check;
-  const cudaError_t attr_err =
-      dg::ensure_smem(reinterpret_cast<const void*>(k->fn), plan.smem_bytes, &k->smem_high_water);
+  const cudaError_t attr_err = dg::ensure_smem(reinterpret_cast<const void*>(k->fn), &k->smem_set);
   if (attr_err != cudaSuccess) return attr_err;
-  if (plan.cluster > 8 && k->nonportable_cluster.load(std::memory_order_acquire) == 0) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(reinterpret_cast<const void*>(k->fn), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (plan.cluster > 8) {
+    const cudaError_t e = dg::set_func_attribute_once(reinterpret_cast<const void*>(k->fn),
+                                                      cudaFuncAttributeNonPortableClusterSizeAllowed, 1,
+                                                      &k->nonportable_set);
     if (e != cudaSuccess) return e;
-    k->nonportable_cluster.store(1, std::memory_order_release);
   }
   return dg::launch_kernel(k->fn, plan, p, *w_map, *a_map, stream, pdl_attr);
 }
@@ -343,12 +342,12 @@ int dg_max_active_clusters(const dg_config* cfg, int M, int N, int K, int* out) 
   if (plan.error != nullptr) return cudaErrorInvalidValue;
   KernelEntry* k = select_kernel(plan.mma_m, plan.copies, plan.epw);
   if (k == nullptr) return cudaErrorInvalidValue;
-  cudaError_t err = dg::ensure_smem(reinterpret_cast<const void*>(k->fn), plan.smem_bytes, &k->smem_high_water);
+  cudaError_t err = dg::ensure_smem(reinterpret_cast<const void*>(k->fn), &k->smem_set);
   if (err != cudaSuccess) return err;
-  if (plan.cluster > 8 && k->nonportable_cluster.load(std::memory_order_acquire) == 0) {
-    err = cudaFuncSetAttribute(reinterpret_cast<const void*>(k->fn), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (plan.cluster > 8) {
+    err = dg::set_func_attribute_once(reinterpret_cast<const void*>(k->fn),
+                                      cudaFuncAttributeNonPortableClusterSizeAllowed, 1, &k->nonportable_set);
     if (err != cudaSuccess) return err;
-    k->nonportable_cluster.store(1, std::memory_order_release);
   }
   cudaLaunchConfig_t lc{};
   cudaLaunchAttribute attr[1]{};

@@ -410,13 +410,39 @@ inline cudaError_t check_register_pool(const void* fn, int copies, int epw) {
 // reference's single cached value per Cfg (kernels/decode_gemm.cuh:1100-1109)
 // this keeps the largest size set so far per kernel, so interleaved callers
 // with different M never lower it under each other.
-inline cudaError_t ensure_smem(const void* fn, uint32_t bytes, std::atomic<int>* high_water) {
-  int cur = high_water->load(std::memory_order_acquire);
-  if (cur >= static_cast<int>(bytes)) return cudaSuccess;
-  const cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(kMaxDynamicSmem));
-  if (err == cudaSuccess) high_water->store(static_cast<int>(kMaxDynamicSmem), std::memory_order_release);
+// Function attributes belong to the current device's context, so a cache of
+// "already set" keeps one bit per device id below 64 (devices from 64 on set
+// the attribute on every call).
+inline unsigned long long current_device_bit() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0ull;
+  }
+  return (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
+}
+
+inline bool func_attribute_done(const std::atomic<unsigned long long>* done) {
+  const unsigned long long bit = current_device_bit();
+  return bit != 0ull && (done->load(std::memory_order_acquire) & bit) != 0ull;
+}
+
+// Sets `attr` = `value` on `fn` for the current device unless `done` says it
+// was set there already.
+inline cudaError_t set_func_attribute_once(const void* fn, cudaFuncAttribute attr, int value,
+                                           std::atomic<unsigned long long>* done) {
+  const unsigned long long bit = current_device_bit();
+  if (bit != 0ull && (done->load(std::memory_order_acquire) & bit) != 0ull) return cudaSuccess;
+  const cudaError_t err = cudaFuncSetAttribute(fn, attr, value);
+  if (err == cudaSuccess && bit != 0ull) done->fetch_or(bit, std::memory_order_acq_rel);
   return err;
+}
+
+// Raises the kernel's dynamic shared memory limit to the sm_100 maximum (once
+// per device); every plan's smem_bytes is at most that.
+inline cudaError_t ensure_smem(const void* fn, std::atomic<unsigned long long>* done) {
+  return set_func_attribute_once(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kMaxDynamicSmem), done);
 }
 
 // Checks the pointers a plan needs before anything is enqueued.

@@ -334,15 +334,16 @@ inline LaunchPlan make_launch_plan(const Problem& p) {
 // covers the kernel's register split (setmaxnreg) before anything launches it.
 template <typename Cfg>
 inline cudaError_t ensure_smem_attribute(uint32_t smem_bytes) {
-  static std::atomic<int> high_water{-1};
-  if (high_water.load(std::memory_order_acquire) >= static_cast<int>(smem_bytes)) return cudaSuccess;
+  // Raised once per device to the sm_100 maximum (function attributes belong
+  // to the device's context; the reference caches one value per process).
+  static std::atomic<unsigned long long> done{0};
+  if (smem_bytes > kMaxDynamicSmemBytes) return cudaErrorInvalidValue;
+  if (dg::func_attribute_done(&done)) return cudaSuccess;
   const void* fn = reinterpret_cast<const void*>(&fp8_decode_gemm<Cfg>);
   const cudaError_t pool = dg::check_register_pool(fn, Cfg::Traits::kCopies, Cfg::Traits::kEpw);
   if (pool != cudaSuccess) return pool;
-  const cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(kMaxDynamicSmemBytes));
-  if (err == cudaSuccess) high_water.store(static_cast<int>(kMaxDynamicSmemBytes), std::memory_order_release);
-  return err;
+  return dg::set_func_attribute_once(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kMaxDynamicSmemBytes), &done);
 }
 
 // Launch with pre-built tensor maps (keep map encoding out of timed loops).
