@@ -369,8 +369,9 @@ inline cudaError_t make_weight_map(CUtensorMap* map, const Config& c, const void
 
 // Activation map: dims {128, M, K/128}, strides {K, 128}, box {128, a_rows, 1}
 // with a_rows = M rounded up to 8 (rows M..a_rows-1 land as zeros); the
-// producer issues one box per 128-K block and batch copy.
-inline cudaError_t make_activation_map(CUtensorMap* map, const Config& c, const void* act, int M, int K) {
+// producer issues one box per 128-K block and batch copy.  The map does not
+// depend on the configuration (kept in the signature beside the weight map's).
+inline cudaError_t make_activation_map(CUtensorMap* map, const Config& /*c*/, const void* act, int M, int K) {
   std::memset(map, 0, sizeof(*map));
   EncodeTiledFn encode = encode_tiled_fn();
   if (encode == nullptr) return cudaErrorInsufficientDriver;
