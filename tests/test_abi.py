@@ -195,3 +195,44 @@ def test_kernel_config_maps_onto_b200_config():
         (8, 56, 2, 6, dg.LAYOUT_PACKED, True, 1, 0)
     plan = dg.make_launch_plan(k, dg.Problem(1, 7168, 16384))
     assert plan.error is None and plan.grid == (128, 1, 1) and plan.mma_m == 64 and plan.n_mma == 64
+
+
+B200_CLUSTER_OCC = [0, 148, 74, 45, 33, 26, 22, 15, 15]   # clusters of S CTAs resident at once (measured)
+
+
+def _rule_split(t, c, independent):
+    """The split rule restated: independent inputs -> the smallest one-wave S
+    giving >= 32 CTAs; dependent -> the largest one-wave S (S <= 8, S <= C)."""
+    s_max = min(c, 8)
+    if independent:
+        for s in range(2, s_max + 1):
+            if t <= B200_CLUSTER_OCC[s] and t * s >= 32:
+                return s
+    for s in range(s_max, 1, -1):
+        if t <= B200_CLUSTER_OCC[s]:
+            return s
+    return 1
+
+
+@pytest.mark.parametrize("n,k", [(7168, 16384), (7168, 12288), (6144, 16384), (6144, 8192), (2048, 4096)])
+@pytest.mark.parametrize("m", [1, 8, 16, 17, 32, 33, 64, 65, 128])
+@pytest.mark.parametrize("independent", [False, True])
+def test_default_plans_follow_the_split_rule(n, k, m, independent):
+    """Every BASELINE model shape: the default plan is a one-wave cluster
+    split-K plan whose split is the rule's pick for its tile count, with no
+    workspace, a ring that fits, and the batch class M calls for."""
+    c = dg.default_config(m, n, k, layout=dg.LAYOUT_PACKED_SWIZZLED, independent_inputs=independent)
+    p = c.plan(m, n, k)
+    assert p.error is None
+    assert c.grid_ctas == dg.GRID_CLUSTER and c.block_n in (224, 256)
+    tiles = -(-n // c.block_n)
+    chunks = (k // 128) // c.subs
+    assert p.grid == (tiles, p.cluster, 1) and p.num_ctas == tiles * p.cluster
+    assert p.cluster == _rule_split(tiles, chunks, independent)
+    assert tiles <= B200_CLUSTER_OCC[p.cluster]                  # one wave of clusters
+    assert p.ws_floats == 0 and p.sem_ints == 0
+    assert p.stages >= 2 and p.smem_bytes <= 227 * 1024
+    assert p.mma_m == (64 if m <= 32 else 128)
+    assert p.block[0] == (192 if m <= 16 else 320 if m <= 64 else 384)
+    if independent:
+        assert p.num_ctas >= 32 or p.cluster == min(chunks, 8)
