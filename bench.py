@@ -71,6 +71,8 @@ def parse_args():
                          "reference's back-to-back PDL protocol); dependent: every launch waits for "
                          "the previous grid before reading its activation (a layer chain). Both are "
                          "timed; this picks the headline.")
+    ap.add_argument("--schedule", choices=["cluster", "stream_k"], default="cluster",
+                    help="default_config's schedule: cluster split-K (default) or stream-K over one CTA per SM")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-depth", type=int, default=4,
                     help="e2e loop on 1 GPU: requests in flight, one stream each (1: no pipelined loop)")
@@ -309,6 +311,10 @@ def b200_arm(args, rank, world, local_rank):
     layout = {"raw": dg.LAYOUT_RAW, "packed": dg.LAYOUT_PACKED, "swizzled": dg.LAYOUT_PACKED_SWIZZLED}[args.layout]
     pdl = not args.no_pdl
     independent = args.pdl_mode == "independent"
+
+    def default_config(*a, **kw):
+        return dg.default_config(*a, schedule=args.schedule, **kw)
+
     stream = torch.cuda.Stream(device=dev)
     pg = dist.group.WORLD if world > 1 else None
 
@@ -387,8 +393,8 @@ def b200_arm(args, rank, world, local_rank):
 
     # The headline mode's schedule and the other PDL mode's, each with its own
     # weight copies (packed for its tile width) and tensor maps.
-    cfg = dg.default_config(m, n, k, layout=layout, pdl=pdl, independent_inputs=independent)
-    cfg_other = dg.default_config(m, n, k, layout=layout, pdl=pdl, independent_inputs=not independent)
+    cfg = default_config(m, n, k, layout=layout, pdl=pdl, independent_inputs=independent)
+    cfg_other = default_config(m, n, k, layout=layout, pdl=pdl, independent_inputs=not independent)
     rot = rotation(cfg.block_n)
     gs = GemmSetup(rot, cfg, m, qx, wscale, ascale, dev)
     gs_other = GemmSetup(rotation(cfg_other.block_n), cfg_other, m, qx, wscale, ascale, dev)
@@ -478,7 +484,7 @@ def b200_arm(args, rank, world, local_rank):
         strong = None
         if n % world == 0 and n_s % 128 == 0:
             q_s = qw[:n_s].contiguous()
-            cfg_s = dg.default_config(m, n_s, k, layout=layout, pdl=pdl, independent_inputs=independent)
+            cfg_s = default_config(m, n_s, k, layout=layout, pdl=pdl, independent_inputs=independent)
             rot_s = Rotation(q_s, layout, cfg_s.block_n, dev)
             gs_s = GemmSetup(rot_s, cfg_s, m, qx, wscale[: n_s // 128].contiguous(), ascale, dev)
             gathered_s = torch.empty((world * m, n_s), dtype=torch.bfloat16, device=dev)
@@ -486,7 +492,7 @@ def b200_arm(args, rank, world, local_rank):
             t_s = timed(graphs)
             del graphs
 
-            cfg_sd = dg.default_config(m, n_s, k, layout=layout, pdl=pdl, independent_inputs=False)
+            cfg_sd = default_config(m, n_s, k, layout=layout, pdl=pdl, independent_inputs=False)
             gs_sd = gs_s if cfg_sd == cfg_s else GemmSetup(
                 Rotation(q_s, layout, cfg_sd.block_n, dev) if cfg_sd.block_n != cfg_s.block_n else rot_s,
                 cfg_sd, m, qx, wscale[: n_s // 128].contiguous(), ascale, dev)
@@ -579,7 +585,7 @@ def b200_arm(args, rank, world, local_rank):
             # order -- so one request's copies overlap the others' GEMMs.  The
             # GEMMs do not feed each other: the independent-inputs schedule.
             depth = max(1, args.e2e_depth)
-            cfg_p = dg.default_config(m, n, k, layout=layout, pdl=pdl,
+            cfg_p = default_config(m, n, k, layout=layout, pdl=pdl,
                                       independent_inputs=args.e2e_schedule == "independent")
             slots = []
             for _ in range(depth):
@@ -636,7 +642,7 @@ def b200_arm(args, rank, world, local_rank):
             grp = args.e2e_group
             nset = 2 * grp
             depth = nset
-            cfg_p = dg.default_config(m, n, k, layout=layout, pdl=pdl,
+            cfg_p = default_config(m, n, k, layout=layout, pdl=pdl,
                                       independent_inputs=args.e2e_schedule == "independent")
             fused_p = dg_tp.FusedGather(m, n, buffers=nset, device=dev)
             pdesc = [fused_p.descriptor(j) for j in range(nset)]
@@ -753,7 +759,7 @@ def b200_arm(args, rank, world, local_rank):
         steps_s = min(K, 1000)
         for mm in (1, 2, 4, 8, 16, 32, 64, 128):
             qx_m, as_m, _ = act(mm)
-            cfg_m = dg.default_config(mm, n, k, layout=layout, pdl=pdl, independent_inputs=independent)
+            cfg_m = default_config(mm, n, k, layout=layout, pdl=pdl, independent_inputs=independent)
             gs_m = GemmSetup(rotation(cfg_m.block_n), cfg_m, mm, qx_m, wscale, as_m, dev)
             graphs = capture(lambda i: gs_m.launch(i, stream), steps_s)
             t_m = timed(graphs)
@@ -783,7 +789,7 @@ def b200_arm(args, rank, world, local_rank):
         for (nn, kk) in (dn, up):
             gw = torch.Generator(device=dev).manual_seed(1000 + nn)
             wq, ws_ = quantize_pertensor(torch.randn((nn, kk), device=dev, generator=gw), torch.float8_e4m3fn)
-            cfg_l = dg.default_config(m, nn, kk, layout=layout, pdl=pdl, independent_inputs=False)
+            cfg_l = default_config(m, nn, kk, layout=layout, pdl=pdl, independent_inputs=False)
             packed = wq if layout == dg.LAYOUT_RAW else dg.prepack_weight(wq, cfg_l.block_n, layout)
             base[(nn, kk)] = (packed, torch.full(((nn + 127) // 128, kk // 128), float(ws_), device=dev), cfg_l)
         weights = [base[sh][0].clone() for sh in shapes]
