@@ -236,3 +236,24 @@ def test_default_plans_follow_the_split_rule(n, k, m, independent):
     assert p.block[0] == (192 if m <= 16 else 320 if m <= 64 else 384)
     if independent:
         assert p.num_ctas >= 32 or p.cluster == min(chunks, 8)
+
+
+@pytest.mark.parametrize("bn", list(range(32, 257, 8)))
+def test_cluster_partial_layout_rules(bn):
+    """The cluster reduction's index rules: a row's float4 unit c4 is stored at
+    c4 ^ (m % 8), a permutation of the row's bn/4 units only when bn is a
+    multiple of 32 -- which the planner requires -- and the S ranks' unit
+    ranges [r*q/S, (r+1)*q/S) cover all q = M * ceil(bn_t/4) units once."""
+    units = bn // 4
+    ok = all(sorted(c ^ m for c in range(units)) == list(range(units)) for m in range(8))
+    assert ok == (bn % 32 == 0)
+    plan = dg.B200Config(m_tile=8, block_n=bn, subs=2, stages=0, layout=dg.LAYOUT_PACKED_SWIZZLED,
+                         grid_ctas=dg.GRID_CLUSTER, split_k=4).plan(1, 7168, 16384)
+    if bn % 32:
+        assert plan.error is not None and "multiple of 32" in plan.error
+    for m_rows in (1, 7, 64):
+        for bn_t in (bn, max(4, bn - 20)):
+            q = m_rows * -(-bn_t // 4)
+            for s in (2, 3, 4, 8):
+                cover = [u for r in range(s) for u in range(r * q // s, (r + 1) * q // s)]
+                assert cover == list(range(q))
