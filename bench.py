@@ -779,6 +779,7 @@ def b200_arm(args, rank, world, local_rank):
     # quantiser of its bf16 output into the next layer's e4m3 activation and
     # 1x128 block scales.  Each layer has its own weight copy (7.2 GB, cold).
     chain = None
+    chain_last = None
     if not args.no_chain and world == 1:
         layers = 61
         passes = max(3, min(20, K // 500))
@@ -791,7 +792,11 @@ def b200_arm(args, rank, world, local_rank):
             wq, ws_ = quantize_pertensor(torch.randn((nn, kk), device=dev, generator=gw), torch.float8_e4m3fn)
             cfg_l = default_config(m, nn, kk, layout=layout, pdl=pdl, independent_inputs=False)
             packed = wq if layout == dg.LAYOUT_RAW else dg.prepack_weight(wq, cfg_l.block_n, layout)
-            base[(nn, kk)] = (packed, torch.full(((nn + 127) // 128, kk // 128), float(ws_), device=dev), cfg_l)
+            # Weight scales carry 1/sqrt(K), as a trained layer's output keeps the
+            # size of its input: 61 unnormalised N(0,1) layers would grow by
+            # ~sqrt(K) each and overflow bf16 within ~20 layers.
+            base[(nn, kk)] = (packed, torch.full(((nn + 127) // 128, kk // 128), float(ws_) / math.sqrt(kk),
+                                                 device=dev), cfg_l, wq)
         weights = [base[sh][0].clone() for sh in shapes]
         act_in = {k: torch.zeros((m, k), dtype=torch.uint8, device=dev), n: torch.zeros((m, n), dtype=torch.uint8, device=dev)}
         act_sc = {k: torch.zeros((m, k // 128), device=dev), n: torch.zeros((m, n // 128), device=dev)}
@@ -824,6 +829,13 @@ def b200_arm(args, rank, world, local_rank):
             raise RuntimeError(f"chain status {dg.status_string(int(st_c.item()))}")
         per_layer = t_chain / (layers * passes)
         bytes_layer = sum(nn * kk + m * kk + 2 * m * nn for (nn, kk) in shapes) / layers
+        # The last layer's input activation and scales, its bf16 output and the
+        # quantiser's bytes of that output are still in their buffers: the
+        # CPU leg below checks them against the oracle.
+        ln, lk = shapes[(layers * passes - 1) % layers]
+        chain_last = {"shape": (ln, lk), "act": act_in[lk].clone(), "act_scales": act_sc[lk].clone(),
+                      "out": outs[ln].clone(), "q": act_in[ln].clone(), "q_scales": act_sc[ln].clone(),
+                      "w": base[(ln, lk)][3], "w_scales": base[(ln, lk)][1]}
         chain = {"layers": layers, "passes_timed": passes, "shapes": "alternating 7168x16384 / 16384x7168",
                  "us_per_layer": per_layer * 1e6, "GBps": bytes_layer / per_layer / 1e9,
                  "frac_of_peak": bytes_layer / per_layer / 1e9 / peak,
@@ -934,6 +946,22 @@ def b200_arm(args, rank, world, local_rank):
         parity = {"rel_l2": oracle.rel_l2(got, want), "max_rel_err_floored": worst, "ok": bool(ok),
                   "other_pdl_mode": {"rel_l2": oracle.rel_l2(got_other, want), "max_rel_err_floored": worst_o,
                                      "ok": bool(ok_o)}}
+        if chain_last is not None:
+            # The timed chain's last layer: its GEMM against the oracle on the
+            # bytes it read, and its quantiser bit for bit.
+            cl = chain_last
+            got_c = cl["out"].float().cpu().numpy()
+            want_c = oracle.compute_reference(cl["act"].cpu().numpy(), cl["act_scales"].cpu().numpy(),
+                                              cl["w"].view(torch.uint8).cpu().numpy(),
+                                              cl["w_scales"].cpu().numpy(), threads=os.cpu_count() or 1)
+            ok_c, worst_c = oracle.elementwise_ok(got_c, want_c)
+            rl2_c = oracle.rel_l2(got_c, want_c)
+            want_q, want_s = oracle.quantize_rows(got_c)
+            q_ok = bool(np.array_equal(cl["q"].cpu().numpy(), want_q) and
+                        np.array_equal(cl["q_scales"].cpu().numpy(), want_s))
+            chain["parity"] = {"layer": f"last ({cl['shape'][0]}x{cl['shape'][1]})", "rel_l2": rl2_c,
+                               "max_rel_err_floored": worst_c, "quantiser_bit_exact": q_ok,
+                               "ok": bool(ok_c and rl2_c <= oracle.REL_L2_GATE and q_ok)}
 
     if world > 1:
         dist.barrier()

@@ -244,7 +244,10 @@ __global__ void prepack_kernel(const uint4* __restrict__ src, uint4* __restrict_
 }
 
 // Device address of g_static_scratch on the current device, looked up once per
-// device (cudaGetSymbolAddress, with that device current) and cached.
+// device (cudaGetSymbolAddress, with that device current) and cached for the
+// life of the process: the cache assumes the device's primary context (which
+// holds the array) lives as long as the process, i.e. nobody calls
+// cudaDeviceReset on that device and then this entry point again.
 constexpr int kMaxScratchDevices = 64;
 std::mutex g_scratch_mutex;
 void* g_scratch_ptr[kMaxScratchDevices] = {};
@@ -289,6 +292,7 @@ AddressRangeFn address_range_fn() {
 struct OpenedAllocation {
   cudaIpcMemHandle_t handle;
   char* base;
+  size_t size;   // bytes of the mapping (cuMemGetAddressRange of base)
   int refs;
 };
 std::mutex g_ipc_mutex;
@@ -477,16 +481,26 @@ int dg_ipc_import(const void* handle64, unsigned long long offset, void** ptr) {
   std::lock_guard<std::mutex> lock(g_ipc_mutex);
   for (int i = 0; i < g_ipc_count; ++i) {
     if (std::memcmp(&g_ipc_open[i].handle, &h, sizeof(h)) == 0) {
+      if (offset >= g_ipc_open[i].size) return cudaErrorInvalidValue;
       ++g_ipc_open[i].refs;
       *ptr = g_ipc_open[i].base + offset;
       return cudaSuccess;
     }
   }
   if (g_ipc_count == 64) return cudaErrorMemoryAllocation;
+  AddressRangeFn range = address_range_fn();
+  if (range == nullptr) return cudaErrorInsufficientDriver;
   void* base = nullptr;
   const cudaError_t err = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
   if (err != cudaSuccess) return err;
-  g_ipc_open[g_ipc_count] = {h, static_cast<char*>(base), 1};
+  CUdeviceptr rbase = 0;
+  size_t size = 0;
+  if (range(&rbase, &size, reinterpret_cast<CUdeviceptr>(base)) != CUDA_SUCCESS ||
+      reinterpret_cast<char*>(rbase) != static_cast<char*>(base) || offset >= size) {
+    cudaIpcCloseMemHandle(base);
+    return cudaErrorInvalidValue;
+  }
+  g_ipc_open[g_ipc_count] = {h, static_cast<char*>(base), size, 1};
   ++g_ipc_count;
   *ptr = static_cast<char*>(base) + offset;
   return cudaSuccess;
@@ -495,11 +509,12 @@ int dg_ipc_import(const void* handle64, unsigned long long offset, void** ptr) {
 int dg_ipc_release(void* ptr) {
   if (ptr == nullptr) return cudaErrorInvalidValue;
   std::lock_guard<std::mutex> lock(g_ipc_mutex);
-  // The opened allocation that holds ptr: the one with the largest base <= ptr.
+  // The opened mapping that holds ptr; a pointer inside none of them (never
+  // imported, or released already) is rejected and changes nothing.
   int best = -1;
+  const char* q = static_cast<const char*>(ptr);
   for (int i = 0; i < g_ipc_count; ++i)
-    if (g_ipc_open[i].base <= static_cast<char*>(ptr) && (best < 0 || g_ipc_open[i].base > g_ipc_open[best].base))
-      best = i;
+    if (g_ipc_open[i].base <= q && q < g_ipc_open[i].base + g_ipc_open[i].size) best = i;
   if (best < 0) return cudaErrorInvalidValue;
   if (--g_ipc_open[best].refs > 0) return cudaSuccess;
   const cudaError_t err = cudaIpcCloseMemHandle(g_ipc_open[best].base);

@@ -109,7 +109,7 @@ enum Layout : int {
 
 enum Flags : int {
   kFlagPdlTrigger = 1,     // producer issues griddepcontrol.launch_dependents
-  kFlagInjectTimeout = 2,  // test hook: the MMA warp waits on a barrier nobody arrives on
+  kFlagInjectTimeout = 2,  // test hook: CTA 0's MMA warp waits on a barrier nobody arrives on
   // The activation and both scale arrays are not written by the preceding
   // grid of the stream (e.g. back-to-back GEMMs on one activation): they may
   // be read before griddepcontrol.wait.  Global writes still wait.
@@ -957,7 +957,10 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
       const uint32_t a_base = smem_addr(a_region);
       bool any_issued = false;
       bool ok = true;
-      if (p.flags & kFlagInjectTimeout) {
+      // Test hook: CTA 0 waits on a barrier nobody arrives on, so its bounded
+      // wait runs out and it aborts while the other CTAs finish (a split tile
+      // it shares is then left with a partial arrival count).
+      if ((p.flags & kFlagInjectTimeout) && cta == 0) {
         ok = mbar_wait_bounded(never_bar, 0, abort_flag, p.status, kErrInjectedTimeout, timeout);
       }
       int acc = 0;  // running accumulator-buffer index

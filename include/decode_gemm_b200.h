@@ -66,8 +66,9 @@ extern "C" {
 #define DG_GRID_CLUSTER (-2)
 
 /* Kernel flags (dg_config.flags). */
-#define DG_FLAG_INJECT_TIMEOUT 2     /* tests: one wait can never complete, so the bounded
-                                        wait expires and the kernel reports status 0x51 */
+#define DG_FLAG_INJECT_TIMEOUT 2     /* tests: one wait of CTA 0 can never complete, so its
+                                        bounded wait expires, CTA 0 aborts (the other CTAs
+                                        finish) and the kernel reports status 0x51 */
 #define DG_FLAG_INDEPENDENT_INPUTS 4 /* the activation and scales are not written by the
                                         preceding kernel on the stream (e.g. back-to-back
                                         GEMMs on one activation): with programmatic
@@ -212,7 +213,8 @@ int dg_gather_wait(const dg_gather* g, int* status, unsigned long long timeout_n
    dg_ipc_export: 64-byte handle of the allocation holding `ptr` and ptr's
    offset in it.  dg_ipc_import: maps a peer's allocation (once per process,
    reference-counted) and returns the peer pointer; dg_ipc_release drops one
-   reference (`ptr` as returned by dg_ipc_import). */
+   reference (`ptr` as returned by dg_ipc_import; a pointer inside no imported
+   mapping returns cudaErrorInvalidValue and changes nothing). */
 int dg_ipc_export(const void* ptr, void* handle64, unsigned long long* offset);
 int dg_ipc_import(const void* handle64, unsigned long long offset, void** ptr);
 int dg_ipc_release(void* ptr);
@@ -234,7 +236,12 @@ int dg_ipc_release(void* ptr);
      DG_STATIC_SEM_INTS tickets (dg_plan reports both as ws_floats, sem_ints).
    - The first call on each device looks up the array's address
      (cudaGetSymbolAddress with that device current): make that first call
-     before any stream capture on the device.
+     before any stream capture on the device.  The address is kept for the
+     life of the process, so the device's primary context must live as long:
+     no cudaDeviceReset on that device before a later call.
+   - The ticket clear is a memset node between the previous kernel on the
+     stream and this launch, so under programmatic dependent launch this call
+     does not overlap the kernel before it (dg_launch does).
    - Every call on a device shares the one array: calls that overlap on the GPU
      (other streams, other host threads) race.  Calls in order on one stream are
      safe.

@@ -19,6 +19,12 @@
 namespace decode_gemm {
 namespace prepack {
 
+// Layout constants of the reference's prepack namespace: one 128-byte K block
+// per packed row, moved as 16-byte vectors.
+inline constexpr uint32_t kKBlock = 128;
+inline constexpr uint32_t kBytesPerUint4 = 16;
+inline constexpr uint32_t kUint4PerKBlock = kKBlock / kBytesPerUint4;
+
 inline int padded_n(int n, int output_rows_per_cta) {
   return ((n + output_rows_per_cta - 1) / output_rows_per_cta) * output_rows_per_cta;
 }
@@ -30,7 +36,7 @@ inline size_t packed_weight_bytes(int n, int k, int output_rows_per_cta) {
 // Returns cudaErrorInvalidValue when K is not a multiple of 128.
 template <int OutputRowsPerCta, int OutputTilesPerCta = 1>
 inline cudaError_t launch_prepack_weight(const __nv_fp8_e4m3* source, __nv_fp8_e4m3* destination, int n, int k,
-                                         cudaStream_t stream) {
+                                         cudaStream_t stream = nullptr) {
   static_assert(OutputRowsPerCta > 0 && OutputRowsPerCta % 8 == 0,
                 "OutputRowsPerCta must be a positive multiple of 8");
   static_assert(OutputTilesPerCta > 0, "OutputTilesPerCta must be positive");

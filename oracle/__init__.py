@@ -46,9 +46,26 @@ def smoke_act_seed(shape_seed: int, m: int) -> int:
     return (shape_seed ^ ((0x9E3779B97F4A7C15 * m) & 0xFFFFFFFFFFFFFFFF)) & 0xFFFFFFFFFFFFFFFF
 
 
+def reference_root():
+    """The reference checkout the reference builds compile from: the
+    environment variable DG_REF_ROOT, else a ``reference`` directory beside
+    this repository; None when neither holds the reference's smoke test."""
+    cands = [os.environ.get("DG_REF_ROOT", ""),
+             os.path.join(os.path.dirname(os.path.dirname(_HERE)), "reference")]
+    for c in cands:
+        if c and os.path.isfile(os.path.join(c, "kernels", "smoke_test.cu")):
+            return os.path.abspath(c)
+    return None
+
+
 def build() -> None:
-    """Compile liboracle.so (and the reference build when its source exists)."""
-    subprocess.run(["make", "-s", "-j", str(max(1, min(8, os.cpu_count() or 1))), "-C", _HERE], check=True)
+    """Compile liboracle.so, plus the reference builds (``_ref/``) when a
+    reference checkout is found (:func:`reference_root`)."""
+    cmd = ["make", "-s", "-j", str(max(1, min(8, os.cpu_count() or 1))), "-C", _HERE]
+    ref = reference_root()
+    if ref is not None:
+        cmd.append(f"REF_ROOT={ref}")
+    subprocess.run(cmd, check=True)
 
 
 def _ptr(a: np.ndarray, t):

@@ -1,0 +1,177 @@
+"""GPU parity of the dependent decode-layer chain that bench.py times
+(``chain_61``): every layer is a GEMM launched with programmatic dependent
+launch in the dependent mode -- weights requested before
+griddepcontrol.wait, the activation and scales read after it -- followed by
+the GPU quantiser of its bf16 output into the next layer's e4m3 activation
+and 1x128 scales, also launched with the PDL attribute (it releases its
+dependents at once and waits for the GEMM before reading).  The chain is
+captured in a CUDA graph, as in the benchmark, so every edge is a
+programmatic one.
+
+The hazard this guards (the reference's README, kernels/README.md:148-151 and
+833-858): under PDL a launch may start while its predecessor still runs, so a
+read placed before griddepcontrol.wait, or a trigger placed so that a grid's
+writes race its successor's reads, produces wrong numbers rather than an
+error.  Every activation and output buffer is filled with garbage before the
+replay, so a stale read shows up as a mismatch.
+
+Checks, layer by layer: the GEMM's bf16 output against the oracle
+(``compute_reference`` on the e4m3 bytes and scales the layer actually read;
+rel_l2 <= 2e-3 and the per-element bound), and the quantiser's bytes and
+scales against the oracle's restatement of the reference's host quantisation,
+bit for bit.  A second replay is bit-identical to the first.  Then the
+benchmark's own buffer scheme -- one output and one activation buffer per
+layer width, reused by every layer of that width, two passes over the layer
+list in one graph -- must end on exactly the bytes of the chain with a
+buffer per layer.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import decode_opt_b200 as dg
+import oracle
+from helpers import check_against_oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def quantize_blocks(w):
+    """float32 [n, k] (device) -> e4m3 bytes [n, k] and 128x128 block scales
+    [ceil(n/128), k/128] (amax/448 per block)."""
+    n, k = w.shape
+    nb = (n + 127) // 128
+    wp = torch.zeros((nb * 128, k), device=w.device)
+    wp[:n] = w
+    blocks = wp.view(nb, 128, k // 128, 128)
+    scale = blocks.abs().amax(dim=(1, 3)).clamp_min(1e-4) / 448.0
+    q = (blocks / scale[:, None, :, None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return q.view(nb * 128, k)[:n].contiguous().view(torch.uint8), scale.contiguous()
+
+
+class Chain:
+    """Weights of `layers` layers alternating (n, k) and (k, n), their
+    configurations, plans and packed copies."""
+
+    def __init__(self, m, n, k, layers, seed):
+        self.m = m
+        self.shapes = [(n, k) if i % 2 == 0 else (k, n) for i in range(layers)]
+        self.dev = torch.device("cuda")
+        self.w_raw, self.w_sc, self.w_packed, self.cfgs = [], [], [], []
+        g = torch.Generator(device=self.dev).manual_seed(seed)
+        for (nn, kk) in self.shapes:
+            # 1/sqrt(K) keeps every layer's output the size of its input.
+            q, s = quantize_blocks(torch.randn((nn, kk), device=self.dev, generator=g) / kk ** 0.5)
+            cfg = dg.default_config(m, nn, kk, layout=dg.LAYOUT_PACKED_SWIZZLED, pdl=True, independent_inputs=False)
+            self.w_raw.append(q)
+            self.w_sc.append(s)
+            self.w_packed.append(dg.prepack_weight(q, cfg.block_n, cfg.layout))
+            self.cfgs.append(cfg)
+        x = torch.randn((m, k), device=self.dev, generator=g).bfloat16()
+        self.a0, self.s0 = dg.quantize_activation(x)
+        torch.cuda.synchronize()
+        ws_floats = max(max(c.plan(m, *sh).ws_floats for c, sh in zip(self.cfgs, self.shapes)), 1)
+        sem_ints = max(max(c.plan(m, *sh).sem_ints for c, sh in zip(self.cfgs, self.shapes)), 1)
+        self.ws = torch.zeros(ws_floats, device=self.dev)
+        self.sem = torch.zeros(sem_ints, dtype=torch.int32, device=self.dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        self.garbage = torch.Generator(device=self.dev).manual_seed(seed + 1)
+
+    def fill_garbage(self, t):
+        """Overwrite a buffer with random bytes (stale data for a racing read)."""
+        b = t.view(torch.uint8).view(-1)
+        b.copy_(torch.randint(0, 256, b.shape, device=self.dev, dtype=torch.uint8, generator=self.garbage))
+
+    def launches(self, acts, scales, outs, order):
+        """Problems and maps for layer list `order` (indices into the weights):
+        step j reads acts[j]/scales[j] and writes outs[j]; its quantiser writes
+        acts[j+1]/scales[j+1]."""
+        steps = []
+        for j, li in enumerate(order):
+            nn, kk = self.shapes[li]
+            cfg = self.cfgs[li]
+            p = dg.Problem(self.m, nn, kk, acts[j], self.w_packed[li], self.w_sc[li], scales[j], outs[j], self.ws,
+                           self.sem, self.status)
+            steps.append((cfg, p, dg.make_weight_tma(cfg, p), dg.make_activation_tma(cfg, p), outs[j], acts[j + 1],
+                          scales[j + 1]))
+        return steps
+
+    def capture(self, steps):
+        stream = torch.cuda.Stream()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(graph, stream=stream):
+                for (cfg, p, wm, am, out, nxt_a, nxt_s) in steps:
+                    rc = dg.launch_with_maps(cfg, p, wm, am, stream, pdl_attr=cfg.pdl)
+                    assert rc == 0, rc
+                    dg.quantize_activation(out, out=nxt_a, scales=nxt_s, stream=stream, pdl_attr=True)
+        return stream, graph
+
+
+def run_graph(stream, graph):
+    with torch.cuda.stream(stream):
+        graph.replay()
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("m,n,k,layers", [(1, 7168, 16384, 8), (8, 7168, 16384, 6), (32, 7168, 16384, 4),
+                                          (128, 2048, 4096, 6)])
+def test_pdl_chain_in_graph_matches_oracle_layer_by_layer(m, n, k, layers):
+    ch = Chain(m, n, k, layers, seed=4242 + m)
+    total = 2 * layers                       # two passes over the layer list
+    order = [i % layers for i in range(total)]
+    widths = [ch.shapes[li][1] for li in order] + [ch.shapes[order[-1]][0]]
+    acts = [ch.a0.clone()] + [torch.empty((m, w), dtype=torch.uint8, device=ch.dev) for w in widths[1:]]
+    scales = [ch.s0.clone()] + [torch.empty((m, w // 128), device=ch.dev) for w in widths[1:]]
+    outs = [torch.empty((m, ch.shapes[li][0]), dtype=torch.bfloat16, device=ch.dev) for li in order]
+    for t in acts[1:] + scales[1:] + outs:
+        ch.fill_garbage(t)
+    stream, graph = ch.capture(ch.launches(acts, scales, outs, order))
+    run_graph(stream, graph)
+    assert int(ch.status.item()) == 0, dg.status_string(int(ch.status.item()))
+    assert int(ch.sem.abs().sum().item()) == 0
+
+    first = [o.clone() for o in outs] + [a.clone() for a in acts] + [s.clone() for s in scales]
+    for j, li in enumerate(order):
+        a_h = acts[j].cpu().numpy()
+        s_h = scales[j].cpu().numpy()
+        want = oracle.compute_reference(a_h, s_h, ch.w_raw[li].cpu().numpy(), ch.w_sc[li].cpu().numpy(), threads=8)
+        got = outs[j].float().cpu().numpy()
+        ok, rl2, worst = check_against_oracle(got, want)
+        assert ok, (j, rl2, worst)
+        want_q, want_s = oracle.quantize_rows(got)
+        assert np.array_equal(acts[j + 1].cpu().numpy(), want_q), j
+        assert np.array_equal(scales[j + 1].cpu().numpy(), want_s), j
+
+    # A second replay over fresh garbage: bit-identical.
+    for t in acts[1:] + scales[1:] + outs:
+        ch.fill_garbage(t)
+    run_graph(stream, graph)
+    again = [o for o in outs] + [a for a in acts] + [s for s in scales]
+    for x, y in zip(first, again):
+        assert torch.equal(x.view(torch.uint8), y.view(torch.uint8))
+    del graph
+
+    # The benchmark's buffer scheme: per width one output and one activation
+    # buffer, reused across layers and passes; layer j reads act[K_j] and
+    # writes out[N_j], its quantiser writes act[N_j].
+    act_by_w = {w: torch.empty((m, w), dtype=torch.uint8, device=ch.dev) for w in (n, k)}
+    sc_by_w = {w: torch.empty((m, w // 128), device=ch.dev) for w in (n, k)}
+    out_by_w = {w: torch.empty((m, w), dtype=torch.bfloat16, device=ch.dev) for w in (n, k)}
+    for t in list(act_by_w.values()) + list(sc_by_w.values()) + list(out_by_w.values()):
+        ch.fill_garbage(t)
+    act_by_w[k].copy_(ch.a0)
+    sc_by_w[k].copy_(ch.s0)
+    r_acts = [act_by_w[ch.shapes[li][1]] for li in order] + [act_by_w[ch.shapes[order[-1]][0]]]
+    r_sc = [sc_by_w[ch.shapes[li][1]] for li in order] + [sc_by_w[ch.shapes[order[-1]][0]]]
+    r_outs = [out_by_w[ch.shapes[li][0]] for li in order]
+    stream2, graph2 = ch.capture(ch.launches(r_acts, r_sc, r_outs, order))
+    run_graph(stream2, graph2)
+    assert int(ch.status.item()) == 0
+    assert torch.equal(r_outs[-1].view(torch.uint8), outs[-1].view(torch.uint8))
+    assert torch.equal(r_acts[-1], acts[-1])
+    assert torch.equal(r_sc[-1], scales[-1])
+    # and the last layer's input, still in its buffer, equals the chain's
+    assert torch.equal(r_acts[-2], acts[-2])
+    del graph2

@@ -1,8 +1,12 @@
 """GPU tests of dg_launch_static_scratch, the entry point that allocates
 nothing: its split-K tickets and workspace live in the library's static
 __device__ array.  Each case runs two calls in a row through the C ABI (the
-second sees the first call's leftover scratch) and compares both outputs with
-dg_launch on caller-allocated workspace.  Named so pytest collects it last.
+second sees the first call's leftover scratch) and requires both outputs to
+equal, bit for bit, dg_launch's on caller-allocated workspace: both run the
+same plan and the split reduction sums the slabs in a fixed order, so the
+results are deterministic.  Neither torch's allocator nor the device's free
+memory (cudaMemGetInfo) may change across the calls.  Named so pytest
+collects it last.
 """
 
 import ctypes
@@ -49,12 +53,20 @@ def _with_workspace(cfg, m, act, a_s, w_dev, w_s, status):
     return out
 
 
-def _close(got, want):
-    g, w = got.float(), want.float()
-    rms = w.pow(2).mean().sqrt().item()
-    rel = ((g - w).norm() / w.norm().clamp_min(1e-30)).item()
-    bound = 1e-2 * w.abs().clamp_min(1e-2 * rms)
-    return rel <= 1e-6 and bool(((g - w).abs() <= bound).all())
+def _static_call(cfg, m, act, a_s, w_dev, w_s, out, status, stream=None):
+    import torch
+    # splitk_ws / splitk_sem are ignored: pass NULL.
+    p = dg.Problem(m, N, K, act, w_dev, w_s, a_s, out, None, None, status)
+    info = _lib.DgPlanInfo()
+    s = stream.cuda_stream if stream is not None else torch.cuda.current_stream().cuda_stream
+    rc = _lib.lib().dg_launch_static_scratch(ctypes.byref(cfg.to_dg()), ctypes.byref(p.to_dg()), s,
+                                             ctypes.byref(info))
+    return rc, info
+
+
+def _bit_equal(got, want):
+    import torch
+    return torch.equal(got.view(torch.int16), want.view(torch.int16))
 
 
 @pytest.mark.parametrize("m,layout", [(1, dg.LAYOUT_PACKED_SWIZZLED), (8, dg.LAYOUT_RAW),
@@ -67,22 +79,66 @@ def test_static_scratch_matches_dg_launch_twice(m, layout):
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     wants = [_with_workspace(cfg, m, a, s, w_dev, w_s, status) for a, s in inputs]
     outs = [torch.zeros(m, N, dtype=torch.bfloat16, device="cuda") for _ in inputs]
+    warm = torch.zeros(m, N, dtype=torch.bfloat16, device="cuda")
+    # One call first: the library looks up its array's address on the first
+    # call on a device and the kernel module may load lazily.
+    rc, info = _static_call(cfg, m, *inputs[0], w_dev, w_s, warm, status)
+    assert rc == 0, info.error
     torch.cuda.synchronize()
     allocated = torch.cuda.memory_allocated()
+    free_before, _ = torch.cuda.mem_get_info()
     for (act, a_s), out in zip(inputs, outs):
-        # splitk_ws / splitk_sem are ignored: pass NULL.
-        p = dg.Problem(m, N, K, act, w_dev, w_s, a_s, out, None, None, status)
-        info = _lib.DgPlanInfo()
-        rc = _lib.lib().dg_launch_static_scratch(ctypes.byref(cfg.to_dg()), ctypes.byref(p.to_dg()),
-                                                 torch.cuda.current_stream().cuda_stream, ctypes.byref(info))
+        rc, info = _static_call(cfg, m, act, a_s, w_dev, w_s, out, status)
         assert rc == 0, info.error
         assert info.max_slabs > 1, "the case must split tiles, so that the static scratch is used"
         assert info.ws_floats <= _lib.STATIC_WS_FLOATS
     torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
     assert torch.cuda.memory_allocated() == allocated
+    assert free_after == free_before, (free_before, free_after)
     assert int(status.item()) == 0, dg.status_string(int(status.item()))
     for got, want in zip(outs, wants):
-        assert _close(got, want)
+        assert _bit_equal(got, want)
+
+
+def test_static_scratch_recovers_after_an_aborted_call():
+    """A call whose CTAs abort (the test hook makes one bounded wait run out)
+    leaves tickets of the shared array non-zero; the next call clears the
+    tickets it uses and must again equal dg_launch bit for bit."""
+    import torch
+    m, layout = 8, dg.LAYOUT_PACKED_SWIZZLED
+    cfg = dg.default_config(m, N, K, layout=layout, schedule="stream_k")
+    w_dev, w_s = _weight(layout)
+    act, a_s = _inputs(m, 300)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    want = _with_workspace(cfg, m, act, a_s, w_dev, w_s, status)
+    torch.cuda.synchronize()
+    from dataclasses import replace
+    bad = replace(cfg, flags=cfg.flags | dg.FLAG_INJECT_TIMEOUT, timeout_ns=20_000_000)
+    junk = torch.zeros(m, N, dtype=torch.bfloat16, device="cuda")
+    # On caller-allocated scratch the same aborted call visibly leaves a
+    # ticket non-zero (CTA 0 never arrives at the tile it shares).
+    plan = cfg.plan(m, N, K)
+    sem = torch.zeros(max(plan.sem_ints, 1), dtype=torch.int32, device="cuda")
+    ws = torch.empty(max(plan.ws_floats, 1), dtype=torch.float32, device="cuda")
+    p = dg.Problem(m, N, K, act, w_dev, w_s, a_s, junk, ws, sem, status)
+    assert _lib.lib().dg_launch(ctypes.byref(bad.to_dg()), ctypes.byref(p.to_dg()),
+                                torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == dg.ERR_INJECTED_TIMEOUT
+    assert int(sem.ne(0).sum().item()) > 0
+    status.zero_()
+    rc, info = _static_call(bad, m, act, a_s, w_dev, w_s, junk, status)
+    assert rc == 0, info.error
+    torch.cuda.synchronize()
+    assert int(status.item()) == dg.ERR_INJECTED_TIMEOUT, dg.status_string(int(status.item()))
+    status.zero_()
+    out = torch.zeros(m, N, dtype=torch.bfloat16, device="cuda")
+    rc, info = _static_call(cfg, m, act, a_s, w_dev, w_s, out, status)
+    assert rc == 0, info.error
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, dg.status_string(int(status.item()))
+    assert _bit_equal(out, want)
 
 
 def test_static_scratch_rejects_plans_over_the_limit():
