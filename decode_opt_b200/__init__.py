@@ -42,6 +42,7 @@ from ._lib import (ERR_INJECTED_TIMEOUT, FLAG_INDEPENDENT_INPUTS, FLAG_INJECT_TI
                    LAYOUT_PACKED_SWIZZLED, LAYOUT_RAW, STATUS_OK, DgConfig, DgPlanInfo, DgProblem, TensorMap)
 
 __all__ = [
+    "cluster_min_stages",
     "KernelConfig", "B200Config", "Problem", "LaunchPlan", "make_launch_plan", "make_weight_tma",
     "make_activation_tma", "launch_with_maps", "launch", "launch_gather", "quantize_activation", "padded_n",
     "packed_weight_bytes",
@@ -99,10 +100,12 @@ class B200Config:
     epi_warps: int = 0
     flags: int = 0
     timeout_ns: int = 0
+    pack_rows: int = 0
 
     def to_dg(self) -> DgConfig:
         return DgConfig(self.m_tile, self.block_n, self.subs, self.stages, self.layout, int(self.pdl),
-                        self.split_k, self.grid_ctas, self.epi_warps, self.flags, self.timeout_ns)
+                        self.split_k, self.grid_ctas, self.epi_warps, self.flags, self.timeout_ns,
+                        self.pack_rows)
 
     def plan(self, m: int, n: int, k: int) -> "LaunchPlan":
         info = DgPlanInfo()
@@ -124,6 +127,12 @@ class B200Config:
     @property
     def prepacked(self) -> bool:
         return self.layout != LAYOUT_RAW
+
+    @property
+    def packed_rows(self) -> int:
+        """Rows per tile of the packed weight layout this configuration reads
+        (the ``block_n`` argument of :func:`prepack_weight`)."""
+        return self.pack_rows or self.block_n
 
 
 def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool = True,
@@ -174,6 +183,21 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
     return base
 
 
+def cluster_min_stages(m: int, subs: int, block_n: int, mma_m: int) -> int:
+    """The shallowest ring whose shared memory holds the fp32 partial of m
+    rows (rows padded to a multiple of 32 floats) that cluster split-K keeps
+    there (dg::cluster_min_stages)."""
+    def align1k(v):
+        return (v + 1023) & ~1023
+    stride = (block_n + 31) & ~31
+    pad = (((block_n + 15) // 16) * 16 - block_n) * K_BLOCK
+    s = 1
+    while s < 16 and (align1k(s * subs * block_n * K_BLOCK + pad) + align1k(s * subs * mma_m * K_BLOCK)
+                      < m * stride * 4):
+        s += 1
+    return s
+
+
 @dataclass(frozen=True)
 class KernelConfig:
     """The reference's ``decode_gemm::KernelConfig`` (kernels/decode_gemm.cuh:147-347).
@@ -182,23 +206,32 @@ class KernelConfig:
     they map onto :class:`B200Config` as follows:
 
     * ``M_TILE`` -> ``m_tile`` (the batch is the tcgen05 M side, padded to 64,
-      or 128 for M_TILE=128); ``OUTPUT_ROWS_PER_CTA`` -> ``block_n`` (BM), the
-      weight rows per tile on the tcgen05 N side (B200 extension: 128 or 256);
+      or 128 for M_TILE=128);
+    * ``OUTPUT_ROWS_PER_CTA`` (BM) -> the packed layout's tile height
+      (``pack_rows``); a CTA takes ``T = 256 // BM`` consecutive BM-row tiles
+      (the reference's TILES_PER_CTA idea sized for the tcgen05 N side), so
+      ``block_n = T * BM`` weight rows per MMA (224-256 for BM 32..64);
     * ``SUBS_PER_STAGE`` -> ``subs``; ``NUM_MATH_WG * STAGES_PER_WG`` -> ``stages``
-      (the ring depth, reduced if it does not fit in 227 KiB);
+      (the ring depth, raised to hold the cluster partial and reduced if it
+      does not fit in 227 KiB);
     * ``PREPACK`` -> weight layout packed (True) or raw (False);
     * ``PDL`` or ``EPI_OVERLAP`` -> ``griddepcontrol.launch_dependents`` after
       the producer's first ring pass (the sm_100a kernel has one trigger
       point, earlier than the reference's after-the-last-TMA trigger);
       ``launch`` sets programmatic stream serialization when ``PDL``;
-    * ``SPLIT_K_CTA`` / ``SPLITK_FACTOR`` -> ``split_k`` = kSplitKFactor with the
-      reference's normalisation (0: follow the bool, 1: off, 2/4/8: S);
+    * ``SPLIT_K_CTA`` / ``SPLITK_FACTOR`` -> the cluster split of every tile's
+      K range: max(kSplitKFactor, 4), kSplitKFactor with the reference's
+      normalisation (0: follow the bool, 1: off, 2/4/8: S) -- the reference's
+      factor split BM-row tiles and a CTA tile here spans T of them; grid
+      ``(ceil(N / block_n), S)``, one thread-block cluster per tile, reduced
+      in rank order through distributed shared memory (deterministic; the
+      workspace and semaphore are not touched);
     * ``NUM_MATH_WG``, ``MATH_REGS``, ``PROD_REGS``, ``SINGLE_PRODUCER_WARP``,
       ``PRELOAD_ACT``, ``SCALE_IN_SMEM``, ``TILES_PER_CTA`` describe the SM90
       warp-group / register split.  They are range-checked exactly as the
       reference's static_asserts check them and otherwise do not change the
       sm_100a kernel, whose warp roles are fixed (TMA warp, MMA warp,
-      epilogue warps) and which schedules one output tile per CTA slice.
+      epilogue warps).
     """
 
     M_TILE: int
@@ -308,15 +341,36 @@ class KernelConfig:
     def kStages(self) -> int:
         return self.NUM_MATH_WG * self.STAGES_PER_WG
 
+    @property
+    def kPackTiles(self) -> int:
+        """BM-row tiles one CTA tile spans."""
+        bm = self.OUTPUT_ROWS_PER_CTA
+        return 256 // bm if bm <= 128 else 1
+
+    @property
+    def kBlockN(self) -> int:
+        """Weight rows per CTA tile (the tcgen05 N side)."""
+        return self.OUTPUT_ROWS_PER_CTA * self.kPackTiles
+
+    @property
+    def kClusterSplit(self) -> int:
+        """CTAs per tile (one cluster), splitting its K range: at least 4,
+        SPLITK_FACTOR when that asks for more."""
+        return max(self.kSplitKFactor, 4)
+
     def to_b200(self) -> B200Config:
-        return B200Config(m_tile=self.M_TILE, block_n=self.OUTPUT_ROWS_PER_CTA,
-                          subs=self.SUBS_PER_STAGE, stages=min(self.kStages, 16),
+        bn = self.kBlockN
+        mma_m = 64 if self.M_TILE <= 32 else 128
+        stages = min(max(self.kStages, cluster_min_stages(self.M_TILE, self.SUBS_PER_STAGE, bn, mma_m)), 16)
+        return B200Config(m_tile=self.M_TILE, block_n=bn,
+                          pack_rows=self.OUTPUT_ROWS_PER_CTA if (self.PREPACK and self.kPackTiles > 1) else 0,
+                          subs=self.SUBS_PER_STAGE, stages=stages,
                           layout=LAYOUT_PACKED if self.PREPACK else LAYOUT_RAW,
-                          pdl=bool(self.PDL or self.EPI_OVERLAP), split_k=self.kSplitKFactor,
-                          grid_ctas=0)
+                          pdl=bool(self.PDL or self.EPI_OVERLAP), split_k=self.kClusterSplit,
+                          grid_ctas=GRID_CLUSTER)
 
     def _fitted(self, m: int, n: int, k: int) -> B200Config:
-        # The ring depth the reference asks for, reduced until it fits.
+        # The ring depth asked for, reduced until it fits.
         cfg = self.to_b200()
         stages = cfg.stages
         while stages > 1:
@@ -330,10 +384,10 @@ class KernelConfig:
         return (n + self.OUTPUT_ROWS_PER_CTA - 1) // self.OUTPUT_ROWS_PER_CTA
 
     def num_ctas_x(self, n: int) -> int:
-        return self.num_output_tiles(n)
+        return (n + self.kBlockN - 1) // self.kBlockN
 
     def num_ctas(self, n: int) -> int:
-        return self.num_ctas_x(n) * self.kSplitKFactor
+        return self.num_ctas_x(n) * self.kClusterSplit
 
     def k_ok_for_splitk(self, k: int) -> bool:
         return k % (K_BLOCK * self.SUBS_PER_STAGE * self.kWgsPerOutputTile * self.kSplitKFactor) == 0
@@ -443,6 +497,9 @@ def make_launch_plan(cfg, p: Problem) -> LaunchPlan:
         plan = _b200(cfg, p).plan(p.M, p.N, p.K)
         if ref_err is not None:
             plan.error = ref_err
+        # The reference's meanings: BM-row tiles and the packed layout's rows.
+        plan.num_output_tiles = cfg.num_output_tiles(p.N)
+        plan.padded_n = padded_n(p.N, cfg.OUTPUT_ROWS_PER_CTA)
         return plan
     return cfg.plan(p.M, p.N, p.K)
 

@@ -13,7 +13,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libdecode_gemm_b200.so")
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 LAYOUT_RAW = 0
 LAYOUT_PACKED = 1
@@ -52,6 +52,7 @@ class DgConfig(ctypes.Structure):
         ("epi_warps", ctypes.c_int),
         ("flags", ctypes.c_int),
         ("timeout_ns", ctypes.c_ulonglong),
+        ("pack_rows", ctypes.c_int),
     ]
 
 

@@ -1024,7 +1024,7 @@ class Session:
             return res
         res.padded_n, res.smem, res.ctas, res.threads = lp.padded_n, lp.smem_bytes, lp.num_ctas, lp.block[0]
         res.mechanism = "launch" if self.o.force_api_launch else "launch_with_maps"
-        sets = self.cache.get(md, b200.layout, b200.block_n)
+        sets = self.cache.get(md, b200.layout, b200.packed_rows)
         res.weight_sets, res.set_bytes = len(sets), sets[0].numel()
         out = torch.empty((m, n), dtype=torch.bfloat16, device=self.dev)
         ws = torch.zeros(max(lp.ws_floats, 1), dtype=torch.float32, device=self.dev)

@@ -44,6 +44,7 @@ Config to_config(const dg_config* c) {
   out.epi_warps = c->epi_warps;
   out.flags = c->flags;
   out.timeout_ns = c->timeout_ns;
+  out.pack_rows = c->pack_rows;
   return out;
 }
 

@@ -48,6 +48,8 @@ struct Config {
   int epi_warps = 0;      // informational; the tile width fixes the epilogue warps
   unsigned long long timeout_ns = 0;  // bounded-wait limit; 0 = 2 s
   int flags = 0;          // extra kernel flags (kFlagInjectTimeout: tests only)
+  int pack_rows = 0;      // kLayoutPacked: rows per tile of the packed weights when a
+                          // CTA tile spans several (block_n a multiple of it); 0 = block_n
 };
 
 // grid_ctas value selecting cluster split-K: grid (tiles, S), cluster
@@ -146,6 +148,20 @@ __host__ __device__ constexpr uint32_t pipeline_smem_bytes(int stages, int subs,
          align1k(static_cast<uint32_t>(stages * subs * mma_m * kKBlock)) + SmemBarriers::bytes(stages, kAccumBuffers);
 }
 
+// The shallowest ring whose drained buffers hold the fp32 partial of M rows
+// that cluster split-K keeps in shared memory (rows of cluster_partial_stride
+// floats); kMaxStages when none does.
+__host__ __device__ constexpr int cluster_min_stages(int M, int subs, int block_n, int mma_m) {
+  int s = 1;
+  while (s < kMaxStages &&
+         static_cast<uint64_t>(align1k(static_cast<uint32_t>(s * subs * block_n * kKBlock +
+                                                             (((block_n + 15) / 16) * 16 - block_n) * kKBlock))) +
+                 align1k(static_cast<uint32_t>(s * subs * mma_m * kKBlock)) <
+             static_cast<uint64_t>(M) * cluster_partial_stride(block_n) * 4u)
+    ++s;
+  return s;
+}
+
 // The deepest ring up to `desired` stages (at least 1) that fits 227 KiB.
 __host__ __device__ constexpr int fitted_stages(int desired, int subs, int block_n, int mma_m) {
   int s = desired > kMaxStages ? kMaxStages : (desired < 1 ? 1 : desired);
@@ -164,6 +180,11 @@ __host__ __device__ inline const char* check_config(const Config& c) {
   if (c.layout < kLayoutRaw || c.layout > kLayoutPackedSwizzled) return "unknown weight layout";
   if (c.split_k < 1) return "split_k must be >= 1";
   if (c.epi_warps != 0) return "epi_warps is chosen by the planner; leave it 0";
+  if (c.pack_rows != 0 && c.pack_rows != c.block_n) {
+    if (c.layout != kLayoutPacked) return "pack_rows applies to the packed layout only";
+    if (c.pack_rows < 8 || c.pack_rows % 8 != 0 || c.block_n % c.pack_rows != 0)
+      return "pack_rows must be a multiple of 8 that divides block_n";
+  }
   return nullptr;
 }
 
@@ -226,10 +247,11 @@ __host__ __device__ inline Plan make_plan(const Config& c, int M, int N, int K, 
     const int S = c.split_k > 1 ? c.split_k
                                 : choose_cluster_split(T, C, (c.flags & kFlagIndependentInputs) != 0, occ);
     if (S > kMaxClusterSplit) return plan.error = "cluster split: split_k must be <= 16", plan;
-    if (S > C) return plan.error = "cluster split: more splits than (K/128)/subs chunks", plan;
-    if (S > 1 && c.block_n % 32 != 0) return plan.error = "cluster split: block_n must be a multiple of 32", plan;
-    // The fp32 partial [M][block_n] goes to the drained pipeline ring.
-    if (S > 1 && static_cast<uint64_t>(M) * c.block_n * 4u >
+    // A given split may exceed the chunks of a tile: the CTAs left without a
+    // chunk contribute zero partials.
+    // The fp32 partial [M][block_n] (rows padded to a multiple of 32 floats)
+    // goes to the drained pipeline ring.
+    if (S > 1 && static_cast<uint64_t>(M) * cluster_partial_stride(c.block_n) * 4u >
                      static_cast<uint64_t>(align1k(stages * w_stage + w_pad)) + align1k(stages * a_stage))
       return plan.error = "cluster split: the M x block_n fp32 partial exceeds the pipeline's shared memory", plan;
     G = static_cast<long long>(T) * S;
@@ -264,6 +286,8 @@ __host__ __device__ inline Plan make_plan(const Config& c, int M, int N, int K, 
   p.N = N;
   p.K = K;
   p.block_n = c.block_n;
+  p.pack_rows = (c.layout == kLayoutPacked && c.pack_rows != 0) ? c.pack_rows : c.block_n;
+  p.pack_tiles = c.block_n / p.pack_rows;
   p.n_mma = n_mma;
   p.a_rows = a_rows;
   p.subs = c.subs;
@@ -300,7 +324,7 @@ __host__ __device__ inline Plan make_plan(const Config& c, int M, int N, int K, 
   plan.max_slabs = max_slabs;
   plan.ws_floats = max_slabs > 1 ? static_cast<size_t>(max_slabs) * M * static_cast<size_t>(N) : 0;
   plan.sem_ints = max_slabs > 1 ? T : 0;
-  plan.padded_n = T * c.block_n;
+  plan.padded_n = padded_n(N, p.pack_rows);
   plan.cluster = cluster;
   return plan;
 }
@@ -325,13 +349,16 @@ inline EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
-// Weight map.  Both TMA layouts use a rank-4 map with box {128, BM, subs, 1}
-// so one copy lands subs*BM*128 bytes in [subs][BM][128] order with the
-// 128-byte swizzle the MMA descriptors expect:
-//   raw    dims {128, N, K/128, 1}, byte strides {K, 128, N*K}: dim 0 and 2
-//          walk K in 128-byte blocks, dim 1 walks rows (the K-block split
-//          keeps the inner box at the 128-byte swizzle span);
-//   packed dims {128, BM, K/128, tiles}, strides {128, BM*128, (K/128)*BM*128}.
+// Weight map.  Both TMA layouts use a rank-4 map so that one copy lands
+// subs*BM*128 bytes in [subs][BM][128] order with the 128-byte swizzle the
+// MMA descriptors expect:
+//   raw    dims {128, N, K/128, 1}, byte strides {K, 128, N*K}, box {128, BM,
+//          subs, 1}: dim 0 and 2 walk K in 128-byte blocks, dim 1 walks rows
+//          (the K-block split keeps the inner box at the 128-byte swizzle
+//          span);
+//   packed dims {128, R, tiles, K/128} (R = pack_rows, the packed tile
+//          height), strides {128, (K/128)*R*128, R*128}, box {128, R, BM/R,
+//          subs}.
 // The swizzled-packed layout is read with bulk copies and needs no map.
 inline cudaError_t make_weight_map(CUtensorMap* map, const Config& c, const void* weight, int N, int K) {
   std::memset(map, 0, sizeof(*map));
@@ -350,16 +377,25 @@ inline cudaError_t make_weight_map(CUtensorMap* map, const Config& c, const void
     strides[1] = kKBlock;
     strides[2] = static_cast<cuuint64_t>(N) * static_cast<cuuint64_t>(K);
   } else {
-    const cuuint64_t tiles = static_cast<cuuint64_t>((N + c.block_n - 1) / c.block_n);
+    // Packed [tile][kb][rows][128] with the tile dimension ahead of the K
+    // blocks (strides need not grow with the dimension): box {128, rows,
+    // block_n / rows, subs} lands [sub][block_n rows][128 B], the MMA's
+    // operand order, also when one CTA tile spans several packed tiles.
+    const cuuint64_t rows = static_cast<cuuint64_t>(c.pack_rows != 0 ? c.pack_rows : c.block_n);
+    const cuuint64_t tiles = (static_cast<cuuint64_t>(N) + rows - 1) / rows;
     dims[0] = kKBlock;
-    dims[1] = static_cast<cuuint64_t>(c.block_n);
-    dims[2] = kb;
-    dims[3] = tiles;
+    dims[1] = rows;
+    dims[2] = tiles;
+    dims[3] = kb;
     strides[0] = kKBlock;
-    strides[1] = static_cast<cuuint64_t>(c.block_n) * kKBlock;
-    strides[2] = kb * c.block_n * kKBlock;
+    strides[1] = kb * rows * kKBlock;
+    strides[2] = rows * kKBlock;
   }
-  const cuuint32_t box[4] = {kKBlock, static_cast<cuuint32_t>(c.block_n), static_cast<cuuint32_t>(c.subs), 1};
+  const bool packed = c.layout == kLayoutPacked;
+  const cuuint32_t rows_box = static_cast<cuuint32_t>(packed && c.pack_rows != 0 ? c.pack_rows : c.block_n);
+  const cuuint32_t box[4] = {kKBlock, rows_box,
+                             static_cast<cuuint32_t>(packed ? c.block_n / rows_box : c.subs),
+                             static_cast<cuuint32_t>(packed ? c.subs : 1)};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(weight), dims, strides,
                             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

@@ -161,6 +161,8 @@ enum Status : int {
 struct KernelParams {
   int M, N, K;
   int block_n;          // BN: weight rows (output columns) per tile
+  int pack_tiles;       // kLayoutPacked: packed tiles of pack_rows rows one CTA tile spans (1: pack_rows = BN)
+  int pack_rows;        // kLayoutPacked: rows per tile of the packed layout (BN / pack_tiles)
   int n_mma;            // MMA N: BN rounded up to 16
   int a_rows;           // activation rows per TMA box: M rounded up to 8
   int subs;             // 128-K blocks per pipeline stage
@@ -292,6 +294,12 @@ struct SmemBarriers {
     return static_cast<uint32_t>((2 * stages + 2 * bufs + 4) * 8 + 32);
   }
 };
+
+// Row stride, in floats, of a CTA's fp32 partial [M][BN] in shared memory
+// under cluster split-K: BN rounded up to 32, so that float4 column c4 of row
+// m, stored at c4 ^ (m & 7), stays inside its row for every BN (a multiple
+// of 8).
+__host__ __device__ constexpr int cluster_partial_stride(int block_n) { return (block_n + 31) & ~31; }
 
 __host__ __device__ __forceinline__ long long cta_of_unit(long long u, long long G, long long U) {
   // CTA c owns [floor(c*U/G), floor((c+1)*U/G)); this inverts it.
@@ -700,6 +708,7 @@ __device__ __forceinline__ void cluster_reduce_tile(const KernelParams& p, uint3
   const int S = static_cast<int>(gridDim.y);
   const int r = static_cast<int>(cluster_ctarank());
   const int bn = p.block_n;
+  const int bn_s = cluster_partial_stride(bn);
   const int bn_t = min(bn, p.N - tile * bn);
   const int u4 = (bn_t + 3) / 4;
   const long long q_all = static_cast<long long>(p.M) * u4;
@@ -709,7 +718,7 @@ __device__ __forceinline__ void cluster_reduce_tile(const KernelParams& p, uint3
   for (long long u = lo + tid; u < hi; u += nthreads) {
     const int m = static_cast<int>(u / u4);
     const int c4 = static_cast<int>(u - static_cast<long long>(m) * u4);
-    const uint32_t off = buf + static_cast<uint32_t>((m * bn + 4 * (c4 ^ (m & 7))) * 4);
+    const uint32_t off = buf + static_cast<uint32_t>((m * bn_s + 4 * (c4 ^ (m & 7))) * 4);
     // Eight peers' loads in flight at a time, summed in rank order.
     float4 tot = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
@@ -804,7 +813,10 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   const long long G = p.num_ctas;
   const long long U = p.total_units;
   const long long cta = static_cast<long long>(blockIdx.x) * gridDim.y + blockIdx.y;
-  if (static_cast<long long>(gridDim.x) * gridDim.y != G || blockDim.x != Tr::kThreads) {
+  // The grid and block of the plan, and under cluster split-K clusters of all
+  // gridDim.y CTAs of a tile (a launch without them could not reduce).
+  if (static_cast<long long>(gridDim.x) * gridDim.y != G || blockDim.x != Tr::kThreads ||
+      ((p.flags & kFlagCluster) && cluster_dim_y() != gridDim.y)) {
     if (threadIdx.x == 0 && p.status != nullptr) atomicCAS(p.status, 0, kErrBadLaunchShape);
     return;
   }
@@ -887,7 +899,11 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         if (p.layout == kLayoutRaw) {
           tma_load_4d(w_map, &full_bar[slot], dst, 0, tile * p.block_n, kb0, 0, pol_w);
         } else if (p.layout == kLayoutPacked) {
-          tma_load_4d(w_map, &full_bar[slot], dst, 0, 0, kb0, tile, pol_w);
+          // Map dims {128, pack_rows, packed tiles, K blocks}: the box's
+          // pack_tiles consecutive packed tiles of each K block land back to
+          // back as BN contiguous 128-byte rows (tiles past the end read as
+          // zeros).
+          tma_load_4d(w_map, &full_bar[slot], dst, 0, 0, tile * p.pack_tiles, kb0, pol_w);
         } else {
           const size_t src_off =
               (static_cast<size_t>(tile) * p.num_kb + kb0) * static_cast<size_t>(p.block_n) * kKBlock;
@@ -1135,7 +1151,7 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
           // This CTA's partial of its one tile -> its shared memory, reduced
           // by the cluster after the loop.
           if (row_ok && *abort_flag == 0) {
-            float* row = reinterpret_cast<float*>(w_region) + static_cast<size_t>(m) * bn;
+            float* row = reinterpret_cast<float*>(w_region) + static_cast<size_t>(m) * cluster_partial_stride(bn);
 #pragma unroll
             for (int j4 = 0; j4 < Tr::kColsPerWarp / 4; ++j4) {
               const int c4 = (col0 >> 2) + j4;
@@ -1194,6 +1210,16 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
           }
         }
         u = seg_end;
+      }
+      // A cluster CTA without units (a split finer than the tile's chunks)
+      // contributes a zero partial.
+      if ((p.flags & kFlagCluster) && n_units == 0 && row_ok && *abort_flag == 0) {
+        float* row = reinterpret_cast<float*>(w_region) + static_cast<size_t>(m) * cluster_partial_stride(bn);
+#pragma unroll
+        for (int j4 = 0; j4 < Tr::kColsPerWarp / 4; ++j4) {
+          const int c4 = (col0 >> 2) + j4;
+          if (4 * c4 < bn) *reinterpret_cast<float4*>(row + 4 * (c4 ^ (m & 7))) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
       // ----------------------------------------------- split reduction ----
       // Only a CTA with reduction work enters the (cold) reduction code: any

@@ -357,6 +357,12 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
+// CTAs of this CTA's cluster along y (1 when launched without clusters).
+__device__ __forceinline__ uint32_t cluster_dim_y() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctaid.y;" : "=r"(r));
+  return r;
+}
 // The shared::cluster address of offset `saddr` (a shared::cta address of
 // this CTA) in the shared memory of cluster CTA `rank`.
 __device__ __forceinline__ uint32_t map_shared_rank(uint32_t saddr, uint32_t rank) {

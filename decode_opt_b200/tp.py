@@ -96,9 +96,9 @@ class TPDecodeGemm:
     def _weight(self, cfg):
         if cfg.layout == self.dg.LAYOUT_RAW:
             return self.w_raw
-        key = (cfg.block_n, cfg.layout)
+        key = (cfg.packed_rows, cfg.layout)
         if key not in self._packed:
-            self._packed[key] = self.dg.prepack_weight(self.w_raw, cfg.block_n, cfg.layout)
+            self._packed[key] = self.dg.prepack_weight(self.w_raw, cfg.packed_rows, cfg.layout)
         return self._packed[key]
 
     def forward(self, act, act_scales, stream=None):

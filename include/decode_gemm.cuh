@@ -24,14 +24,32 @@
 //
 // Mapping of the reference's configuration (B200 semantics):
 //   M_TILE              batch class of the kernel (MMA M 64 up to 32, else 128)
-//   OUTPUT_ROWS_PER_CTA weight rows per tile, the MMA's N side: multiple of 8
-//                       in [8, 256] (the reference allows <= 64)
+//   OUTPUT_ROWS_PER_CTA BM: rows per tile of the weight layout (the packed
+//                       layout's tile height, multiple of 8 in [8, 256]).  A CTA
+//                       takes T = floor(256 / BM) consecutive BM-row tiles --
+//                       the reference's TILES_PER_CTA idea, sized for the
+//                       tcgen05 N side: kBlockN = T * BM weight rows (224-256
+//                       for BM 32..64) per MMA, 7-8 KiB of weights per
+//                       instruction instead of BM * 128 bytes.  Packed weights
+//                       are read in the reference's layout as they are: one
+//                       TMA box {128, BM, 1, T} per 128-K block lands the T
+//                       tiles as one MMA operand.
 //   SUBS_PER_STAGE      128-K blocks per pipeline stage: 1, 2 or 4
-//   NUM_MATH_WG x STAGES_PER_WG  ring depth, reduced to what fits 227 KiB
+//   NUM_MATH_WG x STAGES_PER_WG  ring depth, raised to hold the cluster
+//                       split's partial and reduced to what fits 227 KiB
 //   PREPACK             packed (prepack) weight layout instead of raw [N][K]
 //   PDL, EPI_OVERLAP    griddepcontrol.launch_dependents (either); PDL also
 //                       sets programmatic stream serialization in launch*
-//   SPLIT_K_CTA, SPLITK_FACTOR  split-K factor S (grid.y), deterministic
+//   SPLIT_K_CTA, SPLITK_FACTOR  the split of every tile's K range, S =
+//                       max(factor, 4) (the reference's factor split BM-row
+//                       tiles; a CTA tile here spans T of them): grid (tiles, S) as
+//                       one thread-block cluster per tile, the S partials
+//                       reduced through distributed shared memory in rank
+//                       order (deterministic; no workspace or semaphore is
+//                       touched, so splitk_sem stays zero).  S is a
+//                       compile-time constant of Cfg, so fp8_decode_gemm<Cfg>
+//                       carries it as __cluster_dims__ and a caller's own
+//                       launch with make_launch_plan's grid forms the clusters.
 //   MATH_REGS, PROD_REGS, SINGLE_PRODUCER_WARP, PRELOAD_ACT, SCALE_IN_SMEM,
 //   TILES_PER_CTA       range-checked as the reference checks them; the
 //                       sm_100a kernel's warp roles are fixed.
@@ -129,24 +147,35 @@ struct KernelConfig {
   using Traits = typename detail::ClassOf<M_TILE_>::type;
   static constexpr uint32_t kNumThreads = static_cast<uint32_t>(Traits::kThreads);
   static constexpr int kMmaM = Traits::kMmaM;
-  // Ring depth the kernel runs with: NUM_MATH_WG x STAGES_PER_WG, reduced
-  // until the pipeline fits 227 KiB.
-  static constexpr int kRingStages = dg::fitted_stages(static_cast<int>(kStages), SUBS_PER_STAGE_,
-                                                       OUTPUT_ROWS_PER_CTA_, Traits::kMmaM);
+  // BM-row tiles per CTA tile and the CTA tile's weight rows (the MMA N).
+  static constexpr int kPackTiles = OUTPUT_ROWS_PER_CTA_ <= 128 ? 256 / OUTPUT_ROWS_PER_CTA_ : 1;
+  static constexpr int kBlockN = OUTPUT_ROWS_PER_CTA_ * kPackTiles;
+  // CTAs per tile: one cluster, split along K -- at least 4 (the split the
+  // B200 planner takes for 224-256-row tiles of the reference's shapes in a
+  // dependent chain), SPLITK_FACTOR when that asks for more.  The
+  // reference's factor split BM-row tiles; a CTA tile here is T of them.
+  static constexpr int kClusterSplit = kSplitKFactor > 4u ? static_cast<int>(kSplitKFactor) : 4;
+  // Ring depth the kernel runs with: NUM_MATH_WG x STAGES_PER_WG, at least
+  // what holds the cluster partial of M_TILE rows, at most what fits 227 KiB.
+  static constexpr int kMinStages = dg::cluster_min_stages(M_TILE_, SUBS_PER_STAGE_, kBlockN, Traits::kMmaM);
+  static constexpr int kRingStages =
+      dg::fitted_stages(static_cast<int>(kStages) > kMinStages ? static_cast<int>(kStages) : kMinStages,
+                        SUBS_PER_STAGE_, kBlockN, Traits::kMmaM);
   static constexpr uint32_t kFixedSmemBytes =
-      dg::pipeline_smem_bytes(kRingStages, SUBS_PER_STAGE_, OUTPUT_ROWS_PER_CTA_, Traits::kMmaM);
+      dg::pipeline_smem_bytes(kRingStages, SUBS_PER_STAGE_, kBlockN, Traits::kMmaM);
 
   // The planner's configuration (host and device).
   static __host__ __device__ constexpr dg::Config b200_config() {
     dg::Config c{};
     c.m_tile = M_TILE_;
-    c.block_n = OUTPUT_ROWS_PER_CTA_;
+    c.block_n = kBlockN;
+    c.pack_rows = (PREPACK_ && kPackTiles > 1) ? OUTPUT_ROWS_PER_CTA_ : 0;
     c.subs = SUBS_PER_STAGE_;
     c.stages = kRingStages;
     c.layout = PREPACK_ ? dg::kLayoutPacked : dg::kLayoutRaw;
     c.pdl = (PDL_ || EPI_OVERLAP_) ? 1 : 0;
-    c.split_k = static_cast<int>(kSplitKFactor);
-    c.grid_ctas = 0;
+    c.split_k = kClusterSplit;
+    c.grid_ctas = dg::kGridCluster;
     c.epi_warps = 0;
     c.timeout_ns = 0;
     c.flags = dg::kFlagClassFromMTile;
@@ -166,15 +195,22 @@ struct KernelConfig {
     c.epi_warps = 0;
     c.flags = b.flags;
     c.timeout_ns = 0;
+    c.pack_rows = b.pack_rows;
     return c;
   }
 
-  // ---- geometry (the grid is tiles x S: one output tile per CTA)
+  // ---- geometry: num_output_tiles counts BM-row tiles as the reference does
+  // (the packed layout's tiles; splitk_sem needs no more ints); the grid is
+  // (ceil(N / kBlockN), kClusterSplit).
   static __host__ __device__ constexpr uint32_t num_output_tiles(int n) {
     return (static_cast<uint32_t>(n) + kOutputRows - 1) / kOutputRows;
   }
-  static __host__ __device__ constexpr uint32_t num_ctas_x(int n) { return num_output_tiles(n); }
-  static __host__ __device__ constexpr uint32_t num_ctas(int n) { return num_ctas_x(n) * kSplitKFactor; }
+  static __host__ __device__ constexpr uint32_t num_ctas_x(int n) {
+    return (static_cast<uint32_t>(n) + kBlockN - 1) / kBlockN;
+  }
+  static __host__ __device__ constexpr uint32_t num_ctas(int n) {
+    return num_ctas_x(n) * static_cast<uint32_t>(kClusterSplit);
+  }
   static __host__ __device__ uint32_t dynamic_smem_bytes(int m, int k) {
     (void)m;
     (void)k;
@@ -241,7 +277,7 @@ struct LaunchPlan {
 // The kernel entry (launched by launch_with_maps's callers themselves)
 // ---------------------------------------------------------------------------
 template <typename Cfg>
-__global__ void __launch_bounds__(Cfg::kNumThreads, 1)
+__global__ void __launch_bounds__(Cfg::kNumThreads, 1) __cluster_dims__(1, Cfg::kClusterSplit, 1)
     fp8_decode_gemm(__nv_bfloat16* output, const float* weight_scales, const float* activation_scales,
                     const __grid_constant__ CUtensorMap w_tma, const __grid_constant__ CUtensorMap a_tma,
                     GemmRuntime rt) {
@@ -321,8 +357,8 @@ inline LaunchPlan make_launch_plan(const Problem& p) {
     plan.grid = dim3(info.grid_x, info.grid_y, info.grid_z);
     plan.block = dim3(info.block_x, 1u, 1u);
     plan.smem_bytes = info.smem_bytes;
-    plan.num_output_tiles = info.num_output_tiles;
-    plan.padded_n = info.padded_n;
+    plan.num_output_tiles = static_cast<int>(Cfg::num_output_tiles(p.N));
+    plan.padded_n = prepack::padded_n(p.N, static_cast<int>(Cfg::kOutputRows));
   } else if (plan.error == nullptr) {
     plan.error = detail::keep_message(info.error[0] ? info.error : "the sm_100a planner rejects this shape");
   }

@@ -53,7 +53,7 @@
 extern "C" {
 #endif
 
-#define DG_ABI_VERSION 3
+#define DG_ABI_VERSION 4
 
 /* Weight layouts. */
 #define DG_LAYOUT_RAW 0             /* W[N,K], K contiguous (checkpoint layout) */
@@ -117,6 +117,12 @@ typedef struct dg_config {
   int epi_warps; /* 0 (or the value block_n implies: 4 per 64 tile columns)            */
   int flags;     /* DG_FLAG_* (tests only)                                              */
   unsigned long long timeout_ns; /* bounded-wait limit per wait; 0 = 2 s               */
+  int pack_rows; /* DG_LAYOUT_PACKED only: rows per tile of the packed weights when one
+                    tile of the kernel (block_n rows) spans several of them -- block_n a
+                    multiple of pack_rows; 0 = block_n.  The reference's prepack layout
+                    for OUTPUT_ROWS_PER_CTA = BM is read this way with block_n = T * BM
+                    (its TILES_PER_CTA idea): one TMA box per 128-K block lands T
+                    packed tiles as one MMA operand                                      */
 } dg_config;
 
 /* One GEMM (reference decode_gemm::Problem, kernels/decode_gemm.cuh:352-363). */

@@ -47,9 +47,9 @@ class DeviceCase:
         import decode_opt_b200 as dg
         if cfg.layout == dg.LAYOUT_RAW:
             return self.w
-        key = (cfg.block_n, cfg.layout)
+        key = (cfg.packed_rows, cfg.layout)
         if key not in self.packed:
-            self.packed[key] = dg.prepack_weight(self.w, cfg.block_n, cfg.layout)
+            self.packed[key] = dg.prepack_weight(self.w, cfg.packed_rows, cfg.layout)
         return self.packed[key]
 
     def run(self, cfg, clear_out: bool = True, stream=None, ws_offset: int = 0):

@@ -189,12 +189,31 @@ def test_kernel_config_mirror_reference_rules():
 
 
 def test_kernel_config_maps_onto_b200_config():
+    """A reference configuration runs T = 256 // BM of its BM-row tiles per
+    CTA (224 rows at BM 56) in the reference's packed layout, on the cluster
+    split (4 unless SPLITK_FACTOR says otherwise); the plan keeps the
+    reference's meanings of num_output_tiles and padded_n."""
     k = dg.KernelConfig(8, 56, 2, 80, 3, 1, 2, True, True, False, False)
     b = k.to_b200()
-    assert (b.m_tile, b.block_n, b.subs, b.stages, b.layout, b.pdl, b.split_k, b.grid_ctas) == \
-        (8, 56, 2, 6, dg.LAYOUT_PACKED, True, 1, 0)
+    assert (b.m_tile, b.block_n, b.pack_rows, b.subs, b.stages, b.layout, b.pdl, b.split_k, b.grid_ctas) == \
+        (8, 224, 56, 2, 6, dg.LAYOUT_PACKED, True, 4, dg.GRID_CLUSTER)
+    assert b.packed_rows == 56 and k.kBlockN == 224 and k.num_ctas(7168) == 128
     plan = dg.make_launch_plan(k, dg.Problem(1, 7168, 16384))
-    assert plan.error is None and plan.grid == (128, 1, 1) and plan.mma_m == 64 and plan.n_mma == 64
+    assert plan.error is None and plan.grid == (32, 4, 1) and plan.cluster == 4
+    assert plan.mma_m == 64 and plan.n_mma == 224 and plan.ws_floats == 0 and plan.sem_ints == 0
+    assert plan.num_output_tiles == 128 and plan.padded_n == 7168
+    # BM 48 on N = 7168: 150 packed tiles (padded_n 7200), five per CTA tile.
+    k48 = dg.KernelConfig(8, 48, 2, 80, 3, 1, 2, True, True, True, True, SPLITK_FACTOR=8)
+    p48 = dg.make_launch_plan(k48, dg.Problem(8, 7168, 16384))
+    assert p48.error is None and p48.grid == (30, 8, 1) and p48.n_mma == 240
+    assert p48.num_output_tiles == 150 and p48.padded_n == 7200
+    # Raw weights: the tile width alone (no packed tile height).
+    kr = dg.KernelConfig(128, 64, 1, 232, 2, 1, 1, False, True, False, False, SCALE_IN_SMEM=False)
+    br = kr.to_b200()
+    assert br.block_n == 256 and br.pack_rows == 0 and br.layout == dg.LAYOUT_RAW
+    # The ring is deepened until the cluster partial of M_TILE rows fits.
+    assert br.stages >= dg.cluster_min_stages(128, 1, 256, 128) == 3
+    assert dg.make_launch_plan(kr, dg.Problem(128, 7168, 16384)).error is None
 
 
 B200_CLUSTER_OCC = [0, 148, 74, 45, 33, 26, 22, 15, 15]   # clusters of S CTAs resident at once (measured)
@@ -241,16 +260,18 @@ def test_default_plans_follow_the_split_rule(n, k, m, independent):
 @pytest.mark.parametrize("bn", list(range(32, 257, 8)))
 def test_cluster_partial_layout_rules(bn):
     """The cluster reduction's index rules: a row's float4 unit c4 is stored at
-    c4 ^ (m % 8), a permutation of the row's bn/4 units only when bn is a
-    multiple of 32 -- which the planner requires -- and the S ranks' unit
-    ranges [r*q/S, (r+1)*q/S) cover all q = M * ceil(bn_t/4) units once."""
+    c4 ^ (m % 8) in a row of ceil(bn/32)*32 floats -- one-to-one and inside
+    the row for every bn that is a multiple of 8, so the planner takes any
+    such width -- and the S ranks' unit ranges [r*q/S, (r+1)*q/S) cover all
+    q = M * ceil(bn_t/4) units once."""
     units = bn // 4
-    ok = all(sorted(c ^ m for c in range(units)) == list(range(units)) for m in range(8))
-    assert ok == (bn % 32 == 0)
+    row_units = ((bn + 31) // 32) * 8
+    for m in range(8):
+        slots = [c ^ m for c in range(units)]
+        assert len(set(slots)) == units and max(slots) < row_units
     plan = dg.B200Config(m_tile=8, block_n=bn, subs=2, stages=0, layout=dg.LAYOUT_PACKED_SWIZZLED,
                          grid_ctas=dg.GRID_CLUSTER, split_k=4).plan(1, 7168, 16384)
-    if bn % 32:
-        assert plan.error is not None and "multiple of 32" in plan.error
+    assert plan.error is None, plan.error
     for m_rows in (1, 7, 64):
         for bn_t in (bn, max(4, bn - 20)):
             q = m_rows * -(-bn_t // 4)

@@ -2,7 +2,8 @@
 thread-block cluster and reduce through distributed shared memory.  Parity
 with the oracle across batch classes, layouts, ragged N and split factors
 (portable and non-portable cluster sizes), run-to-run bit determinism, no
-workspace, back-to-back launches under programmatic dependent launch, and the
+workspace, back-to-back launches under programmatic dependent launch, tile
+widths that are any multiple of 8, splits finer than a tile's chunks, and the
 planner's rejections."""
 
 import numpy as np
@@ -109,10 +110,19 @@ def test_back_to_back_pdl_graph():
     assert np.array_equal(got.view(np.uint32), single.view(np.uint32))
 
 
+@pytest.mark.parametrize("m,n,k,bn,subs,split", [
+    (8, 1000, 2048, 56, 2, 2),     # a tile width that is no multiple of 32 (partial rows padded to 64 floats)
+    (5, 1000, 2048, 240, 2, 9),    # 9 CTAs per cluster, 8 chunks per tile: one CTA adds a zero partial
+    (64, 700, 1024, 120, 1, 16),   # 16 CTAs (non-portable cluster), 8 chunks: half of them idle
+])
+def test_any_width_and_splits_finer_than_the_chunks(m, n, k, bn, subs, split):
+    w, ws, a, as_, ref = smoke_case(n, k, 61, m)
+    dc = DeviceCase(w, ws, a, as_, n)
+    _check(dc, _cfg(m, block_n=bn, subs=subs, split=split, stages=0), ref)
+
+
 def test_planner_rejections():
-    assert "multiple of 32" in _cfg(8, block_n=56, split=2).plan(8, 7168, 4096).error
     assert "split_k must be <= 16" in _cfg(8, split=17).plan(8, 2048, 16384).error
-    assert "more splits" in _cfg(8, subs=2, split=9).plan(8, 2048, 2048).error
     # M=128 x 256 fp32 = 128 KiB of partial does not fit a 1-stage ring
     assert "partial" in _cfg(128, subs=1, split=2, stages=1).plan(128, 2048, 4096).error
     # S = 1 is the plain tile schedule (no cluster)

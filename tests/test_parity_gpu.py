@@ -155,6 +155,36 @@ def test_reference_smoke_case(idx):
     assert np.array_equal(got, got2), "second launch not bit-identical"
 
 
+@pytest.mark.parametrize("n,k,m,bm,subs,pack,skf", [
+    (200, 256, 1, 48, 2, True, 0),      # one chunk per tile, split 4: three CTAs of each cluster idle
+    (200, 384, 8, 48, 1, True, 0),      # 3 chunks over 4 CTAs; N below one 240-row CTA tile
+    (1000, 512, 3, 40, 1, True, 0),     # BM 40: six packed tiles (240 rows) per CTA, ragged N
+    (1000, 512, 17, 24, 2, True, 2),    # BM 24: ten packed tiles per CTA, M_TILE 32 (split max(2, 4))
+    (1000, 2048, 64, 56, 2, True, 8),   # M_TILE 64 on BM 56 (224 rows), split 8: one chunk per CTA
+    (777, 1024, 100, 64, 1, False, 0),  # raw weights, M_TILE 128 (ring deepened for the partial)
+    (136, 2048, 128, 8, 4, True, 0),    # BM 8: 32 packed tiles per CTA, four K blocks per stage
+])
+def test_reference_config_wide_tiles(n, k, m, bm, subs, pack, skf):
+    """A KernelConfig's CTA spans T = 256 // BM packed tiles (one TMA box
+    over the tile dimension per stage) on a cluster split fixed by the
+    configuration: splits finer than a tile's chunks, N narrower than one CTA
+    tile and every batch class match the oracle, leave the ticket array
+    untouched and repeat bit for bit."""
+    w, ws = oracle.gen_weight_smoke(n, k, n + k)
+    a, as_ = oracle.gen_activation_smoke(m, k, m + 5)
+    ref = oracle.compute_reference(a, as_, w, ws)
+    dc = DeviceCase(w, ws, a, as_, n)
+    mt = dg.m_tile_for(m)
+    kcfg = cfg(mt, bm, 1, 112, 2, 1, subs, pack, True, False, skf > 1, skf=skf)
+    rc, got, status = run_reference_config(dc, kcfg)
+    assert rc == 0 and status == 0, (rc, dg.status_string(status))
+    ok, rl2, worst = check_against_oracle(got, ref)
+    assert ok, (rl2, worst)
+    assert dc.sem_clean()
+    rc, got2, status = run_reference_config(dc, kcfg, clear_out=False)
+    assert rc == 0 and status == 0 and np.array_equal(got, got2)
+
+
 # ---------------------------------------------------------------------------
 # B200 schedules
 # ---------------------------------------------------------------------------
