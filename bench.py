@@ -188,6 +188,30 @@ def cpu_parallel_gemm(run, a, as_, w, ws, threads):
     return out
 
 
+def cublaslt_driver(n, k, ms, dev):
+    """Runs decode_opt_b200/dg_cublaslt_fp8 (block-scaled and per-tensor) on
+    `dev`: {"block": [per-M dicts], "tensor": [...]}, or {"unavailable": why}."""
+    import subprocess
+    exe = os.path.join(os.path.dirname(os.path.abspath(__file__)), "decode_opt_b200", "dg_cublaslt_fp8")
+    if not os.path.exists(exe):
+        return {"unavailable": "dg_cublaslt_fp8 not built"}
+    # The child's device 0 is this process's `dev`.
+    idx = dev.index or 0
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES=visible[idx] if idx < len(visible) and visible[idx] else str(idx))
+    out = {}
+    for mode in ("block", "tensor"):
+        try:
+            proc = subprocess.run([exe, "--n", str(n), "--k", str(k), "--ms", ",".join(map(str, ms)),
+                                   "--mode", mode, "--iters", "200"], capture_output=True, text=True,
+                                  timeout=600, env=env)
+            rows = [json.loads(ln) for ln in proc.stdout.splitlines() if ln.startswith("{")]
+            out[mode] = rows if proc.returncode == 0 else [{"unavailable": proc.stderr[-300:]}]
+        except Exception as exc:  # noqa: BLE001 - reported, not fatal
+            out[mode] = [{"unavailable": f"{type(exc).__name__}: {exc}"[:200]}]
+    return out
+
+
 def host_inputs(n, k, m, seed=20260913):
     """Per-tensor-scaled N(0,1) e4m3 inputs on the host (torch CPU generator)."""
     import numpy as np
@@ -886,7 +910,7 @@ def b200_arm(args, rank, world, local_rank):
                 except Exception as exc:  # noqa: BLE001 - try the next scale layout
                     last_err = f"{type(exc).__name__}: {exc}"[:200]
             if blk is None:
-                cublas["blockwise"] = {"unavailable": last_err}
+                cublas["blockwise_torch"] = {"unavailable": last_err}
             else:
                 def cub_blk(i):
                     torch._scaled_mm(a16, raw_sets[i % len(raw_sets)].t(), scale_a=blk[1], scale_b=blk[2],
@@ -898,12 +922,26 @@ def b200_arm(args, rank, world, local_rank):
                 graphs = capture(cub_blk, K)
                 t_b = timed(graphs)
                 del graphs
-                cublas["blockwise"] = {"us_per_gemm": t_b / K * 1e6, "GBps": byt_gpu / (t_b / K) / 1e9,
-                                       "call": f"torch._scaled_mm e4m3 1x128 activation / 128x128 weight block "
-                                               f"scales ({blk[0]}), M padded to {m16}"}
+                cublas["blockwise_torch"] = {"us_per_gemm": t_b / K * 1e6, "GBps": byt_gpu / (t_b / K) / 1e9,
+                                             "call": f"torch._scaled_mm e4m3 1x128 activation / 128x128 weight "
+                                                     f"block scales ({blk[0]}), M padded to {m16}"}
             del raw_sets
         except Exception as exc:  # noqa: BLE001 - reported, not fatal
             cublas = {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+        # The CUDA toolkit's cuBLASLt (whose header declares the 128-block
+        # scale modes torch's bundled build refuses) in its own process: the
+        # reference's scale layout (CUBLASLT_MATMUL_MATRIX_SCALE_BLK128x128_32F
+        # on the weights, VEC128_32F on the activation) and per-tensor, each
+        # checked against an fp32 reference before it is timed, at the
+        # reference's baseline batch sizes (results/baseline_cublaslt.csv).
+        cublas["toolkit_cublaslt"] = cublaslt_driver(n, k, sorted({1, 8, 64, 128, m}), dev)
+        blk_rows = [r for r in cublas["toolkit_cublaslt"].get("block", []) if r.get("M") == m]
+        if blk_rows and "us_per_gemm" in blk_rows[0]:
+            cublas["blockwise"] = {"us_per_gemm": blk_rows[0]["us_per_gemm"], "GBps": blk_rows[0]["GBps"],
+                                   "call": f"cuBLASLt {blk_rows[0]['cublaslt']} e4m3 BLK128x128 weight / VEC128 "
+                                           f"activation scales, M={m}, bf16 out"}
+        elif blk_rows:
+            cublas["blockwise"] = {"unavailable": blk_rows[0].get("unavailable", "no result")}
 
     # ---- CPU baseline on rank 0 (N = 1 only), also the parity check -----------
     cpu = None

@@ -159,8 +159,8 @@ def lib():
     L.dg_ipc_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_ulonglong)]
     L.dg_ipc_import.argtypes = [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_void_p)]
     L.dg_ipc_release.argtypes = [ctypes.c_void_p]
-    L.dg_probe_mma.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
-                               ctypes.c_void_p, ctypes.c_void_p]
+    L.dg_probe_mma.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                               ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     if L.dg_abi_version() != ABI_VERSION:
         raise RuntimeError(f"{LIB_PATH}: ABI version {L.dg_abi_version()} != {ABI_VERSION}")
     _LIB = L

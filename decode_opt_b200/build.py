@@ -9,7 +9,10 @@ GPU (the CPU test suite checks its exported symbols there).
 It then compiles ``tests/cpp/dg_drop_in_check.cu`` against the C++ headers
 (``include/decode_gemm.cuh``, ``include/weight_prepack.cuh``) and the
 library into ``decode_opt_b200/dg_drop_in_check``, the program the GPU tests
-run to check the C++ interface.
+run to check the C++ interface, and ``csrc/dg_cublaslt_fp8.cu`` into
+``decode_opt_b200/dg_cublaslt_fp8``, the cuBLASLt FP8 baseline bench.py runs
+in its own process (linked to the CUDA toolkit's cuBLASLt, which declares the
+128-block scale modes; torch's bundled cuBLAS is never loaded beside it).
 """
 
 from __future__ import annotations
@@ -27,6 +30,8 @@ LIB_NAME = "libdecode_gemm_b200.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
 DROP_IN_SRC = os.path.join(ROOT, "tests", "cpp", "dg_drop_in_check.cu")
 DROP_IN_BIN = os.path.join(HERE, "dg_drop_in_check")
+CUBLASLT_SRC = os.path.join(CSRC, "dg_cublaslt_fp8.cu")
+CUBLASLT_BIN = os.path.join(HERE, "dg_cublaslt_fp8")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 SOURCES = ("dg_capi.cu", "dg_probe.cu", "dg_quant.cu")
@@ -53,7 +58,26 @@ def needs_build(target: str = LIB_PATH, extra=()) -> bool:
 def build(verbose: bool = False, ptxas_verbose: bool = False, force: bool = False) -> str:
     lib = build_library(verbose, ptxas_verbose, force)
     build_drop_in_check(verbose, force)
+    build_cublaslt_bench(verbose, force)
     return lib
+
+
+def cuda_lib_dir() -> str:
+    return os.path.join(os.path.dirname(os.path.dirname(os.path.realpath(nvcc()))), "lib64")
+
+
+def build_cublaslt_bench(verbose: bool = False, force: bool = False) -> str:
+    """The cuBLASLt FP8 baseline program (block-scaled and per-tensor)."""
+    if not force and os.path.exists(CUBLASLT_BIN) and os.path.getmtime(CUBLASLT_BIN) > os.path.getmtime(CUBLASLT_SRC):
+        return CUBLASLT_BIN
+    libdir = cuda_lib_dir()
+    cmd = [nvcc(), "-std=c++17", "-O3", *ARCH_FLAGS, CUBLASLT_SRC, "-o", CUBLASLT_BIN + ".tmp", "-L", libdir,
+           "-lcublasLt", "-Xlinker", f"-rpath,{libdir}"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(CUBLASLT_BIN + ".tmp", CUBLASLT_BIN)
+    return CUBLASLT_BIN
 
 
 def build_drop_in_check(verbose: bool = False, force: bool = False) -> str:

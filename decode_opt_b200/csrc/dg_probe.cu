@@ -18,12 +18,13 @@
 // L2: it must read far above HBM speed, which shows the cold-buffer numbers
 // are not L2 hits.
 //
-//   dg_probe_mma          tcgen05.mma cost: one thread issues a run of
+//   dg_probe_mma          tcgen05.mma cost: 1-4 warps each issue a run of
 //                         kind::f8f6f4 MMAs of one shape (zeroed smem
-//                         operands) round-robin over TMEM accumulators and
-//                         reads clock64 around the issue loop and around the
-//                         completion (tcgen05.commit -> mbarrier).  It is the
-//                         measurement behind the GEMM's operand placement.
+//                         operands) round-robin over their own TMEM
+//                         accumulators, clock64 around the issue loops and
+//                         until every MMA has completed (tcgen05.commit ->
+//                         mbarrier): the per-instruction cost of one issuing
+//                         thread against the tensor pipe's throughput.
 //
 // Timing of the two HBM probes is the caller's (CUDA events around the
 // launch).  Every wait is bounded; a timeout is reported through *status
@@ -141,19 +142,32 @@ __device__ bool probe_wait(uint64_t* bar, uint32_t parity, int* status, int code
   return true;
 }
 
+// `issuers` warps (lane 0 of warps 0..issuers-1) issue MMAs concurrently, each
+// round-robin over its own `accumulators` TMEM accumulators (every MMA of a
+// run of four into one accumulator depends on the previous one; different
+// accumulators are independent), with the smem descriptors computed before
+// the timed loop.  Per CTA: out[2c] = cycles until the slowest issuer has
+// issued, out[2c+1] = cycles until every issued MMA has completed (each
+// issuer commits to its own mbarrier), both from one common clock64 start.
 __global__ void __launch_bounds__(kMmaProbeThreads, 1)
-    mma_cost_kernel(int mma_m, int mma_n, int iters, int accumulators, long long* out, int* status) {
+    mma_cost_kernel(int mma_m, int mma_n, int iters, int accumulators, int issuers, long long* out,
+                    int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023));
   uint8_t* a_tile = smem;                 // 128 rows x 128 B, SWIZZLE_128B K-major
   uint8_t* b_tile = smem + 16384;         // 256 rows x 128 B
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 16384 + 32768);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 16384 + 32768);   // [4]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 4);
+  long long* t_issue = reinterpret_cast<long long*>(bar + 6);          // [4]
+  __shared__ long long t_start;
   for (int i = threadIdx.x; i < (16384 + 32768) / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(smem)[i] = make_uint4(0u, 0u, 0u, 0u);
   fence_proxy_async_shared();             // zero fill -> tensor-core operand reads
   if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
+    for (int w = 0; w < 4; ++w) {
+      mbar_init(&bar[w], 1);
+      t_issue[w] = -1;
+    }
     fence_barrier_init();
   }
   if (threadIdx.x < 32) {
@@ -164,30 +178,51 @@ __global__ void __launch_bounds__(kMmaProbeThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  if (threadIdx.x == 0) {
-    const uint32_t idesc = make_idesc_e4m3_f32(static_cast<uint32_t>(mma_m), static_cast<uint32_t>(mma_n));
-    const uint32_t a0 = smem_addr(a_tile);
-    const uint32_t b0 = smem_addr(b_tile);
-    for (int i = 0; i < 8; ++i) mma_f8f6f4(tmem_base, make_desc_k_sw128(a0), make_desc_k_sw128(b0), idesc, 0u);
-    mma_commit(bar);
-    long long issue = -1, done = -1;
-    if (probe_wait(bar, 0u, status, 0x93)) {
-      const long long t0 = clock64();
-      for (int i = 0; i < iters; ++i) {
-        const int r = i % accumulators;
-        const uint32_t d = tmem_base + static_cast<uint32_t>(r * mma_n);
-        const uint32_t k = 32u * static_cast<uint32_t>(i & 3);
-        mma_f8f6f4(d, make_desc_k_sw128(a0 + k), make_desc_k_sw128(b0 + k), idesc, ((i / accumulators) & 3) != 0 ? 1u : 0u);
-      }
-      const long long t1 = clock64();
-      mma_commit(bar);
-      if (probe_wait(bar, 1u, status, 0x93)) {
-        issue = t1 - t0;
-        done = clock64() - t0;
+  const int warp = threadIdx.x / 32;
+  const bool issuer = (threadIdx.x & 31) == 0 && warp < issuers;
+  const uint32_t idesc = make_idesc_e4m3_f32(static_cast<uint32_t>(mma_m), static_cast<uint32_t>(mma_n));
+  const uint32_t a0 = smem_addr(a_tile);
+  const uint32_t b0 = smem_addr(b_tile);
+  uint64_t adesc[4], bdesc[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    adesc[k] = make_desc_k_sw128(a0 + 32u * k);
+    bdesc[k] = make_desc_k_sw128(b0 + 32u * k);
+  }
+  const uint32_t d0 = tmem_base + static_cast<uint32_t>(warp * accumulators * mma_n);
+  bool ok = true;
+  if (issuer) {   // warm-up: the first MMAs of each issuer, completed before timing
+    for (int i = 0; i < 8; ++i) mma_f8f6f4(d0, adesc[i & 3], bdesc[i & 3], idesc, 0u);
+    mma_commit(&bar[warp]);
+    ok = probe_wait(&bar[warp], 0u, status, 0x93);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) t_start = clock64();
+  __syncthreads();
+  const int mine = iters / issuers;
+  if (issuer && ok) {
+    int r = 0, run = 0;
+    for (int i = 0; i < mine; ++i) {
+      mma_f8f6f4(d0 + static_cast<uint32_t>(r * mma_n), adesc[i & 3], bdesc[i & 3], idesc, run != 0 ? 1u : 0u);
+      if (++r == accumulators) {
+        r = 0;
+        run = (run + 1) & 3;
       }
     }
+    const long long t = clock64();
+    mma_commit(&bar[warp]);
+    t_issue[warp] = probe_wait(&bar[warp], 1u, status, 0x93) ? t : -1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const long long done = clock64() - t_start;
+    long long issue = 0;
+    for (int w = 0; w < issuers; ++w) {
+      if (t_issue[w] < 0) issue = -1;
+      if (issue >= 0 && t_issue[w] - t_start > issue) issue = t_issue[w] - t_start;
+    }
     out[2 * blockIdx.x] = issue;
-    out[2 * blockIdx.x + 1] = done;
+    out[2 * blockIdx.x + 1] = issue >= 0 ? done : -1;
   }
   tc_fence_before();
   __syncthreads();
@@ -235,17 +270,18 @@ int dg_num_sms(void) { return sm_count(); }
 
 // out: 2 * ctas long longs (issue cycles, completion cycles per CTA; -1 after
 // a timeout).
-int dg_probe_mma(int mma_m, int mma_n, int iters, int accumulators, int ctas, long long* out, int* status,
-                 void* stream) {
+int dg_probe_mma(int mma_m, int mma_n, int iters, int accumulators, int issuers, int ctas, long long* out,
+                 int* status, void* stream) {
   const int n_step = mma_m == 64 ? 8 : 16;
   if (out == nullptr || !(mma_m == 64 || mma_m == 128) || mma_n < n_step || mma_n > 256 || mma_n % n_step != 0 ||
-      accumulators < 1 || accumulators * mma_n > 512 || iters < 1 || ctas < 1 || ctas > sm_count())
+      issuers < 1 || issuers > 4 || accumulators < 1 || issuers * accumulators * mma_n > 512 ||
+      iters < issuers || ctas < 1 || ctas > sm_count())
     return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(mma_cost_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(kMmaProbeSmem));
   if (e != cudaSuccess) return e;
   mma_cost_kernel<<<ctas, kMmaProbeThreads, kMmaProbeSmem, static_cast<cudaStream_t>(stream)>>>(
-      mma_m, mma_n, iters, accumulators, out, status);
+      mma_m, mma_n, iters, accumulators, issuers, out, status);
   return cudaGetLastError();
 }
 

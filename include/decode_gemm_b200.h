@@ -285,15 +285,16 @@ int dg_probe_naive_read(const void* buf, unsigned long long bytes, int blocks_pe
                         unsigned long long* sink, void* stream);
 int dg_num_sms(void);
 
-/* tcgen05.mma cost probe: each of `ctas` CTAs (at most one per SM) issues
-   `iters` kind::f8f6f4 MMAs of shape mma_m x mma_n x 32 (mma_m 64 or 128;
-   mma_n a multiple of 8 (M 64) or 16 (M 128), at most 256) from zeroed smem
-   operands, round-robin over `accumulators` TMEM accumulators
-   (accumulators * mma_n <= 512).  out[2c] = clock64 cycles to issue them,
-   out[2c+1] = cycles until all have completed; -1 and *status = 0x93 if a
-   completion wait timed out. */
-int dg_probe_mma(int mma_m, int mma_n, int iters, int accumulators, int ctas, long long* out, int* status,
-                 void* stream);
+/* tcgen05.mma cost probe: in each of `ctas` CTAs (at most one per SM)
+   `issuers` warps (1..4) issue iters / issuers kind::f8f6f4 MMAs each, of
+   shape mma_m x mma_n x 32 (mma_m 64 or 128; mma_n a multiple of 8 (M 64) or
+   16 (M 128), at most 256) from zeroed smem operands, every warp round-robin
+   over its own `accumulators` TMEM accumulators (runs of four MMAs
+   accumulate; issuers * accumulators * mma_n <= 512).  out[2c] = clock64
+   cycles until the slowest warp has issued, out[2c+1] = cycles until all
+   have completed; -1 and *status = 0x93 if a completion wait timed out. */
+int dg_probe_mma(int mma_m, int mma_n, int iters, int accumulators, int issuers, int ctas, long long* out,
+                 int* status, void* stream);
 
 #ifdef __cplusplus
 }
