@@ -503,59 +503,77 @@ def b200_arm(args, rank, world, local_rank):
         del graphs
         gs.check_status()
         # Strong scaling: the one n x k layer N-sharded over
-        # the ranks, each streaming n/world rows, then the gather.
+        # the ranks, each streaming n/world rows, then the gather -- at the
+        # headline M and at config 5's M = 1, 8, 64.
         n_s = n // world
         strong = None
         if n % world == 0 and n_s % 128 == 0:
             q_s = qw[:n_s].contiguous()
-            cfg_s = default_config(m, n_s, k, layout=layout, pdl=pdl, independent_inputs=independent)
-            rot_s = Rotation(q_s, layout, cfg_s.block_n, dev)
-            gs_s = GemmSetup(rot_s, cfg_s, m, qx, wscale[: n_s // 128].contiguous(), ascale, dev)
-            gathered_s = torch.empty((world * m, n_s), dtype=torch.bfloat16, device=dev)
-            graphs = capture(lambda i: gs_s.launch(i, stream), K)
-            t_s = timed(graphs)
-            del graphs
+            ws_s = wscale[: n_s // 128].contiguous()
+            rot_cache = {}
 
-            cfg_sd = default_config(m, n_s, k, layout=layout, pdl=pdl, independent_inputs=False)
-            gs_sd = gs_s if cfg_sd == cfg_s else GemmSetup(
-                Rotation(q_s, layout, cfg_sd.block_n, dev) if cfg_sd.block_n != cfg_s.block_n else rot_s,
-                cfg_sd, m, qx, wscale[: n_s // 128].contiguous(), ascale, dev)
-            with torch.cuda.stream(stream):
-                for i in range(3):
+            def rot_for(block_n):
+                key = 0 if layout == dg.LAYOUT_RAW else block_n
+                if key not in rot_cache:
+                    rot_cache[key] = Rotation(q_s, layout, block_n, dev)
+                return rot_cache[key]
+
+            def strong_for(mm, qx_m, ascale_m):
+                cfg_s = default_config(mm, n_s, k, layout=layout, pdl=pdl, independent_inputs=independent)
+                gs_s = GemmSetup(rot_for(cfg_s.block_n), cfg_s, mm, qx_m, ws_s, ascale_m, dev)
+                gathered_s = torch.empty((world * mm, n_s), dtype=torch.bfloat16, device=dev)
+                graphs = capture(lambda i: gs_s.launch(i, stream), K)
+                t_s = timed(graphs)
+                del graphs
+                cfg_sd = default_config(mm, n_s, k, layout=layout, pdl=pdl, independent_inputs=False)
+                gs_sd = gs_s if cfg_sd == cfg_s else GemmSetup(rot_for(cfg_sd.block_n), cfg_sd, mm, qx_m, ws_s,
+                                                               ascale_m, dev)
+                with torch.cuda.stream(stream):
+                    for i in range(3):
+                        gs_sd.launch(i, stream)
+                torch.cuda.synchronize(dev)
+
+                def strong_tp(i):
                     gs_sd.launch(i, stream)
-            torch.cuda.synchronize(dev)
+                    dist.all_gather_into_tensor(gathered_s, gs_sd.out, group=pg)
+                graphs = capture(strong_tp, K)
+                t_s_tp = timed(graphs)
+                del graphs
+                fused_s = dg_tp.FusedGather(mm, n_s, device=dev)
+                fdesc_s = [fused_s.descriptor(0), fused_s.descriptor(1)]
 
-            def strong_tp(i):
-                gs_sd.launch(i, stream)
-                dist.all_gather_into_tensor(gathered_s, gs_sd.out, group=pg)
-            graphs = capture(strong_tp, K)
-            t_s_tp = timed(graphs)
-            del graphs
-            fused_s = dg_tp.FusedGather(m, n_s, device=dev)
-            fdesc_s = [fused_s.descriptor(0), fused_s.descriptor(1)]
+                def strong_fused(i):
+                    rc = dg.launch_gather(gs_s.cfg, gs_s.probs[i % gs_s.nsets], fdesc_s[i % 2],
+                                          gs_s.wmaps[i % gs_s.nsets], gs_s.amap, stream, pdl_attr=gs_s.cfg.pdl)
+                    if rc != 0:
+                        raise RuntimeError(f"fused launch failed: cudaError {rc}")
 
-            def strong_fused(i):
-                rc = dg.launch_gather(gs_s.cfg, gs_s.probs[i % gs_s.nsets], fdesc_s[i % 2],
-                                      gs_s.wmaps[i % gs_s.nsets], gs_s.amap, stream, pdl_attr=gs_s.cfg.pdl)
-                if rc != 0:
-                    raise RuntimeError(f"fused launch failed: cudaError {rc}")
-            def strong_fused_steps(i):
-                strong_fused(i)
-                if i == K - 1:
-                    fused_s.wait((K - 1) % 2, stream=stream, status=gs_s.status)
-            graphs = capture(strong_fused_steps, K)
-            t_s_fused = timed(graphs)
-            del graphs
-            fused_s.close()
-            gs_s.check_status()
-            byt_layer = n * k + m * k + 2 * m * n
-            strong = {"N_layer": n, "rows_per_gpu": n_s,
-                      "gemm_only": {"us_per_gemm": t_s / K * 1e6, "GBps_job": byt_layer / (t_s / K) / 1e9},
-                      "with_gather": {"us_per_step": t_s_tp / K * 1e6,
-                                      "GBps_job": byt_layer / (t_s_tp / K) / 1e9},
-                      "with_fused_gather": {"us_per_step": t_s_fused / K * 1e6,
-                                            "GBps_job": byt_layer / (t_s_fused / K) / 1e9}}
-            del rot_s, gs_s
+                def strong_fused_steps(i):
+                    strong_fused(i)
+                    if i == K - 1:
+                        fused_s.wait((K - 1) % 2, stream=stream, status=gs_s.status)
+                graphs = capture(strong_fused_steps, K)
+                t_s_fused = timed(graphs)
+                del graphs
+                fused_s.close()
+                gs_s.check_status()
+                byt_layer = n * k + mm * k + 2 * mm * n
+                return {"M": mm, "N_layer": n, "rows_per_gpu": n_s,
+                        "gemm_only": {"us_per_gemm": t_s / K * 1e6, "GBps_job": byt_layer / (t_s / K) / 1e9},
+                        "with_gather": {"us_per_step": t_s_tp / K * 1e6,
+                                        "GBps_job": byt_layer / (t_s_tp / K) / 1e9},
+                        "with_fused_gather": {"us_per_step": t_s_fused / K * 1e6,
+                                              "GBps_job": byt_layer / (t_s_fused / K) / 1e9}}
+
+            strong = strong_for(m, qx, ascale)
+            strong["m_sweep"] = []
+            for mm in (1, 8, 64):
+                if mm == m:
+                    strong["m_sweep"].append({kk: vv for kk, vv in strong.items() if kk != "m_sweep"})
+                    continue
+                q_m, s_m, _ = act(mm)
+                strong["m_sweep"].append(strong_for(mm, q_m, s_m))
+            del rot_cache
         tp = {"with_gather": {"us_per_step": t_tp / K * 1e6, "GBps_job": byt_job / (t_tp / K) / 1e9,
                               "collective": "NCCL all_gather_into_tensor of the bf16 [M, N/g] slices"},
               "with_fused_gather": {"us_per_step": t_fused / K * 1e6, "GBps_job": byt_job / (t_fused / K) / 1e9,
@@ -1056,6 +1074,10 @@ def b200_arm(args, rank, world, local_rank):
         "m_sweep": sweep,
         "cublaslt_fp8": cublas,
         "tensor_parallel": tp,
+        # BASELINE config 5 as strong scaling: the one N x K layer split over
+        # the ranks (also inside tensor_parallel), at the headline M and at
+        # M = 1, 8, 64.
+        "strong_scaling": tp.get("strong_scaling") if tp else None,
         "chain_61": chain,
     }
     print(json.dumps(line), file=JSON_OUT, flush=True)

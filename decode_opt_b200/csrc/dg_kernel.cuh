@@ -813,10 +813,11 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   const long long G = p.num_ctas;
   const long long U = p.total_units;
   const long long cta = static_cast<long long>(blockIdx.x) * gridDim.y + blockIdx.y;
-  // The grid and block of the plan, and under cluster split-K clusters of all
-  // gridDim.y CTAs of a tile (a launch without them could not reduce).
+  // The grid, block and shared memory of the plan, and under cluster split-K
+  // clusters of all gridDim.y CTAs of a tile (a launch without them could
+  // not reduce).
   if (static_cast<long long>(gridDim.x) * gridDim.y != G || blockDim.x != Tr::kThreads ||
-      ((p.flags & kFlagCluster) && cluster_dim_y() != gridDim.y)) {
+      dynamic_smem_size() < p.smem_bytes || ((p.flags & kFlagCluster) && cluster_dim_y() != gridDim.y)) {
     if (threadIdx.x == 0 && p.status != nullptr) atomicCAS(p.status, 0, kErrBadLaunchShape);
     return;
   }

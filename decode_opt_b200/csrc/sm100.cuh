@@ -357,6 +357,12 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
+// Dynamic shared memory this launch gave the CTA, in bytes.
+__device__ __forceinline__ uint32_t dynamic_smem_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(r));
+  return r;
+}
 // CTAs of this CTA's cluster along y (1 when launched without clusters).
 __device__ __forceinline__ uint32_t cluster_dim_y() {
   uint32_t r;

@@ -211,10 +211,11 @@ struct KernelConfig {
   static __host__ __device__ constexpr uint32_t num_ctas(int n) {
     return num_ctas_x(n) * static_cast<uint32_t>(kClusterSplit);
   }
+  // Dynamic shared memory of a launch for M = m: the plan's (N does not
+  // enter it).
   static __host__ __device__ uint32_t dynamic_smem_bytes(int m, int k) {
-    (void)m;
-    (void)k;
-    return kFixedSmemBytes;
+    const dg::Plan pl = dg::make_plan(b200_config(), m, kBlockN, k, 0);
+    return pl.error == nullptr ? pl.smem_bytes : kFixedSmemBytes;
   }
   template <uint32_t K>
   static constexpr bool k_ok_for_splitk() {
