@@ -246,6 +246,15 @@ struct KernelTraits {
   static constexpr int kThreads = block_threads(kCopies, kEpw);
   static constexpr int kLdBatch = 4;                 // 16-column TMEM loads per wait
   static constexpr int kRedGroups = 2;               // plain-path reduction units in flight per thread
+  // Cluster reduction units a thread may hold in registers while its grid
+  // still waits on the preceding one (the deferred reduction of
+  // cluster_sum_units).  Four covers M <= 32 in every class (a thread folds
+  // kColsPerWarp columns of one row, so S >= 2 ranks leave it at most
+  // kColsPerWarp / 8 units: 4 at M <= 32); measured with independent inputs
+  // at C2, deferring took M = 32 from 21.8 to 19.3-20.2 us, left M <= 16
+  // and M = 64 unchanged within noise and took M = 128 from 23.9 to 28.3 us,
+  // so larger shares keep the wait-first order.
+  static constexpr int kDeferUnits = 4;
   static constexpr int kNumBufs = 2;                 // 2 x 256 columns = all of TMEM
   static constexpr uint32_t kTmemCols = 512u;
   static_assert(kColsPerCopy == kEpw * kColsPerWarp, "column split");
@@ -760,6 +769,104 @@ __device__ __forceinline__ void cluster_reduce_tile(const KernelParams& p, uint3
   }
 }
 
+// The cluster reduction in two passes, for a grid whose inputs do not come
+// from the preceding grid (kFlagIndependentInputs): pass one sums this
+// thread's units over the S partials (the same rank order as
+// cluster_reduce_tile, so the same bits) into registers as packed bf16,
+// before the grid waits on the preceding one; pass two stores them after it.
+// Only the global stores must follow the preceding grid, so the cluster
+// barriers and the distributed-shared-memory reads overlap its tail instead
+// of holding the SM idle.  Needs every unit of the thread in `R` registers
+// (cluster_units_per_thread <= R).
+__device__ __forceinline__ int cluster_units_per_thread(const KernelParams& p, int tile, int nthreads) {
+  const int S = static_cast<int>(gridDim.y);
+  const int bn_t = min(p.block_n, p.N - tile * p.block_n);
+  const int q_all = p.M * ((bn_t + 3) / 4);   // at most 128 x 64
+  const int share = (q_all + S - 1) / S;
+  return (share + nthreads - 1) / nthreads;
+}
+
+template <int R>
+__device__ __forceinline__ void cluster_sum_units(const KernelParams& p, uint32_t buf, int tile, int tid, int nthreads,
+                                                  uint2 (&staged)[R]) {
+  using namespace sm100;
+  const int S = static_cast<int>(gridDim.y);
+  const int r = static_cast<int>(cluster_ctarank());
+  const int bn = p.block_n;
+  const int bn_s = cluster_partial_stride(bn);
+  const int bn_t = min(bn, p.N - tile * bn);
+  const int u4 = (bn_t + 3) / 4;
+  const int q_all = p.M * u4;   // at most 128 x 64
+  const int lo = r * q_all / S;
+  const int hi = (r + 1) * q_all / S;
+#pragma unroll
+  for (int j = 0; j < R; ++j) {
+    const int u = lo + tid + j * nthreads;
+    if (u >= hi) continue;
+    const int m = u / u4;
+    const int c4 = u - m * u4;
+    const uint32_t off = buf + static_cast<uint32_t>((m * bn_s + 4 * (c4 ^ (m & 7))) * 4);
+    float4 tot = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int q0 = 0; q0 < kMaxClusterSplit; q0 += 4) {
+      if (q0 >= S) break;
+      float4 v[4];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj)
+        if (q0 + jj < S) v[jj] = ld_shared_cluster_f4(map_shared_rank(off, static_cast<uint32_t>(q0 + jj)));
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        if (q0 + jj >= S) continue;
+        if (q0 + jj == 0) {
+          tot = v[jj];
+        } else {
+          tot.x += v[jj].x;
+          tot.y += v[jj].y;
+          tot.z += v[jj].z;
+          tot.w += v[jj].w;
+        }
+      }
+    }
+    const __nv_bfloat162 lo2 = __floats2bfloat162_rn(tot.x, tot.y);
+    const __nv_bfloat162 hi2 = __floats2bfloat162_rn(tot.z, tot.w);
+    staged[j].x = *reinterpret_cast<const uint32_t*>(&lo2);
+    staged[j].y = *reinterpret_cast<const uint32_t*>(&hi2);
+  }
+}
+
+template <int R>
+__device__ __forceinline__ void cluster_store_units(const KernelParams& p, int tile, int tid, int nthreads,
+                                                    bool out_vec, const uint2 (&staged)[R]) {
+  using namespace sm100;
+  const int S = static_cast<int>(gridDim.y);
+  const int r = static_cast<int>(cluster_ctarank());
+  const int bn = p.block_n;
+  const int bn_t = min(bn, p.N - tile * bn);
+  const int u4 = (bn_t + 3) / 4;
+  const int q_all = p.M * u4;   // at most 128 x 64
+  const int lo = r * q_all / S;
+  const int hi = (r + 1) * q_all / S;
+  const int col_base = tile * bn;
+#pragma unroll
+  for (int j = 0; j < R; ++j) {
+    const int u = lo + tid + j * nthreads;
+    if (u >= hi) continue;
+    const int m = u / u4;
+    const int c = 4 * (u - m * u4);
+    const int valid = min(4, bn_t - c);
+    for (int o = 0; o < p.n_outs; ++o) {
+      __nv_bfloat16* dst = p.outs[o] + static_cast<size_t>(m) * p.ldo + col_base + c;
+      if (out_vec && valid == 4) {
+        *reinterpret_cast<uint2*>(dst) = staged[j];
+      } else {
+        const uint32_t w2[2] = {staged[j].x, staged[j].y};
+        for (int e = 0; e < valid; ++e)
+          dst[e] = reinterpret_cast<const __nv_bfloat16*>(w2)[e];
+      }
+    }
+  }
+}
+
 // Fused gather (tensor parallel, world > 1), run by thread 0 of every CTA
 // after the CTA's last output store.  Every output element was stored to all
 // world ranks' gathered buffers (peer memory mapped over NVLink).  Each CTA
@@ -1140,7 +1247,10 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         }
 
         // ----------------------------------------------------- emit ------
-        if (!waited) {
+        // Global writes follow the preceding grid; a cluster CTA's partial
+        // goes to its own shared memory, and the wait comes before its first
+        // global store, after the cluster reduction.
+        if (!waited && !(p.flags & kFlagCluster)) {
           griddep_wait();
           waited = true;
         }
@@ -1242,14 +1352,31 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
                                            active_tid, static_cast<int>(epi_threads), ws_vec, out_vec, smem,
                                            p.w_region_bytes + p.a_region_bytes, red_bar, red_mailbox, abort_flag);
       if (p.flags & kFlagCluster) {
-        if (!waited) griddep_wait();   // a CTA without units still stores its share
+        const int tile = static_cast<int>(blockIdx.x);
+        // Independent inputs: reduce before waiting on the preceding grid
+        // when this thread's units fit in registers.
+        const bool defer = !waited && cluster_units_per_thread(p, tile, static_cast<int>(epi_threads)) <= Tr::kDeferUnits;
+        if (!waited && !defer) griddep_wait();   // a CTA without units still stores its share
         cluster_sync_acq_rel();        // every partial of the tile is in place
-        if (*abort_flag == 0) {
-          if (leader) *wrote_output = 1;
-          cluster_reduce_tile(p, smem_addr(w_region), static_cast<int>(blockIdx.x), active_tid,
-                              static_cast<int>(epi_threads), out_vec);
+        if (defer) {
+          uint2 staged[Tr::kDeferUnits];
+          const bool live = *abort_flag == 0;
+          if (live)
+            cluster_sum_units<Tr::kDeferUnits>(p, smem_addr(w_region), tile, active_tid, static_cast<int>(epi_threads),
+                                               staged);
+          cluster_sync_acq_rel();      // no peer reads this CTA's partial any more
+          griddep_wait();              // the stores follow the preceding grid
+          if (live) {
+            if (leader) *wrote_output = 1;
+            cluster_store_units<Tr::kDeferUnits>(p, tile, active_tid, static_cast<int>(epi_threads), out_vec, staged);
+          }
+        } else {
+          if (*abort_flag == 0) {
+            if (leader) *wrote_output = 1;
+            cluster_reduce_tile(p, smem_addr(w_region), tile, active_tid, static_cast<int>(epi_threads), out_vec);
+          }
+          cluster_sync_acq_rel();      // no peer reads this CTA's partial any more
         }
-        cluster_sync_acq_rel();        // no peer reads this CTA's partial any more
       }
     } else if (p.flags & kFlagCluster) {
       cluster_sync_acq_rel();
