@@ -136,7 +136,8 @@ class B200Config:
 
 
 def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool = True,
-                   independent_inputs: bool = False, schedule: str = "cluster") -> B200Config:
+                   independent_inputs: bool = False, schedule: str = "cluster",
+                   quantized_output: bool = False) -> B200Config:
     """The B200 schedule used by :func:`fp8_decode_gemm` and the benchmark.
 
     Two 128-K blocks per stage and weight tiles on the tcgen05 N side, 256
@@ -157,18 +158,34 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
       workspace reduction (two 64 KiB stages).
 
     `independent_inputs` sets FLAG_INDEPENDENT_INPUTS (see
-    include/decode_gemm_b200.h).
+    include/decode_gemm_b200.h).  `quantized_output` asks for a configuration
+    :func:`launch_quantized` accepts: the cluster schedule on 256-row tiles
+    (whole 128-column quantisation blocks per tile) with at least two CTAs
+    per tile; ValueError where the cluster plan does not apply or N is not a
+    multiple of 128.
     """
     from dataclasses import replace
     flags = FLAG_INDEPENDENT_INPUTS if independent_inputs else 0
     stream_k = B200Config(m_tile=m_tile_for(m), block_n=256, subs=2, stages=2, layout=layout, pdl=pdl,
                           split_k=1, grid_ctas=-1, flags=flags)
-    if schedule == "stream_k":
+    if schedule == "stream_k" and not quantized_output:
         return stream_k
-    if schedule != "cluster":
+    if schedule not in ("cluster", "stream_k"):
         raise ValueError("schedule must be 'cluster' or 'stream_k'")
     base = replace(stream_k, grid_ctas=GRID_CLUSTER, stages=0)
     p256 = base.plan(m, n, k)
+    if quantized_output:
+        if schedule != "cluster" or n % 128 != 0 or p256.error is not None:
+            raise ValueError(f"no quantized-output plan for M={m} N={n} K={k}: needs the cluster schedule "
+                             f"and N a multiple of 128 ({p256.error})")
+        if p256.cluster < 2:
+            # The quantisation runs in the cluster reduction: at least two
+            # CTAs per tile (a CTA without a K chunk adds a zero partial).
+            base = replace(base, split_k=2)
+            err = base.plan(m, n, k).error
+            if err is not None:
+                raise ValueError(f"no quantized-output plan for M={m} N={n} K={k}: {err}")
+        return base
     if p256.error is not None or p256.cluster < 2:
         return stream_k
     if n % 224 == 0:
@@ -537,6 +554,24 @@ def launch_with_maps(cfg, p: Problem, w_map: TensorMap, a_map: TensorMap, stream
         attr = cfg.PDL
     return _lib.lib().dg_launch_with_maps(ctypes.byref(b.to_dg()), ctypes.byref(p.to_dg()), w_map, a_map,
                                           _stream_handle(stream), int(bool(attr)))
+
+
+def launch_quantized(cfg, p: Problem, w_map: TensorMap, a_map: TensorMap, q_out, q_scales, stream=None,
+                     pdl_attr: Optional[bool] = None) -> int:
+    """``launch_with_maps`` that also writes the next layer's activation:
+    e4m3 ``q_out`` [M, N] (uint8) and fp32 ``q_scales`` [M, N/128], the
+    block quantisation of this GEMM's bf16 output (bench/bench_decode.cu:459-467)
+    -- the bytes ``quantize_activation`` would make from it -- computed in the
+    cluster reduction (``dg_launch_quantized``).  Needs the cluster schedule
+    and N, block_n multiples of 128.  Returns a cudaError_t value."""
+    b = _b200(cfg, p)
+    attr = b.pdl if pdl_attr is None else pdl_attr
+    if tuple(q_out.shape) != (p.M, p.N) or tuple(q_scales.shape) != (p.M, p.N // 128) or \
+            not q_out.is_contiguous() or not q_scales.is_contiguous():
+        return CUDA_ERROR_INVALID_VALUE
+    return _lib.lib().dg_launch_quantized(ctypes.byref(b.to_dg()), ctypes.byref(p.to_dg()), w_map, a_map,
+                                          q_out.data_ptr(), q_scales.data_ptr(), _stream_handle(stream),
+                                          int(bool(attr)))
 
 
 def launch_gather(cfg, p: Problem, gather, w_map: TensorMap, a_map: TensorMap, stream=None,

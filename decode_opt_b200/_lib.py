@@ -13,7 +13,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libdecode_gemm_b200.so")
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 LAYOUT_RAW = 0
 LAYOUT_PACKED = 1
@@ -35,7 +35,7 @@ EXPORTED_SYMBOLS = (
     "dg_packed_weight_bytes", "dg_status_string", "dg_flush_l2", "dg_probe_bulk_stream",
     "dg_probe_naive_read", "dg_num_sms", "dg_launch_static_scratch", "dg_probe_mma",
     "dg_launch_gather", "dg_gather_wait", "dg_ipc_export", "dg_ipc_import", "dg_ipc_release",
-    "dg_quantize_act", "dg_max_active_clusters",
+    "dg_quantize_act", "dg_max_active_clusters", "dg_launch_quantized",
 )
 
 
@@ -136,6 +136,8 @@ def lib():
     L.dg_make_activation_map.argtypes = [cfgp, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
     L.dg_launch_with_maps.argtypes = [cfgp, probp, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                       ctypes.c_int]
+    L.dg_launch_quantized.argtypes = [cfgp, probp, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
     L.dg_launch.argtypes = [cfgp, probp, ctypes.c_void_p]
     L.dg_launch_static_scratch.argtypes = [cfgp, probp, ctypes.c_void_p, ctypes.POINTER(DgPlanInfo)]
     L.dg_prepack_weight.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,

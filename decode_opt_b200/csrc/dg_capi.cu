@@ -188,7 +188,8 @@ cudaError_t apply_gather(dg::KernelParams& p, const dg_gather* g) {
 }
 
 int launch_impl(const dg_config* cfg, const dg_problem* prob, const CUtensorMap* w_map,
-                const CUtensorMap* a_map, cudaStream_t stream, bool pdl_attr, const dg_gather* g = nullptr) {
+                const CUtensorMap* a_map, cudaStream_t stream, bool pdl_attr, const dg_gather* g = nullptr,
+                void* q_out = nullptr, float* q_scales = nullptr) {
   if (cfg == nullptr || prob == nullptr) return cudaErrorInvalidValue;
   const Config c = to_config(cfg);
   Plan plan = plan_for(c, prob->M, prob->N, prob->K);
@@ -206,6 +207,18 @@ int launch_impl(const dg_config* cfg, const dg_problem* prob, const CUtensorMap*
   p.weight = static_cast<const uint8_t*>(prob->weight);
   const cudaError_t buf_err = dg::check_buffers(plan, p);
   if (buf_err != cudaSuccess) return buf_err;
+  if (q_out != nullptr || q_scales != nullptr) {
+    // The fused quantiser owns whole 128-column blocks of one tile and stores
+    // 8-byte bf16 and 4-byte e4m3 vectors.
+    if (q_out == nullptr || q_scales == nullptr || g != nullptr || (p.flags & dg::kFlagCluster) == 0 ||
+        p.N % 128 != 0 || p.block_n % 128 != 0 || p.ldo != p.N ||
+        (reinterpret_cast<uintptr_t>(p.output) & 7u) != 0 || (reinterpret_cast<uintptr_t>(q_out) & 3u) != 0 ||
+        (reinterpret_cast<uintptr_t>(q_scales) & 3u) != 0)
+      return cudaErrorInvalidValue;
+    p.q_out = static_cast<uint8_t*>(q_out);
+    p.q_scales = q_scales;
+    p.flags |= dg::kFlagQuantizeOut;
+  }
   KernelEntry* k = select_kernel(plan.mma_m, plan.copies, plan.epw);
   if (k == nullptr) return cudaErrorInvalidValue;
   if (k->pool_check != cudaSuccess) return k->pool_check;
@@ -389,6 +402,15 @@ int dg_launch_with_maps(const dg_config* cfg, const dg_problem* p, const void* w
   return launch_impl(cfg, p, static_cast<const CUtensorMap*>(weight_map128),
                      static_cast<const CUtensorMap*>(activation_map128),
                      static_cast<cudaStream_t>(stream), pdl_attr != 0);
+}
+
+int dg_launch_quantized(const dg_config* cfg, const dg_problem* p, const void* weight_map128,
+                        const void* activation_map128, void* q_out, float* q_scales, void* stream, int pdl_attr) {
+  if (weight_map128 == nullptr || activation_map128 == nullptr || q_out == nullptr || q_scales == nullptr)
+    return cudaErrorInvalidValue;
+  return launch_impl(cfg, p, static_cast<const CUtensorMap*>(weight_map128),
+                     static_cast<const CUtensorMap*>(activation_map128), static_cast<cudaStream_t>(stream),
+                     pdl_attr != 0, nullptr, q_out, q_scales);
 }
 
 int dg_launch(const dg_config* cfg, const dg_problem* p, void* stream) {

@@ -86,6 +86,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -123,6 +124,9 @@ enum Flags : int {
   kFlagCluster = 16,
   // Host planning only: take the batch class from m_tile instead of M.
   kFlagClassFromMTile = 32,
+  // Cluster split-K only (set by dg_launch_quantized): the reduction also
+  // writes the e4m3 block quantisation of the bf16 output (q_out, q_scales).
+  kFlagQuantizeOut = 64,
 };
 
 constexpr int kMaxClusterSplit = 16;   // CTAs per cluster (above 8: non-portable size)
@@ -195,6 +199,8 @@ struct KernelParams {
   int* sem;                  // [num_tiles] tickets, zero between launches
   int* status;               // first error code, may be null
   const uint8_t* weight;     // kLayoutPackedSwizzled: bulk-copy source
+  uint8_t* q_out;            // kFlagQuantizeOut: e4m3 [M, N] of the bf16 output
+  float* q_scales;           // kFlagQuantizeOut: fp32 [M, N/128]
 };
 
 // Epilogue geometry shared with the host planner: weight columns one
@@ -867,6 +873,86 @@ __device__ __forceinline__ void cluster_store_units(const KernelParams& p, int t
   }
 }
 
+// The cluster reduction with the next layer's activation quantisation
+// (kFlagQuantizeOut; block_n and N multiples of 128, so every 128-column
+// block of the output lies in one tile).  Ownership is split in whole blocks:
+// rank r owns blocks [r*B/S, (r+1)*B/S) of the tile's B = M * bn_t/128, one
+// warp per block, lane l summing float4 unit 32*j + l of its row over the
+// peers in rank order -- the same sums, so the bf16 output is bit-identical
+// to cluster_reduce_tile's.  The warp then quantises its 128 bf16 values the
+// way dg_quantize_act does (bench/bench_decode.cu:459-467 of the reference):
+// amax over the block (each lane's four values in order, then a shuffle
+// tree), scale = max(amax, 1e-4) / 448, q = e4m3(clamp(v / scale, +-448)),
+// with the same comparisons, division and conversion, so the bytes and
+// scales equal the standalone quantiser's on this output.
+__device__ __forceinline__ float quant_max(float a, float b) { return a < b ? b : a; }   // std::max
+__device__ __forceinline__ float quant_min(float a, float b) { return b < a ? b : a; }   // std::min
+
+__device__ __forceinline__ void cluster_reduce_tile_quant(const KernelParams& p, uint32_t buf, int tile, int wid,
+                                                          int lane, int nwarps) {
+  using namespace sm100;
+  const int S = static_cast<int>(gridDim.y);
+  const int r = static_cast<int>(cluster_ctarank());
+  const int bn = p.block_n;
+  const int bn_s = cluster_partial_stride(bn);
+  const int bn_t = min(bn, p.N - tile * bn);
+  const int bpr = bn_t / 128;                  // 128-column blocks per row of this tile
+  const int blocks = p.M * bpr;
+  const int blo = r * blocks / S;
+  const int bhi = (r + 1) * blocks / S;
+  const int col_base = tile * bn;
+  const int kb_next = p.N / 128;
+  for (int blk = blo + wid; blk < bhi; blk += nwarps) {
+    const int m = blk / bpr;
+    const int jb = blk - m * bpr;
+    const int c4 = jb * 32 + lane;
+    const uint32_t off = buf + static_cast<uint32_t>((m * bn_s + 4 * (c4 ^ (m & 7))) * 4);
+    float4 tot = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int q0 = 0; q0 < kMaxClusterSplit; q0 += 8) {
+      if (q0 >= S) break;
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (q0 + j < S) v[j] = ld_shared_cluster_f4(map_shared_rank(off, static_cast<uint32_t>(q0 + j)));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (q0 + j >= S) continue;
+        if (q0 + j == 0) {
+          tot = v[j];
+        } else {
+          tot.x += v[j].x;
+          tot.y += v[j].y;
+          tot.z += v[j].z;
+          tot.w += v[j].w;
+        }
+      }
+    }
+    const __nv_bfloat162 lo2 = __floats2bfloat162_rn(tot.x, tot.y);
+    const __nv_bfloat162 hi2 = __floats2bfloat162_rn(tot.z, tot.w);
+    const size_t col = static_cast<size_t>(col_base) + 4u * static_cast<uint32_t>(c4);
+    uint2 pk;
+    pk.x = *reinterpret_cast<const uint32_t*>(&lo2);
+    pk.y = *reinterpret_cast<const uint32_t*>(&hi2);
+    *reinterpret_cast<uint2*>(p.output + static_cast<size_t>(m) * p.ldo + col) = pk;
+    const float v4[4] = {__low2float(lo2), __high2float(lo2), __low2float(hi2), __high2float(hi2)};
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) amax = quant_max(amax, fabsf(v4[j]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = quant_max(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = quant_max(amax, 1.0e-4f) / 448.0f;
+    uint32_t packed = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float c = quant_min(quant_max(v4[j] / scale, -448.0f), 448.0f);
+      packed |= static_cast<uint32_t>(__nv_fp8_e4m3(c).__x) << (8 * j);
+    }
+    *reinterpret_cast<uint32_t*>(p.q_out + static_cast<size_t>(m) * p.N + col) = packed;
+    if (lane == 0) p.q_scales[static_cast<size_t>(m) * kb_next + col_base / 128 + jb] = scale;
+  }
+}
+
 // Fused gather (tensor parallel, world > 1), run by thread 0 of every CTA
 // after the CTA's last output store.  Every output element was stored to all
 // world ranks' gathered buffers (peer memory mapped over NVLink).  Each CTA
@@ -1355,7 +1441,9 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         const int tile = static_cast<int>(blockIdx.x);
         // Independent inputs: reduce before waiting on the preceding grid
         // when this thread's units fit in registers.
-        const bool defer = !waited && cluster_units_per_thread(p, tile, static_cast<int>(epi_threads)) <= Tr::kDeferUnits;
+        const bool quant = (p.flags & kFlagQuantizeOut) != 0;
+        const bool defer = !waited && !quant &&
+                           cluster_units_per_thread(p, tile, static_cast<int>(epi_threads)) <= Tr::kDeferUnits;
         if (!waited && !defer) griddep_wait();   // a CTA without units still stores its share
         cluster_sync_acq_rel();        // every partial of the tile is in place
         if (defer) {
@@ -1373,7 +1461,11 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         } else {
           if (*abort_flag == 0) {
             if (leader) *wrote_output = 1;
-            cluster_reduce_tile(p, smem_addr(w_region), tile, active_tid, static_cast<int>(epi_threads), out_vec);
+            if (quant)
+              cluster_reduce_tile_quant(p, smem_addr(w_region), tile, active_tid / 32, active_tid & 31,
+                                        static_cast<int>(epi_threads) / 32);
+            else
+              cluster_reduce_tile(p, smem_addr(w_region), tile, active_tid, static_cast<int>(epi_threads), out_vec);
           }
           cluster_sync_acq_rel();      // no peer reads this CTA's partial any more
         }

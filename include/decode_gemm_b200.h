@@ -24,6 +24,8 @@
  *   dg_launch_with_maps     launch_with_maps    kernels/decode_gemm.cuh:1113-1147
  *                           (and the harness's direct cudaLaunchKernelEx of
  *                           fp8_decode_gemm<Cfg>, bench/variant_impl.cuh:136-165)
+ *   dg_launch_quantized     (new) launch_with_maps fused with the next layer's
+ *                           activation quantisation (bench/bench_decode.cu:459-467)
  *   dg_launch               launch              kernels/decode_gemm.cuh:1150-1159
  *   dg_launch_static_scratch (none: no counterpart in the reference) dg_launch
  *                           with library-owned static split-K scratch
@@ -53,7 +55,7 @@
 extern "C" {
 #endif
 
-#define DG_ABI_VERSION 4
+#define DG_ABI_VERSION 5
 
 /* Weight layouts. */
 #define DG_LAYOUT_RAW 0             /* W[N,K], K contiguous (checkpoint layout) */
@@ -179,6 +181,18 @@ int dg_make_activation_map(const dg_config* cfg, const void* activation, int M, 
    serialization for this launch independently of cfg->pdl. */
 int dg_launch_with_maps(const dg_config* cfg, const dg_problem* p, const void* weight_map128,
                         const void* activation_map128, void* stream, int pdl_attr);
+
+/* (new) The GEMM and the next layer's activation quantisation in one kernel:
+   besides the bf16 output it writes q_out [M,N] e4m3 and q_scales [M,N/128]
+   fp32 -- the block quantisation of that bf16 output (bench/bench_decode.cu
+   459-467 of the reference, which the reference's decode chain runs as a
+   separate step, here dg_quantize_act), bit for bit the bytes and scales
+   dg_quantize_act would write from it.  Cluster split-K schedule only
+   (grid_ctas == DG_GRID_CLUSTER), N and block_n multiples of 128, output
+   8-byte and q_out / q_scales 4-byte aligned; the quantised stores, like the
+   output's, follow griddepcontrol.wait.  Otherwise as dg_launch_with_maps. */
+int dg_launch_quantized(const dg_config* cfg, const dg_problem* p, const void* weight_map128,
+                        const void* activation_map128, void* q_out, float* q_scales, void* stream, int pdl_attr);
 
 /* Encodes both maps, then launches (attribute follows cfg->pdl). */
 int dg_launch(const dg_config* cfg, const dg_problem* p, void* stream);

@@ -278,3 +278,19 @@ def test_cluster_partial_layout_rules(bn):
             for s in (2, 3, 4, 8):
                 cover = [u for r in range(s) for u in range(r * q // s, (r + 1) * q // s)]
                 assert cover == list(range(q))
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 7168, 16384), (1, 16384, 7168), (64, 2048, 4096), (3, 640, 512),
+                                   (128, 128, 256)])
+def test_quantized_output_config(m, n, k):
+    """The configuration dg.launch_quantized takes: cluster split-K on
+    256-row tiles (whole 128-column quantisation blocks in every tile), no
+    workspace; refused where N is not a multiple of 128."""
+    c = dg.default_config(m, n, k, layout=dg.LAYOUT_PACKED_SWIZZLED, quantized_output=True)
+    p = c.plan(m, n, k)
+    assert p.error is None and c.grid_ctas == dg.GRID_CLUSTER and c.block_n == 256
+    assert p.grid == (-(-n // 256), p.cluster, 1) and p.cluster >= 2 and p.ws_floats == 0 and p.sem_ints == 0
+    with pytest.raises(ValueError):
+        dg.default_config(m, n + 64, k, quantized_output=True)
+    with pytest.raises(ValueError):
+        dg.default_config(m, n, k, schedule="stream_k", quantized_output=True)
