@@ -577,10 +577,15 @@ def launch_quantized(cfg, p: Problem, w_map: TensorMap, a_map: TensorMap, q_out,
 def launch_gather(cfg, p: Problem, gather, w_map: TensorMap, a_map: TensorMap, stream=None,
                   pdl_attr: Optional[bool] = None) -> int:
     """Tensor-parallel launch with the all-gather fused into the kernel
-    (``dg_launch_gather``; ``gather`` is a ``DgGather``, e.g. from
+    (``gather`` a ``DgGather``: ``dg_launch_gather``, epoch flags; or a
+    ``DgGatherLines``: ``dg_launch_gather_lines``, tagged lines; both from
     ``tp.FusedGather.descriptor``).  Returns a cudaError_t value."""
     b = _b200(cfg, p)
     attr = b.pdl if pdl_attr is None else pdl_attr
+    if isinstance(gather, _lib.DgGatherLines):
+        return _lib.lib().dg_launch_gather_lines(ctypes.byref(b.to_dg()), ctypes.byref(p.to_dg()),
+                                                 ctypes.byref(gather), w_map, a_map, _stream_handle(stream),
+                                                 int(bool(attr)))
     return _lib.lib().dg_launch_gather(ctypes.byref(b.to_dg()), ctypes.byref(p.to_dg()), ctypes.byref(gather),
                                        w_map, a_map, _stream_handle(stream), int(bool(attr)))
 

@@ -13,7 +13,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libdecode_gemm_b200.so")
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 LAYOUT_RAW = 0
 LAYOUT_PACKED = 1
@@ -35,7 +35,7 @@ EXPORTED_SYMBOLS = (
     "dg_packed_weight_bytes", "dg_status_string", "dg_flush_l2", "dg_probe_bulk_stream",
     "dg_probe_naive_read", "dg_num_sms", "dg_launch_static_scratch", "dg_probe_mma",
     "dg_launch_gather", "dg_gather_wait", "dg_ipc_export", "dg_ipc_import", "dg_ipc_release",
-    "dg_quantize_act", "dg_max_active_clusters", "dg_launch_quantized",
+    "dg_quantize_act", "dg_max_active_clusters", "dg_launch_quantized", "dg_launch_gather_lines",
 )
 
 
@@ -110,6 +110,17 @@ class DgGather(ctypes.Structure):
     ]
 
 
+class DgGatherLines(ctypes.Structure):
+    _fields_ = [
+        ("world", ctypes.c_int),
+        ("rank", ctypes.c_int),
+        ("ldo", ctypes.c_int),
+        ("output", ctypes.c_void_p),
+        ("lines", ctypes.c_void_p * MAX_RANKS),
+        ("sync", ctypes.c_void_p),
+    ]
+
+
 TensorMap = ctypes.c_uint8 * 128
 IpcHandle = ctypes.c_uint8 * 64
 
@@ -157,6 +168,8 @@ def lib():
                                    ctypes.c_void_p, ctypes.c_int]
     L.dg_quantize_act.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+    L.dg_launch_gather_lines.argtypes = [cfgp, probp, ctypes.POINTER(DgGatherLines), ctypes.c_void_p,
+                                         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
     L.dg_gather_wait.argtypes = [ctypes.POINTER(DgGather), ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_void_p]
     L.dg_ipc_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_ulonglong)]
     L.dg_ipc_import.argtypes = [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_void_p)]

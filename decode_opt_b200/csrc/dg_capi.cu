@@ -187,9 +187,36 @@ cudaError_t apply_gather(dg::KernelParams& p, const dg_gather* g) {
   return cudaSuccess;
 }
 
+// Fills the fused-gather-in-lines fields of `p` from `gl` (world 1: a plain
+// launch into gl->output with row stride gl->ldo).
+cudaError_t apply_gather_lines(dg::KernelParams& p, const dg_gather_lines* gl) {
+  if (gl->world < 1 || gl->world > DG_MAX_RANKS || gl->rank < 0 || gl->rank >= gl->world || gl->output == nullptr ||
+      gl->ldo < 0 || static_cast<long long>(gl->world) * p.N > gl->ldo || (gl->ldo & 3) != 0 || (p.N & 3) != 0 ||
+      (reinterpret_cast<uintptr_t>(gl->output) & 7u) != 0)
+    return cudaErrorInvalidValue;
+  p.output = static_cast<__nv_bfloat16*>(gl->output) + static_cast<size_t>(gl->rank) * p.N;
+  p.outs[0] = p.output;
+  p.ldo = gl->ldo;
+  if (gl->world == 1) return cudaSuccess;
+  if (gl->sync == nullptr || (p.flags & dg::kFlagCluster) == 0) return cudaErrorInvalidValue;
+  for (int r = 0; r < gl->world; ++r)
+    if (gl->lines[r] == nullptr || (reinterpret_cast<uintptr_t>(gl->lines[r]) & 15u) != 0)
+      return cudaErrorInvalidValue;
+  p.world = gl->world;
+  p.rank = gl->rank;
+  p.output = static_cast<__nv_bfloat16*>(gl->output);   // the unpack writes all columns
+  p.outs[0] = p.output;
+  p.n_outs = 1;
+  for (int r = 0; r < gl->world; ++r) p.lines[r] = static_cast<uint4*>(gl->lines[r]);
+  p.lines_per_row = gl->world * p.N / 4;
+  p.sync_ctr = gl->sync;
+  p.flags |= dg::kFlagGatherLines;
+  return cudaSuccess;
+}
+
 int launch_impl(const dg_config* cfg, const dg_problem* prob, const CUtensorMap* w_map,
                 const CUtensorMap* a_map, cudaStream_t stream, bool pdl_attr, const dg_gather* g = nullptr,
-                void* q_out = nullptr, float* q_scales = nullptr) {
+                void* q_out = nullptr, float* q_scales = nullptr, const dg_gather_lines* gl = nullptr) {
   if (cfg == nullptr || prob == nullptr) return cudaErrorInvalidValue;
   const Config c = to_config(cfg);
   Plan plan = plan_for(c, prob->M, prob->N, prob->K);
@@ -199,6 +226,11 @@ int launch_impl(const dg_config* cfg, const dg_problem* prob, const CUtensorMap*
   if (g != nullptr) p.output = static_cast<__nv_bfloat16*>(g->outputs[g->rank >= 0 && g->rank < DG_MAX_RANKS ? g->rank : 0]);
   const cudaError_t g_err = apply_gather(p, g);
   if (g_err != cudaSuccess) return g_err;
+  if (gl != nullptr) {
+    if (g != nullptr || q_out != nullptr) return cudaErrorInvalidValue;
+    const cudaError_t l_err = apply_gather_lines(p, gl);
+    if (l_err != cudaSuccess) return l_err;
+  }
   p.w_scales = prob->weight_scales;
   p.a_scales = prob->activation_scales;
   p.ws = prob->splitk_ws;
@@ -470,6 +502,14 @@ int dg_launch_gather(const dg_config* cfg, const dg_problem* p, const dg_gather*
   return launch_impl(cfg, p, static_cast<const CUtensorMap*>(weight_map128),
                      static_cast<const CUtensorMap*>(activation_map128), static_cast<cudaStream_t>(stream),
                      pdl_attr != 0, g);
+}
+
+int dg_launch_gather_lines(const dg_config* cfg, const dg_problem* p, const dg_gather_lines* g,
+                           const void* weight_map128, const void* activation_map128, void* stream, int pdl_attr) {
+  if (g == nullptr || weight_map128 == nullptr || activation_map128 == nullptr) return cudaErrorInvalidValue;
+  return launch_impl(cfg, p, static_cast<const CUtensorMap*>(weight_map128),
+                     static_cast<const CUtensorMap*>(activation_map128), static_cast<cudaStream_t>(stream),
+                     pdl_attr != 0, nullptr, nullptr, nullptr, g);
 }
 
 int dg_gather_wait(const dg_gather* g, int* status, unsigned long long timeout_ns, void* stream) {

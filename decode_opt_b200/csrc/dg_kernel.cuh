@@ -127,6 +127,11 @@ enum Flags : int {
   // Cluster split-K only (set by dg_launch_quantized): the reduction also
   // writes the e4m3 block quantisation of the bf16 output (q_out, q_scales).
   kFlagQuantizeOut = 64,
+  // Cluster split-K only (set by dg_launch_gather_lines): the fused gather
+  // stores every output element as tagged lines into every rank's line buffer
+  // and each CTA unpacks a slice of this rank's buffer once it is whole (no
+  // flags, no system-scope fences).
+  kFlagGatherLines = 128,
 };
 
 constexpr int kMaxClusterSplit = 16;   // CTAs per cluster (above 8: non-portable size)
@@ -201,6 +206,8 @@ struct KernelParams {
   const uint8_t* weight;     // kLayoutPackedSwizzled: bulk-copy source
   uint8_t* q_out;            // kFlagQuantizeOut: e4m3 [M, N] of the bf16 output
   float* q_scales;           // kFlagQuantizeOut: fp32 [M, N/128]
+  uint4* lines[kMaxOutputs]; // kFlagGatherLines: rank r's line buffer of this launch's set, [M][lines_per_row]
+  int lines_per_row;         // kFlagGatherLines: world * N / 4 (4 output columns per 16-byte line)
 };
 
 // Epilogue geometry shared with the host planner: weight columns one
@@ -711,6 +718,14 @@ __device__ __noinline__ void reduce_split_tiles(const KernelParams& p, const int
   }
 }
 
+// Fused gather in lines (kFlagGatherLines).  The tag of this launch: the
+// epoch of the last launch completed on this rank + 1.  Read only after
+// griddepcontrol.wait (the last CTA of the previous launch stored it), and
+// only before this CTA counts itself done in gather_lines_complete.
+__device__ __forceinline__ uint32_t gather_lines_epoch(const KernelParams& p) {
+  return static_cast<uint32_t>(sm100::load_relaxed_gpu(p.sync_ctr + 1)) + 1u;
+}
+
 // Cluster split-K reduction of tile `tile` (kFlagCluster), run by the active
 // epilogue threads of every CTA of the tile's cluster between the two
 // cluster barriers.  `buf` is the shared::cta address of this CTA's partial
@@ -730,6 +745,8 @@ __device__ __forceinline__ void cluster_reduce_tile(const KernelParams& p, uint3
   const long long lo = r * q_all / S;
   const long long hi = (r + 1) * q_all / S;
   const int col_base = tile * bn;
+  // kFlagGatherLines: this launch's tag (read after griddepcontrol.wait).
+  const uint32_t epoch = (p.flags & kFlagGatherLines) ? gather_lines_epoch(p) : 0u;
   for (long long u = lo + tid; u < hi; u += nthreads) {
     const int m = static_cast<int>(u / u4);
     const int c4 = static_cast<int>(u - static_cast<long long>(m) * u4);
@@ -760,6 +777,18 @@ __device__ __forceinline__ void cluster_reduce_tile(const KernelParams& p, uint3
     const int valid = min(4, bn_t - c);
     const __nv_bfloat162 lo2 = __floats2bfloat162_rn(tot.x, tot.y);
     const __nv_bfloat162 hi2 = __floats2bfloat162_rn(tot.z, tot.w);
+    if (p.flags & kFlagGatherLines) {
+      // N % 4 == 0 (checked on the host), so every unit is whole.
+      const size_t line = static_cast<size_t>(m) * p.lines_per_row +
+                          static_cast<size_t>(p.rank * p.N + col_base + c) / 4;
+      const uint64_t w0 = (static_cast<uint64_t>(epoch) << 32) | *reinterpret_cast<const uint32_t*>(&lo2);
+      const uint64_t w1 = (static_cast<uint64_t>(epoch) << 32) | *reinterpret_cast<const uint32_t*>(&hi2);
+      for (int i = 1; i <= p.world; ++i) {            // peers first, this rank last
+        const int r = (p.rank + i) % p.world;
+        st_volatile_line(p.lines[r] + line, w0, w1);
+      }
+      continue;
+    }
     for (int o = 0; o < p.n_outs; ++o) {
       __nv_bfloat16* dst = p.outs[o] + static_cast<size_t>(m) * p.ldo + col_base + c;
       if (out_vec && valid == 4) {
@@ -993,6 +1022,59 @@ __device__ __noinline__ inline void gather_complete(const KernelParams& p, bool 
     }
   }
   fence_acq_rel_sys();
+}
+
+// Completion of the fused gather in lines, run by every thread of every CTA
+// after the CTA's own line stores.  Each output element travels as half of
+// an 8-byte word {2 bf16, epoch} that the writing rank stored into every
+// rank's line buffer; a word is single-copy atomic, so seeing this launch's
+// epoch in it means its payload has landed -- no fence or flag round trip.
+// CTA c polls lines [c*L/G, (c+1)*L/G) of this rank's buffer (L = M *
+// lines_per_row) until both words of each carry the epoch (bounded by
+// p.timeout_ns, status kErrGatherWait otherwise) and unpacks them into the
+// gathered [M, ldo] output.  So the grid completes only when this rank's
+// gathered output is whole, which also keeps every rank within one launch of
+// the others (the two alternating line-buffer sets rely on it).  The last CTA
+// to finish stores the epoch for the next launch.
+__device__ __noinline__ inline void gather_lines_complete(const KernelParams& p, long long cta) {
+  using namespace sm100;
+  griddep_wait();
+  const uint32_t epoch = gather_lines_epoch(p);
+  const long long total = static_cast<long long>(p.M) * p.lines_per_row;
+  const long long lo = cta * total / p.num_ctas;
+  const long long hi = (cta + 1) * total / p.num_ctas;
+  const uint4* mine = p.lines[p.rank];
+  const uint64_t start = global_timer_ns();
+  for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    uint64_t w0 = 0, w1 = 0;
+    bool ok = true;
+    for (;;) {
+      ld_volatile_line(mine + i, w0, w1);
+      if (static_cast<uint32_t>(w0 >> 32) == epoch && static_cast<uint32_t>(w1 >> 32) == epoch) break;
+      if (global_timer_ns() - start > p.timeout_ns) {
+        ok = false;
+        break;
+      }
+    }
+    if (!ok) {
+      if (p.status != nullptr) atomicCAS(p.status, 0, kErrGatherWait);
+      break;
+    }
+    const int m = static_cast<int>(i / p.lines_per_row);
+    const int col = static_cast<int>(i - static_cast<long long>(m) * p.lines_per_row) * 4;
+    uint2 v;
+    v.x = static_cast<uint32_t>(w0);
+    v.y = static_cast<uint32_t>(w1);
+    *reinterpret_cast<uint2*>(p.output + static_cast<size_t>(m) * p.ldo + col) = v;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int done = atomic_add_acq_rel_gpu(p.sync_ctr, 1);
+    if (done == p.num_ctas - 1) {
+      store_relaxed_gpu(p.sync_ctr, 0);
+      store_relaxed_gpu(p.sync_ctr + 1, static_cast<int>(epoch));
+    }
+  }
 }
 
 template <class Tr>
@@ -1442,7 +1524,7 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         // Independent inputs: reduce before waiting on the preceding grid
         // when this thread's units fit in registers.
         const bool quant = (p.flags & kFlagQuantizeOut) != 0;
-        const bool defer = !waited && !quant &&
+        const bool defer = !waited && !quant && !(p.flags & kFlagGatherLines) &&
                            cluster_units_per_thread(p, tile, static_cast<int>(epi_threads)) <= Tr::kDeferUnits;
         if (!waited && !defer) griddep_wait();   // a CTA without units still stores its share
         cluster_sync_acq_rel();        // every partial of the tile is in place
@@ -1481,7 +1563,10 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   __syncthreads();
   tc_fence_after();
   if (warp == Tr::kMmaWarp) tmem_dealloc(tmem_base, Tr::kTmemCols);
-  if (p.world > 1 && threadIdx.x == 0) gather_complete(p, *wrote_output != 0);
+  if (p.world > 1 && (p.flags & kFlagGatherLines))
+    gather_lines_complete(p, cta);
+  else if (p.world > 1 && threadIdx.x == 0)
+    gather_complete(p, *wrote_output != 0);
 }
 
 template <int MMA_M, int COPIES, int EPW>

@@ -298,6 +298,18 @@ __device__ __forceinline__ int load_relaxed_gpu(const int* addr) {
   return v;
 }
 
+// 16-byte line of two 8-byte words, each an aligned 64-bit element and so
+// single-copy atomic on its own (a vector access is a set of element
+// accesses): a reader that sees a word's tag sees that word's payload.
+// Volatile = relaxed at system scope, for peer memory.
+__device__ __forceinline__ void st_volatile_line(void* addr, uint64_t w0, uint64_t w1) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(addr), "l"(w0), "l"(w1) : "memory");
+}
+
+__device__ __forceinline__ void ld_volatile_line(const void* addr, uint64_t& w0, uint64_t& w1) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(addr) : "memory");
+}
+
 __device__ __forceinline__ int load_acquire_gpu(const int* addr) {
   int v;
   asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");

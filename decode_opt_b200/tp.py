@@ -15,7 +15,10 @@ The fused alternative (`FusedGather`, `dg_launch_gather`) drops the
 collective: each rank's GEMM stores every output element straight into all
 ranks' gathered [M, N] buffers over NVLink (peer memory mapped with CUDA IPC)
 and its grid completes only when every rank's slices of that launch have
-arrived, signalled through per-rank epoch flags with bounded waits.
+arrived, signalled through per-rank epoch flags with bounded waits
+(`dg_launch_gather_lines` instead sends the slices as tagged lines whose
+8-byte words carry the launch's epoch beside the data, so the data signals
+itself: no flags, no system-scope fences).
 
 The reference is single-GPU; this module is the B200 multi-GPU extension the
 benchmark uses (`bench.py --gpus N`).
@@ -128,6 +131,24 @@ def gather_descriptor(world: int, rank: int, n_loc: int, out_bases, flag_ptrs, s
     return g
 
 
+def lines_descriptor(world: int, rank: int, n_loc: int, output, line_bases, sync_ptr):
+    """The dg_gather_lines for rank `rank`: `output` is this rank's gathered
+    [M, world*n_loc] bf16 buffer, line_bases[q] rank q's line buffer of the
+    launch's set as mapped in this process."""
+    from ._lib import DgGatherLines, MAX_RANKS
+    if not 1 <= world <= MAX_RANKS or not 0 <= rank < world:
+        raise ValueError("bad world/rank")
+    g = DgGatherLines()
+    g.world = world
+    g.rank = rank
+    g.ldo = world * n_loc
+    g.output = int(output)
+    for q in range(world):
+        g.lines[q] = int(line_bases[q])
+    g.sync = int(sync_ptr)
+    return g
+
+
 def serving_schedule(base: int, count: int, group: int):
     """The operations of the N-GPU serving loop for requests base .. base+count-1,
     in issue order, as (kind, j, waits).
@@ -181,9 +202,16 @@ class FusedGather:
     `descriptor(i)` is the dg_gather of buffer set i: alternate i between
     consecutive launches (a rank must never overwrite slices a peer has not
     consumed yet).  Every rank must make the same launches in the same order.
+
+    ``protocol="lines"`` (dg_launch_gather_lines): peers store tagged 16-byte
+    lines {2 bf16, epoch, 2 bf16, epoch} into `buffers` line buffers of
+    m_max x world*n_loc/4 lines on every rank (exported and mapped instead of
+    the gathered buffers and flags); each rank's kernel unpacks its own into
+    its local gathered buffers.  `descriptor(i)` is then a dg_gather_lines.
     """
 
-    def __init__(self, m_max: int, n_loc: int, group=None, buffers: int = 2, device=None):
+    def __init__(self, m_max: int, n_loc: int, group=None, buffers: int = 2, device=None,
+                 protocol: str = "flags"):
         import ctypes
         import torch
         import torch.distributed as dist
@@ -193,11 +221,20 @@ class FusedGather:
         self.rank = dist.get_rank(group)
         self.n_loc = n_loc
         self.m_max = m_max
+        if protocol not in ("flags", "lines"):
+            raise ValueError("protocol must be 'flags' or 'lines'")
+        if protocol == "lines" and n_loc % 4 != 0:
+            raise ValueError("the lines protocol needs n_loc % 4 == 0")
+        self.protocol = protocol
         dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.storage = torch.zeros((buffers, m_max, self.world * n_loc), dtype=torch.bfloat16, device=dev)
         self.buffers = [self.storage[i] for i in range(buffers)]
         self.flags = torch.zeros(self.world, dtype=torch.int32, device=dev)
         self.sync = torch.zeros(2, dtype=torch.int32, device=dev)
+        if protocol == "lines":
+            # 16-byte lines: two int64 words {payload, epoch} per 4 columns
+            self.line_storage = torch.zeros((buffers, m_max, self.world * n_loc // 4, 2), dtype=torch.int64,
+                                            device=dev)
         torch.cuda.synchronize(dev)
 
         def export(t):
@@ -208,10 +245,17 @@ class FusedGather:
                 raise RuntimeError(f"dg_ipc_export failed: cudaError {rc}")
             return bytes(h), off.value
 
+        self._imported = []
+        if protocol == "lines":
+            sets = [self.line_storage[i] for i in range(buffers)]
+            everyone = [None] * self.world
+            dist.all_gather_object(everyone, [export(t) for t in sets], group=group)
+            self.peer_lines = [[sets[i].data_ptr() if q == self.rank else self._import(*everyone[q][i])
+                                for q in range(self.world)] for i in range(buffers)]
+            return
         mine = [export(b) for b in self.buffers] + [export(self.flags)]
         everyone = [None] * self.world
         dist.all_gather_object(everyone, mine, group=group)
-        self._imported = []
         self.peer_bufs = []    # [set][rank] base pointers in this process
         self.peer_flags = []
         for i in range(buffers):
@@ -234,14 +278,20 @@ class FusedGather:
         return ptr.value
 
     def descriptor(self, i: int):
+        if self.protocol == "lines":
+            return lines_descriptor(self.world, self.rank, self.n_loc, self.buffers[i].data_ptr(),
+                                    self.peer_lines[i], self.sync.data_ptr())
         return gather_descriptor(self.world, self.rank, self.n_loc, self.peer_bufs[i], self.peer_flags,
                                  self.sync.data_ptr())
 
     def wait(self, i: int, stream=None, status=None, timeout_ns: int = 0) -> None:
         """Enqueue the completion wait for the last fused launch (buffer set i
-        is then complete on this rank)."""
+        is then complete on this rank).  Under the lines protocol a completed
+        launch has already unpacked the whole set: nothing to enqueue."""
         import ctypes
         import torch
+        if self.protocol == "lines":
+            return
         d = self.descriptor(i)
         s = (stream if stream is not None else torch.cuda.current_stream()).cuda_stream
         rc = self._lib.dg_gather_wait(ctypes.byref(d), status.data_ptr() if status is not None else None,

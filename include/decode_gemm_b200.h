@@ -41,6 +41,7 @@
  *   dg_probe_naive_read     tools/peak_bw_probe.cu naive_read_nc :138-170
  *   dg_launch_gather        (new: the reference is single-GPU) tensor-parallel launch
  *                           with the all-gather fused into the epilogue
+ *   dg_launch_gather_lines  (new) the same with the gather in tagged lines (no flags)
  *   dg_gather_wait          (new) completion wait for the fused gather
  *   dg_ipc_export / dg_ipc_import / dg_ipc_release  (new) peer buffers for it
  *   dg_num_sms              (new) SM count of the current device
@@ -55,7 +56,7 @@
 extern "C" {
 #endif
 
-#define DG_ABI_VERSION 5
+#define DG_ABI_VERSION 6
 
 /* Weight layouts. */
 #define DG_LAYOUT_RAW 0             /* W[N,K], K contiguous (checkpoint layout) */
@@ -222,6 +223,33 @@ typedef struct dg_gather {
    pre-built maps and the fused gather. */
 int dg_launch_gather(const dg_config* cfg, const dg_problem* p, const dg_gather* g, const void* weight_map128,
                      const void* activation_map128, void* stream, int pdl_attr);
+
+/* (new) The fused gather without flags: every output element travels as half
+   of an 8-byte word {2 bf16, 32-bit epoch} -- single-copy atomic, so a rank
+   that sees the epoch has the data, with no system-scope fence and no flag
+   round trip (the low-latency protocol of collective libraries).  Rank r
+   stores its N columns as 16-byte lines into every rank's line buffer (world
+   * N / 4 lines per row); each CTA then waits (bounded, DG_ERR_GATHER_WAIT)
+   until its slice of this rank's buffer carries the launch's epoch and
+   unpacks it into `output`.  When the grid has completed, this rank's
+   gathered [M, ldo] output is whole.  Cluster split-K schedule only
+   (grid_ctas == DG_GRID_CLUSTER, at least two CTAs per tile), N a multiple of
+   4, output 8-byte and lines 16-byte aligned, ldo a multiple of 4.  The
+   epoch lives in sync[1]: consecutive launches must alternate between two
+   sets of line buffers, every rank must make the same sequence of launches,
+   and after any error every rank re-zeroes its line buffers and sync words.
+   p->output is ignored. */
+typedef struct dg_gather_lines {
+  int world, rank;            /* tensor-parallel group, 1 <= world <= DG_MAX_RANKS            */
+  int ldo;                    /* row stride of `output` in elements (>= world * N)             */
+  void* output;               /* this rank's gathered [M, ldo] bf16 buffer, column 0           */
+  void* lines[DG_MAX_RANKS];  /* rank q's line buffer of this launch's set (as mapped here):
+                                 M * world * N * 4 bytes, zeroed once                          */
+  int* sync;                  /* this rank's int[2] (CTA done count, last epoch), zeroed once  */
+} dg_gather_lines;
+
+int dg_launch_gather_lines(const dg_config* cfg, const dg_problem* p, const dg_gather_lines* g,
+                           const void* weight_map128, const void* activation_map128, void* stream, int pdl_attr);
 
 /* Waits on `stream` (one thread, bounded by timeout_ns, 0 = 2 s) until every
    peer has published this rank's latest epoch -- already true once the last

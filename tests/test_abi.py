@@ -42,7 +42,7 @@ def test_struct_layouts_match_header(tmp_path):
     if cc is None:
         pytest.skip("no C compiler")
     structs = {"dg_config": _lib.DgConfig, "dg_problem": _lib.DgProblem, "dg_plan_info": _lib.DgPlanInfo,
-               "dg_gather": _lib.DgGather}
+               "dg_gather": _lib.DgGather, "dg_gather_lines": _lib.DgGatherLines}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "decode_gemm_b200.h"', "int main(void) {"]
     for cname, py in structs.items():
         lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')

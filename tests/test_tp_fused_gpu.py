@@ -4,11 +4,13 @@ kernel (dg_launch_gather).
 * One GPU: the output-copy path with a row stride and a column offset (a
   world of one writing into a wider buffer); columns outside its slice keep
   their sentinel.
+* One GPU: the lines protocol (dg_launch_gather_lines) with a world of one,
+  and its rejections.
 * Two GPUs (skipped on a box with fewer): two ranks as child processes, each
   computing its N-shard and storing into both ranks' gathered buffers over
-  NVLink; after the completion wait both gathered outputs must match the
-  oracle for the whole N over two consecutive launches (alternating buffer
-  sets), with status 0.
+  NVLink (epoch flags) or both ranks' line buffers (tagged lines); after the
+  completion both gathered outputs must match the oracle for the whole N over
+  four consecutive launches (alternating buffer sets), with status 0.
 * Two GPUs: the serving loop's schedule (decode_opt_b200.tp.serving_schedule)
   run for 24 requests in groups of 4 -- H2D copies, fused GEMMs and D2H
   copies on three streams, input slots and gathered sets reused -- with five
@@ -63,6 +65,72 @@ def test_strided_output_at_column_offset():
     assert np.all(got[:, :col] == -7.0) and np.all(got[:, col + n:] == -7.0)
 
 
+def test_lines_world_one_and_rejections():
+    """dg_launch_gather_lines with a world of one is a plain launch into the
+    gathered buffer (row stride ldo); configurations the lines protocol cannot
+    serve are refused before any launch: a stream-K plan, N not a multiple of
+    4, misaligned line or output pointers, ldo < world * N."""
+    import oracle
+    from helpers import check_against_oracle
+    n, k, m = 1024, 2048, 3
+    w, ws = oracle.gen_weight_smoke(n, k, 81)
+    a, as_ = oracle.gen_activation_smoke(m, k, 82)
+    ref = oracle.compute_reference(a, as_, w, ws, threads=8)
+    dev = "cuda"
+    cfg = dg.default_config(m, n, k, layout=dg.LAYOUT_PACKED_SWIZZLED)
+    assert cfg.plan(m, n, k).cluster >= 2
+    wt = dg.prepack_weight(torch.from_numpy(w).to(dev), cfg.block_n, cfg.layout)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    p = dg.Problem(m, n, k, torch.from_numpy(a).to(dev), wt, torch.from_numpy(ws).to(dev),
+                   torch.from_numpy(as_).to(dev), None, None, None, status)
+    wm, am = dg.make_weight_tma(cfg, p), dg.make_activation_tma(cfg, p)
+    ldo = n + 64
+    wide = torch.full((m, ldo), -7.0, dtype=torch.bfloat16, device=dev)
+    sync = torch.zeros(2, dtype=torch.int32, device=dev)
+    g1 = tp.lines_descriptor(1, 0, n, wide.data_ptr(), [0], sync.data_ptr())
+    g1.ldo = ldo
+    assert dg.launch_gather(cfg, p, g1, wm, am) == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    got = wide.float().cpu().numpy()
+    ok, rl2, worst = check_against_oracle(got[:, :n], ref)
+    assert ok, (rl2, worst)
+    assert np.all(got[:, n:] == -7.0)
+
+    # world 2 descriptors over local buffers: every one is refused.
+    lines = torch.zeros((2, m, 2 * n // 4, 2), dtype=torch.int64, device=dev)
+    out2 = torch.zeros((m, 2 * n), dtype=torch.bfloat16, device=dev)
+
+    def desc(**kw):
+        g = tp.lines_descriptor(2, 0, n, out2.data_ptr(), [lines[0].data_ptr(), lines[1].data_ptr()],
+                                sync.data_ptr())
+        for key, v in kw.items():
+            if key == "line1":
+                g.lines[1] = v
+            else:
+                setattr(g, key, v)
+        return g
+    sk = dg.default_config(m, n, k, layout=dg.LAYOUT_PACKED_SWIZZLED, schedule="stream_k")
+    skp = dg.Problem(m, n, k, p.activation, dg.prepack_weight(torch.from_numpy(w).to(dev), sk.block_n, sk.layout),
+                     p.weight_scales, p.activation_scales, None,
+                     torch.zeros(max(sk.plan(m, n, k).ws_floats, 1), device=dev),
+                     torch.zeros(max(sk.plan(m, n, k).sem_ints, 1), dtype=torch.int32, device=dev), status)
+    assert dg.launch_gather(sk, skp, desc(), dg.make_weight_tma(sk, skp), dg.make_activation_tma(sk, skp)) == \
+        dg.CUDA_ERROR_INVALID_VALUE
+    assert dg.launch_gather(cfg, p, desc(line1=lines[1].data_ptr() + 8), wm, am) == dg.CUDA_ERROR_INVALID_VALUE
+    assert dg.launch_gather(cfg, p, desc(output=out2.data_ptr() + 2), wm, am) == dg.CUDA_ERROR_INVALID_VALUE
+    assert dg.launch_gather(cfg, p, desc(ldo=2 * n - 4), wm, am) == dg.CUDA_ERROR_INVALID_VALUE
+    assert dg.launch_gather(cfg, p, desc(sync=0), wm, am) == dg.CUDA_ERROR_INVALID_VALUE
+    n6 = n - 2
+    p6 = dg.Problem(m, n6, k, p.activation, wt, p.weight_scales, p.activation_scales, None, None, None, status)
+    g6 = tp.lines_descriptor(2, 0, n6, out2.data_ptr(), [lines[0].data_ptr(), lines[1].data_ptr()], sync.data_ptr())
+    assert dg.launch_gather(cfg, p6, g6, dg.make_weight_tma(cfg, p6), dg.make_activation_tma(cfg, p6)) == \
+        dg.CUDA_ERROR_INVALID_VALUE
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert not bool(out2.view(torch.int16).any()) and not bool(lines.any()) and not bool(sync.any())
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -71,7 +139,7 @@ def _free_port():
     return port
 
 
-def _rank_main(rank, world, port, m, n, k, result_dir):
+def _rank_main(rank, world, port, m, n, k, result_dir, protocol="flags", steps=2):
     import torch.distributed as dist
     import oracle
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -91,9 +159,9 @@ def _rank_main(rank, world, port, m, n, k, result_dir):
         ws_buf = torch.zeros(max(plan.ws_floats, 1), device=dev)
         sem = torch.zeros(max(plan.sem_ints, 1), dtype=torch.int32, device=dev)
         status = torch.zeros(1, dtype=torch.int32, device=dev)
-        fg = tp.FusedGather(m, n_loc, device=dev)
+        fg = tp.FusedGather(m, n_loc, device=dev, protocol=protocol)
         results = []
-        for step in range(2):
+        for step in range(steps):
             a, as_ = oracle.gen_activation_smoke(m, k, 200 + step)
             act = torch.from_numpy(a).to(dev)
             p = dg.Problem(m, n_loc, k, act, wt, wsc, torch.from_numpy(as_).to(dev), None, ws_buf, sem, status)
@@ -114,15 +182,20 @@ def _rank_main(rank, world, port, m, n, k, result_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("protocol", ["flags", "lines"])
 @pytest.mark.parametrize("m", [1, 8])
-def test_two_gpu_fused_gather_matches_oracle(tmp_path, m):
+def test_two_gpu_fused_gather_matches_oracle(tmp_path, m, protocol):
+    """Four consecutive launches (buffer sets 0, 1, 0, 1; under the lines
+    protocol epochs 1..4, so a set's stale lines from two launches back must
+    not be taken for the current ones)."""
     import torch.multiprocessing as mp
     import oracle
     from helpers import check_against_oracle
-    n, k, world = 2048, 4096, 2
+    n, k, world, steps = 2048, 4096, 2, 4
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, m, n, k, str(tmp_path))) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, m, n, k, str(tmp_path), protocol, steps))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -132,7 +205,7 @@ def test_two_gpu_fused_gather_matches_oracle(tmp_path, m):
             p.kill()
         assert p.exitcode == 0
     w, ws = oracle.gen_weight_smoke(n, k, 91)
-    for step in range(2):
+    for step in range(steps):
         a, as_ = oracle.gen_activation_smoke(m, k, 200 + step)
         ref = oracle.compute_reference(a, as_, w, ws, threads=8)
         for r in range(world):
@@ -141,7 +214,7 @@ def test_two_gpu_fused_gather_matches_oracle(tmp_path, m):
             assert ok, (r, step, rl2, worst)
 
 
-def _serve_main(rank, world, port, m, n, k, group, count, distinct, result_dir):
+def _serve_main(rank, world, port, m, n, k, group, count, distinct, result_dir, protocol="flags"):
     """One rank of the N-GPU serving loop (decode_opt_b200.tp.serving_schedule,
     executed as bench.py executes it, eagerly): request j copies activation
     j % distinct in from pinned host memory, runs the fused GEMM into
@@ -167,7 +240,7 @@ def _serve_main(rank, world, port, m, n, k, group, count, distinct, result_dir):
         sem = torch.zeros(max(plan.sem_ints, 1), dtype=torch.int32, device=dev)
         status = torch.zeros(1, dtype=torch.int32, device=dev)
         nset = 2 * group
-        fg = tp.FusedGather(m, n_loc, buffers=nset, device=dev)
+        fg = tp.FusedGather(m, n_loc, buffers=nset, device=dev, protocol=protocol)
         kb = k // 128
         in_bytes = m * k + m * kb * 4
         hins = []
@@ -217,15 +290,17 @@ def _serve_main(rank, world, port, m, n, k, group, count, distinct, result_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("protocol", ["flags", "lines"])
 @pytest.mark.parametrize("m", [1, 8])
-def test_two_gpu_serving_schedule_matches_oracle(tmp_path, m):
+def test_two_gpu_serving_schedule_matches_oracle(tmp_path, m, protocol):
     import torch.multiprocessing as mp
     import oracle
     from helpers import check_against_oracle
     n, k, world, group, count, distinct = 2048, 4096, 2, 4, 24, 5
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_serve_main, args=(r, world, port, m, n, k, group, count, distinct, str(tmp_path)))
+    procs = [ctx.Process(target=_serve_main, args=(r, world, port, m, n, k, group, count, distinct, str(tmp_path),
+                                                   protocol))
              for r in range(world)]
     for p in procs:
         p.start()
