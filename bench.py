@@ -90,6 +90,9 @@ def parse_args():
     ap.add_argument("--no-sweep", action="store_true", help="skip the M = 1..128 sweep")
     ap.add_argument("--no-cublas", action="store_true", help="skip the cuBLASLt FP8 baseline")
     ap.add_argument("--no-chain", action="store_true", help="skip the 61-layer dependent chain")
+    ap.add_argument("--gather-protocol", choices=["flags", "lines"], default="lines",
+                    help="fused-gather protocol of the N-GPU e2e serving loop (dg_launch_gather with epoch "
+                         "flags, or dg_launch_gather_lines with tagged lines)")
     return ap.parse_args()
 
 
@@ -727,7 +730,7 @@ def b200_arm(args, rank, world, local_rank):
             depth = nset
             cfg_p = default_config(m, n, k, layout=layout, pdl=pdl,
                                       independent_inputs=args.e2e_schedule == "independent")
-            fused_p = dg_tp.FusedGather(m, n, buffers=nset, device=dev)
+            fused_p = dg_tp.FusedGather(m, n, buffers=nset, device=dev, protocol=args.gather_protocol)
             pdesc = [fused_p.descriptor(j) for j in range(nset)]
             slots = []
             for _ in range(nset):
@@ -842,7 +845,8 @@ def b200_arm(args, rank, world, local_rank):
                           "note": "one request at a time on one stream, dependent schedule, CUDA graphs"},
                "schedule": {"block_n": (pipe["cfg"] if pipe is not None else gs_e2e.cfg).block_n,
                             "grid": list(sched.grid), "cluster": sched.cluster,
-                            "pdl_mode": args.e2e_schedule if pipe is not None else "dependent"},
+                            "pdl_mode": args.e2e_schedule if pipe is not None else "dependent",
+                            "gather_protocol": args.gather_protocol if world > 1 and pipe is not None else None},
                "path": "one pinned H2D copy of activation + scales, "
                        + ("dg.launch_gather (GEMM with the fused NVLink all-gather), D2H of the gathered "
                           "bf16 [M, g*N] output" if world > 1 else "dg.launch_with_maps, D2H of the bf16 output")

@@ -98,3 +98,19 @@ def test_gather_descriptor_pointer_table():
         assert g.sync == 0x9000
     with pytest.raises(ValueError):
         tp.gather_descriptor(9, 0, n_loc, bases * 3, flags * 3, 0)
+
+
+def test_lines_descriptor_pointer_table():
+    """The lines protocol's descriptor: this rank's own gathered buffer at
+    column 0, every rank's line buffer base as mapped here (the kernel adds
+    the rank's column offset in lines), row stride g*n_loc, sync passed
+    through; a world above 8 or a rank outside it is refused."""
+    world, n_loc = 8, 896
+    lines = [0x20000000 * (q + 1) for q in range(world)]
+    for rank in range(world):
+        g = tp.lines_descriptor(world, rank, n_loc, 0x5000, lines, 0x9000)
+        assert (g.world, g.rank, g.ldo, g.output, g.sync) == (world, rank, world * n_loc, 0x5000, 0x9000)
+        assert [g.lines[q] for q in range(world)] == lines
+    for bad in ((9, 0), (2, 2), (2, -1)):
+        with pytest.raises(ValueError):
+            tp.lines_descriptor(bad[0], bad[1], n_loc, 0x5000, lines + lines, 0x9000)
