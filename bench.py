@@ -641,12 +641,20 @@ def b200_arm(args, rank, world, local_rank):
         gs_e2e = GemmSetup(rotation(gs_dep.cfg.block_n), gs_dep.cfg, m, act_in, wscale, sc_in, dev)
         hy = torch.empty((m, world * n), dtype=torch.bfloat16).pin_memory()
 
+        fused_e = None
+        if world > 1:
+            fused_e = dg_tp.FusedGather(m, n, device=dev, protocol=args.gather_protocol)
+            edesc = [fused_e.descriptor(0), fused_e.descriptor(1)]
+
         def e2e_step(i):
             dev_in.copy_(hin, non_blocking=True)
             if world > 1:
-                fused_step(i, gs_e2e)
-                fused.wait(i % 2, stream=stream, status=gs_e2e.status)
-                hy.copy_(fused.output(i % 2, m), non_blocking=True)
+                rc = dg.launch_gather(gs_e2e.cfg, gs_e2e.probs[i % gs_e2e.nsets], edesc[i % 2],
+                                      gs_e2e.wmaps[i % gs_e2e.nsets], gs_e2e.amap, stream, pdl_attr=gs_e2e.cfg.pdl)
+                if rc != 0:
+                    raise RuntimeError(f"fused launch failed: cudaError {rc}")
+                fused_e.wait(i % 2, stream=stream, status=gs_e2e.status)
+                hy.copy_(fused_e.output(i % 2, m), non_blocking=True)
             else:
                 gs_e2e.launch(i, stream)
                 hy.copy_(gs_e2e.out, non_blocking=True)
@@ -860,6 +868,8 @@ def b200_arm(args, rank, world, local_rank):
     if fused is not None:
         torch.cuda.synchronize(dev)
         fused.close()
+    if e2e is not None and world > 1 and fused_e is not None:
+        fused_e.close()
 
     # ---- M sweep (M in 1..128), one GPU, headline mode ----
     sweep = None
