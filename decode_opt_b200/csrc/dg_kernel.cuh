@@ -721,7 +721,7 @@ __device__ __noinline__ void reduce_split_tiles(const KernelParams& p, const int
 // Fused gather in lines (kFlagGatherLines).  The tag of this launch: the
 // epoch of the last launch completed on this rank + 1.  Read only after
 // griddepcontrol.wait (the last CTA of the previous launch stored it), and
-// only before this CTA counts itself done in gather_lines_complete.
+// only before this CTA counts itself done in gather_lines_count.
 __device__ __forceinline__ uint32_t gather_lines_epoch(const KernelParams& p) {
   return static_cast<uint32_t>(sm100::load_relaxed_gpu(p.sync_ctr + 1)) + 1u;
 }
@@ -1024,8 +1024,9 @@ __device__ __noinline__ inline void gather_complete(const KernelParams& p, bool 
   fence_acq_rel_sys();
 }
 
-// Completion of the fused gather in lines, run by every thread of every CTA
-// after the CTA's own line stores.  Each output element travels as half of
+// Completion of the fused gather in lines, run after the CTA's own line
+// stores by its epilogue threads (`tid` of `nthreads`; the control warps may
+// hold a reduced register budget and only join the barrier).  Each output element travels as half of
 // an 8-byte word {2 bf16, epoch} that the writing rank stored into every
 // rank's line buffer; a word is single-copy atomic, so seeing this launch's
 // epoch in it means its payload has landed -- no fence or flag round trip.
@@ -1036,7 +1037,7 @@ __device__ __noinline__ inline void gather_complete(const KernelParams& p, bool 
 // gathered output is whole, which also keeps every rank within one launch of
 // the others (the two alternating line-buffer sets rely on it).  The last CTA
 // to finish stores the epoch for the next launch.
-__device__ __noinline__ inline void gather_lines_complete(const KernelParams& p, long long cta) {
+__device__ __noinline__ inline void gather_lines_poll(const KernelParams& p, long long cta, int tid, int nthreads) {
   using namespace sm100;
   griddep_wait();
   const uint32_t epoch = gather_lines_epoch(p);
@@ -1045,7 +1046,7 @@ __device__ __noinline__ inline void gather_lines_complete(const KernelParams& p,
   const long long hi = (cta + 1) * total / p.num_ctas;
   const uint4* mine = p.lines[p.rank];
   const uint64_t start = global_timer_ns();
-  for (long long i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+  for (long long i = lo + tid; i < hi; i += nthreads) {
     uint64_t w0 = 0, w1 = 0;
     bool ok = true;
     for (;;) {
@@ -1067,13 +1068,18 @@ __device__ __noinline__ inline void gather_lines_complete(const KernelParams& p,
     v.y = static_cast<uint32_t>(w1);
     *reinterpret_cast<uint2*>(p.output + static_cast<size_t>(m) * p.ldo + col) = v;
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int done = atomic_add_acq_rel_gpu(p.sync_ctr, 1);
-    if (done == p.num_ctas - 1) {
-      store_relaxed_gpu(p.sync_ctr, 0);
-      store_relaxed_gpu(p.sync_ctr + 1, static_cast<int>(epoch));
-    }
+}
+
+// After every thread of the CTA is past its polling (a CTA barrier), one
+// thread counts the CTA done; the last CTA of the grid resets the count and
+// stores this launch's epoch for the next one.
+__device__ __noinline__ inline void gather_lines_count(const KernelParams& p) {
+  using namespace sm100;
+  const uint32_t epoch = gather_lines_epoch(p);
+  const int done = atomic_add_acq_rel_gpu(p.sync_ctr, 1);
+  if (done == p.num_ctas - 1) {
+    store_relaxed_gpu(p.sync_ctr, 0);
+    store_relaxed_gpu(p.sync_ctr + 1, static_cast<int>(epoch));
   }
 }
 
@@ -1563,10 +1569,14 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   __syncthreads();
   tc_fence_after();
   if (warp == Tr::kMmaWarp) tmem_dealloc(tmem_base, Tr::kTmemCols);
-  if (p.world > 1 && (p.flags & kFlagGatherLines))
-    gather_lines_complete(p, cta);
-  else if (p.world > 1 && threadIdx.x == 0)
+  if (p.world > 1 && (p.flags & kFlagGatherLines)) {
+    if (warp < static_cast<uint32_t>(Tr::kEpiWarps))
+      gather_lines_poll(p, cta, static_cast<int>(threadIdx.x), Tr::kEpiWarps * 32);
+    __syncthreads();
+    if (threadIdx.x == 0) gather_lines_count(p);
+  } else if (p.world > 1 && threadIdx.x == 0) {
     gather_complete(p, *wrote_output != 0);
+  }
 }
 
 template <int MMA_M, int COPIES, int EPW>
