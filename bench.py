@@ -294,7 +294,9 @@ class Rotation:
 class GemmSetup:
     """Problems, maps and buffers for one (rotation, M, config)."""
 
-    def __init__(self, rot, cfg, m, qx, wscale, ascale, dev):
+    def __init__(self, rot, cfg, m, qx, wscale, ascale, dev, host_out=None):
+        """host_out: a pinned host [m, n] bf16 tensor the kernel writes its
+        output into directly (zero-copy, dg.host_device_pointer)."""
         import torch
         import decode_opt_b200 as dg
         self.cfg = cfg
@@ -302,11 +304,16 @@ class GemmSetup:
         self.plan = cfg.plan(m, rot.n, rot.k)
         if self.plan.error:
             raise SystemExit(self.plan.error)
-        self.out = torch.empty((m, rot.n), dtype=torch.bfloat16, device=dev)
+        if host_out is None:
+            self.out = torch.empty((m, rot.n), dtype=torch.bfloat16, device=dev)
+            out_arg = self.out
+        else:
+            self.out = host_out
+            out_arg = dg.host_device_pointer(host_out)
         self.ws = torch.zeros(max(self.plan.ws_floats, 1), dtype=torch.float32, device=dev)
         self.sem = torch.zeros(max(self.plan.sem_ints, 1), dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.probs = [dg.Problem(m, rot.n, rot.k, qx, w, wscale, ascale, self.out, self.ws, self.sem, self.status)
+        self.probs = [dg.Problem(m, rot.n, rot.k, qx, w, wscale, ascale, out_arg, self.ws, self.sem, self.status)
                       for w in rot.sets]
         self.wmaps = [dg.make_weight_tma(cfg, p) for p in self.probs]
         self.amap = dg.make_activation_tma(cfg, self.probs[0])
@@ -659,17 +666,29 @@ def b200_arm(args, rank, world, local_rank):
                 gs_e2e.launch(i, stream)
                 hy.copy_(gs_e2e.out, non_blocking=True)
 
-        def timed_serial(steps):
+        def timed_serial(steps, step_fn=e2e_step):
             """One request at a time on one stream (H2D, GEMM -- with the fused
             gather on N GPUs -- D2H), captured in CUDA graphs."""
             with torch.cuda.stream(stream):
                 for i in range(4):
-                    e2e_step(i)
+                    step_fn(i)
             torch.cuda.synchronize(dev)
-            graphs = capture(lambda i: e2e_step(i + 4), steps)
+            graphs = capture(lambda i: step_fn(i + 4), steps)
             t = timed(graphs)
             del graphs
             return t
+
+        # Zero-copy output (one GPU): the GEMM writes its bf16 result straight
+        # into pinned host memory over PCIe (dg.host_device_pointer), so the
+        # step is the H2D copy and the launch; the result's bytes still cross
+        # PCIe every step, as kernel stores instead of a copy node.
+        hy_zc = torch.empty((m, n), dtype=torch.bfloat16).pin_memory() if world == 1 else None
+        gs_zc = (GemmSetup(rotation(gs_dep.cfg.block_n), gs_dep.cfg, m, act_in, wscale, sc_in, dev, host_out=hy_zc)
+                 if world == 1 else None)
+
+        def e2e_step_zc(i):
+            dev_in.copy_(hin, non_blocking=True)
+            gs_zc.launch(i, stream)
 
         pipe = None
         if world == 1:
@@ -681,44 +700,52 @@ def b200_arm(args, rank, world, local_rank):
             depth = max(1, args.e2e_depth)
             cfg_p = default_config(m, n, k, layout=layout, pdl=pdl,
                                       independent_inputs=args.e2e_schedule == "independent")
-            slots = []
-            for _ in range(depth):
-                d_in = torch.empty(in_bytes, dtype=torch.uint8, device=dev)
-                g_p = GemmSetup(rotation(cfg_p.block_n), cfg_p, m, d_in[: m * k].view(m, k), wscale,
-                                d_in[m * k:].view(torch.float32).view(m, kb), dev)
-                slots.append((d_in, g_p, torch.empty((m, n), dtype=torch.bfloat16).pin_memory(),
-                              torch.cuda.Stream(device=dev)))
 
-            def pipe_step(i):
-                d_in, g_p, h_out, st = slots[i % depth]
-                with torch.cuda.stream(st):
-                    d_in.copy_(hin, non_blocking=True)
-                    g_p.launch(i, st)
-                    h_out.copy_(g_p.out, non_blocking=True)
+            def run_pipe(zero_copy):
+                slots = []
+                for _ in range(depth):
+                    d_in = torch.empty(in_bytes, dtype=torch.uint8, device=dev)
+                    h_out = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+                    g_p = GemmSetup(rotation(cfg_p.block_n), cfg_p, m, d_in[: m * k].view(m, k), wscale,
+                                    d_in[m * k:].view(torch.float32).view(m, kb), dev,
+                                    host_out=h_out if zero_copy else None)
+                    slots.append((d_in, g_p, h_out, torch.cuda.Stream(device=dev)))
 
-            for i in range(3 * depth):
-                pipe_step(i)
-            torch.cuda.synchronize(dev)
-            # The loop is captured in CUDA graphs (graph_chunk requests each,
-            # forked to the slot streams and joined back), as a decode server
-            # replays its step: the copy nodes still move every request's
-            # bytes over PCIe at replay time, but no Python runs per request.
-            graphs = []
-            with torch.cuda.stream(stream):
-                for base in range(0, K, args.graph_chunk):
-                    gr = torch.cuda.CUDAGraph()
-                    with torch.cuda.graph(gr, stream=stream):
-                        for _, _, _, st in slots:
-                            st.wait_stream(stream)
-                        for i in range(base, min(K, base + args.graph_chunk)):
-                            pipe_step(i)
-                        for _, _, _, st in slots:
-                            stream.wait_stream(st)
-                    graphs.append(gr)
-            t_pipe = timed(graphs)
-            del graphs
-            pipe = {"t": t_pipe, "depth": depth, "cfg": cfg_p,
-                    "plan": slots[0][1].plan, "outs": [sl[2] for sl in slots], "setups": [sl[1] for sl in slots]}
+                def pipe_step(i):
+                    d_in, g_p, h_out, st = slots[i % depth]
+                    with torch.cuda.stream(st):
+                        d_in.copy_(hin, non_blocking=True)
+                        g_p.launch(i, st)
+                        if not zero_copy:
+                            h_out.copy_(g_p.out, non_blocking=True)
+
+                for i in range(3 * depth):
+                    pipe_step(i)
+                torch.cuda.synchronize(dev)
+                # The loop is captured in CUDA graphs (graph_chunk requests each,
+                # forked to the slot streams and joined back), as a decode server
+                # replays its step: the copy nodes still move every request's
+                # bytes over PCIe at replay time, but no Python runs per request.
+                graphs = []
+                with torch.cuda.stream(stream):
+                    for base in range(0, K, args.graph_chunk):
+                        gr = torch.cuda.CUDAGraph()
+                        with torch.cuda.graph(gr, stream=stream):
+                            for _, _, _, st in slots:
+                                st.wait_stream(stream)
+                            for i in range(base, min(K, base + args.graph_chunk)):
+                                pipe_step(i)
+                            for _, _, _, st in slots:
+                                stream.wait_stream(st)
+                        graphs.append(gr)
+                t_pipe = timed(graphs)
+                del graphs
+                return {"t": t_pipe, "depth": depth, "cfg": cfg_p, "zero_copy": zero_copy,
+                        "plan": slots[0][1].plan, "outs": [sl[2] for sl in slots], "setups": [sl[1] for sl in slots]}
+
+            pipe_copy = run_pipe(False)
+            pipe_zc = run_pipe(True)
+            pipe = pipe_zc if pipe_zc["t"] < pipe_copy["t"] else pipe_copy
         elif args.e2e_group > 1:
             # Requests pipelined on N GPUs, in groups of `grp`
             # (decode_opt_b200.tp.serving_schedule: which operation waits on
@@ -799,6 +826,7 @@ def b200_arm(args, rank, world, local_rank):
                     "outs": h_outs, "setups": [sl[1] for sl in slots], "fused": fused_p}
 
         te_serial = timed_serial(K)
+        te_serial_zc = timed_serial(K, e2e_step_zc) if world == 1 else None
         gs.check_status()
         gs_e2e.check_status()
         # Output checks.  The serial path runs the dependent schedule and the
@@ -814,18 +842,21 @@ def b200_arm(args, rank, world, local_rank):
             with torch.cuda.stream(stream):
                 gs_dep.launch(0, stream)
             torch.cuda.synchronize(dev)
-            e2e_check["serial_bit_exact"] = bool(torch.equal(hy.view(torch.int16), gs_dep.out.cpu().view(torch.int16)))
+            want_s = gs_dep.out.cpu().view(torch.int16)
+            e2e_check["serial_bit_exact"] = bool(torch.equal(hy.view(torch.int16), want_s))
+            gs_zc.check_status()
+            e2e_check["serial_zero_copy_bit_exact"] = bool(torch.equal(hy_zc.view(torch.int16), want_s))
             if pipe is not None:
-                g0 = pipe["setups"][0]
+                g0 = pipe_copy["setups"][0]
                 g0.out.zero_()
                 with torch.cuda.stream(stream):
                     g0.launch(0, stream)
                 torch.cuda.synchronize(dev)
                 want_p = g0.out.cpu().view(torch.int16)
-                for g_p in pipe["setups"]:
+                for g_p in pipe_copy["setups"] + pipe_zc["setups"]:
                     g_p.check_status()
                 e2e_check["pipelined_bit_exact"] = all(bool(torch.equal(h.view(torch.int16), want_p))
-                                                       for h in pipe["outs"])
+                                                       for h in pipe_copy["outs"] + pipe_zc["outs"])
         elif pipe is not None:
             for g_p in pipe["setups"]:
                 g_p.check_status()
@@ -850,14 +881,26 @@ def b200_arm(args, rank, world, local_rank):
                "us_per_step": te / K * 1e6,
                "requests_in_flight": pipe["depth"] if pipe is not None else 1,
                "serial": {"us_per_step": te_serial / K * 1e6,
-                          "note": "one request at a time on one stream, dependent schedule, CUDA graphs"},
+                          "zero_copy_us_per_step": te_serial_zc / K * 1e6 if te_serial_zc is not None else None,
+                          "note": "one request at a time on one stream, dependent schedule, CUDA graphs"
+                                  + ("; zero_copy: the kernel writes the bf16 result into pinned host memory, "
+                                     "no D2H copy node" if te_serial_zc is not None else "")},
+               "output_to_host": ("zero-copy: the GEMM stores the bf16 result straight into pinned host "
+                                  "memory over PCIe (dg.host_device_pointer), no D2H copy node; the result's "
+                                  "bytes still cross PCIe every step"
+                                  if pipe is not None and pipe.get("zero_copy") else "a D2H copy every step"),
+               "variants_us_per_step": ({"d2h_copy": pipe_copy["t"] / K * 1e6, "zero_copy": pipe_zc["t"] / K * 1e6}
+                                        if world == 1 and pipe is not None else None),
                "schedule": {"block_n": (pipe["cfg"] if pipe is not None else gs_e2e.cfg).block_n,
                             "grid": list(sched.grid), "cluster": sched.cluster,
                             "pdl_mode": args.e2e_schedule if pipe is not None else "dependent",
                             "gather_protocol": args.gather_protocol if world > 1 and pipe is not None else None},
                "path": "one pinned H2D copy of activation + scales, "
                        + ("dg.launch_gather (GEMM with the fused NVLink all-gather), D2H of the gathered "
-                          "bf16 [M, g*N] output" if world > 1 else "dg.launch_with_maps, D2H of the bf16 output")
+                          "bf16 [M, g*N] output" if world > 1 else
+                          "dg.launch_with_maps, the bf16 output to pinned host memory "
+                          + ("written by the kernel (zero-copy)" if pipe is not None and pipe.get("zero_copy")
+                             else "by a D2H copy"))
                        + ", every step" + ("" if pipe is None else
                                            f"; {pipe['depth']} requests in flight on as many streams" if world == 1 else
                                            "; pipelined: the fused GEMMs on one stream in the same order on every "

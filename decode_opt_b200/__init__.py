@@ -609,6 +609,20 @@ def quantize_activation(x, out=None, scales=None, stream=None, pdl_attr: bool = 
     return out, scales
 
 
+def host_device_pointer(t) -> int:
+    """Device address of a pinned host tensor (``tensor.pin_memory()``), for a
+    zero-copy output: a GEMM given it as its output writes the result
+    straight into host memory (``dg_host_device_pointer``).  Raises for
+    memory that is not mapped pinned memory."""
+    if not t.is_pinned():
+        raise ValueError("host_device_pointer needs a pinned host tensor")
+    out = ctypes.c_void_p()
+    rc = _lib.lib().dg_host_device_pointer(ctypes.c_void_p(t.data_ptr()), ctypes.byref(out))
+    if rc != 0 or out.value is None:
+        raise RuntimeError(f"dg_host_device_pointer failed: cudaError {rc}")
+    return int(out.value)
+
+
 def launch(cfg, p: Problem, stream=None) -> int:
     """Encode both tensor maps, then launch (reference ``launch<Cfg>``)."""
     if isinstance(cfg, KernelConfig):

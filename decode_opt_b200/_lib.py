@@ -13,7 +13,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libdecode_gemm_b200.so")
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 LAYOUT_RAW = 0
 LAYOUT_PACKED = 1
@@ -36,6 +36,7 @@ EXPORTED_SYMBOLS = (
     "dg_probe_naive_read", "dg_num_sms", "dg_launch_static_scratch", "dg_probe_mma",
     "dg_launch_gather", "dg_gather_wait", "dg_ipc_export", "dg_ipc_import", "dg_ipc_release",
     "dg_quantize_act", "dg_max_active_clusters", "dg_launch_quantized", "dg_launch_gather_lines",
+    "dg_host_device_pointer",
 )
 
 
@@ -170,6 +171,7 @@ def lib():
                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
     L.dg_launch_gather_lines.argtypes = [cfgp, probp, ctypes.POINTER(DgGatherLines), ctypes.c_void_p,
                                          ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+    L.dg_host_device_pointer.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
     L.dg_gather_wait.argtypes = [ctypes.POINTER(DgGather), ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_void_p]
     L.dg_ipc_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_ulonglong)]
     L.dg_ipc_import.argtypes = [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_void_p)]

@@ -629,6 +629,18 @@ const char* dg_status_string(int code) {
   }
 }
 
+int dg_host_device_pointer(void* host, void** device) {
+  if (host == nullptr || device == nullptr) return cudaErrorInvalidValue;
+  void* d = nullptr;
+  const cudaError_t err = cudaHostGetDevicePointer(&d, host, 0);
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();   // not a sticky error: clear it for the caller's next call
+    return err;
+  }
+  *device = d;
+  return cudaSuccess;
+}
+
 int dg_flush_l2(void* buf, unsigned long long bytes, void* stream) {
   if (buf == nullptr || bytes < 16) return cudaErrorInvalidValue;
   int sms = current_sm_count();

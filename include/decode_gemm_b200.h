@@ -45,6 +45,7 @@
  *   dg_gather_wait          (new) completion wait for the fused gather
  *   dg_ipc_export / dg_ipc_import / dg_ipc_release  (new) peer buffers for it
  *   dg_num_sms              (new) SM count of the current device
+ *   dg_host_device_pointer  (new) device address of pinned host memory (zero-copy output)
  *   dg_probe_mma            (new) tcgen05.mma issue / completion cost per shape
  */
 #ifndef DECODE_GEMM_B200_H_
@@ -56,7 +57,7 @@
 extern "C" {
 #endif
 
-#define DG_ABI_VERSION 6
+#define DG_ABI_VERSION 7
 
 /* Weight layouts. */
 #define DG_LAYOUT_RAW 0             /* W[N,K], K contiguous (checkpoint layout) */
@@ -326,6 +327,15 @@ int dg_probe_bulk_stream(const void* buf, unsigned long long bytes, unsigned op_
 int dg_probe_naive_read(const void* buf, unsigned long long bytes, int blocks_per_sm,
                         unsigned long long* sink, void* stream);
 int dg_num_sms(void);
+
+/* (new) Device address of pinned, mapped host memory (cudaHostAlloc /
+   cudaMallocHost, or cudaHostRegister with the mapped flag).  Passed as
+   dg_problem.output (or dg_gather_lines.output) it makes the kernel write
+   the bf16 result straight into host memory over PCIe: no device buffer and
+   no separate device-to-host copy; the data is in host memory once the
+   launch has completed.  Returns a cudaError_t value (an error, and *device
+   untouched, for memory that is not mapped pinned memory). */
+int dg_host_device_pointer(void* host, void** device);
 
 /* tcgen05.mma cost probe: in each of `ctas` CTAs (at most one per SM)
    `issuers` warps (1..4) issue iters / issuers kind::f8f6f4 MMAs each, of
