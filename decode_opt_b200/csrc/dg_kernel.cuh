@@ -784,8 +784,8 @@ __device__ __forceinline__ void cluster_reduce_tile(const KernelParams& p, uint3
       const uint64_t w0 = (static_cast<uint64_t>(epoch) << 32) | *reinterpret_cast<const uint32_t*>(&lo2);
       const uint64_t w1 = (static_cast<uint64_t>(epoch) << 32) | *reinterpret_cast<const uint32_t*>(&hi2);
       for (int i = 1; i <= p.world; ++i) {            // peers first, this rank last
-        const int r = (p.rank + i) % p.world;
-        st_volatile_line(p.lines[r] + line, w0, w1);
+        const int dst = (p.rank + i) % p.world;
+        st_volatile_line(p.lines[dst] + line, w0, w1);
       }
       continue;
     }
@@ -1026,10 +1026,11 @@ __device__ __noinline__ inline void gather_complete(const KernelParams& p, bool 
 
 // Completion of the fused gather in lines, run after the CTA's own line
 // stores by its epilogue threads (`tid` of `nthreads`; the control warps may
-// hold a reduced register budget and only join the barrier).  Each output element travels as half of
-// an 8-byte word {2 bf16, epoch} that the writing rank stored into every
-// rank's line buffer; a word is single-copy atomic, so seeing this launch's
-// epoch in it means its payload has landed -- no fence or flag round trip.
+// hold a reduced register budget and only join the barrier).  Each output
+// element travels as half of an 8-byte word {2 bf16, epoch} that the writing
+// rank stored into every rank's line buffer; a word is single-copy atomic, so
+// seeing this launch's epoch in it means its payload has landed -- no fence
+// or flag round trip.
 // CTA c polls lines [c*L/G, (c+1)*L/G) of this rank's buffer (L = M *
 // lines_per_row) until both words of each carry the epoch (bounded by
 // p.timeout_ns, status kErrGatherWait otherwise) and unpacks them into the
