@@ -445,6 +445,11 @@ def b200_arm(args, rank, world, local_rank):
         dist.all_gather_into_tensor(gathered, gs_dep.out, group=pg)
 
     K = args.steps
+    # Fused-gather sections alternate two buffer sets per launch; an even
+    # launch count keeps the alternation across graph replays (a replay
+    # restarting on the set the previous one ended on would hand a peer a set
+    # this rank may still be reading).
+    K2 = K + K % 2
     # ---- warm-up: eager launches, then every graph once (in timed()) ------------
     with torch.cuda.stream(stream):
         for i in range(max(args.warmup, 3)):
@@ -506,9 +511,9 @@ def b200_arm(args, rank, world, local_rank):
                 raise RuntimeError(f"fused launch failed: cudaError {rc}")
         def fused_steps(i):
             fused_step(i)
-            if i == K - 1:      # the last launch's gather completes inside the timed region
-                fused.wait((K - 1) % 2, stream=stream, status=gs.status)
-        graphs = capture(fused_steps, K)
+            if i == K2 - 1:      # the last launch's gather completes inside the timed region
+                fused.wait((K2 - 1) % 2, stream=stream, status=gs.status)
+        graphs = capture(fused_steps, K2)
         t_fused = timed(graphs)
         del graphs
         gs.check_status()
@@ -521,13 +526,13 @@ def b200_arm(args, rank, world, local_rank):
                                   stream, pdl_attr=gs.cfg.pdl)
             if rc != 0:
                 raise RuntimeError(f"fused launch (lines) failed: cudaError {rc}")
-        graphs = capture(lines_steps, K)
+        graphs = capture(lines_steps, K2)
         t_fused_l = timed(graphs)
         del graphs
         gs.check_status()
         # Both protocols gathered the same product of the same inputs.
-        lines_match = bool(torch.equal(fused_l.output((K - 1) % 2, m).view(torch.int16),
-                                       fused.output((K - 1) % 2, m).view(torch.int16)))
+        lines_match = bool(torch.equal(fused_l.output((K2 - 1) % 2, m).view(torch.int16),
+                                       fused.output((K2 - 1) % 2, m).view(torch.int16)))
         fused_l.close()
         # Strong scaling: the one n x k layer N-sharded over
         # the ranks, each streaming n/world rows, then the gather -- at the
@@ -577,9 +582,9 @@ def b200_arm(args, rank, world, local_rank):
 
                 def strong_fused_steps(i):
                     strong_fused(i)
-                    if i == K - 1:
-                        fused_s.wait((K - 1) % 2, stream=stream, status=gs_s.status)
-                graphs = capture(strong_fused_steps, K)
+                    if i == K2 - 1:
+                        fused_s.wait((K2 - 1) % 2, stream=stream, status=gs_s.status)
+                graphs = capture(strong_fused_steps, K2)
                 t_s_fused = timed(graphs)
                 del graphs
                 fused_sl = dg_tp.FusedGather(mm, n_s, device=dev, protocol="lines")
@@ -590,11 +595,11 @@ def b200_arm(args, rank, world, local_rank):
                                           gs_s.wmaps[i % gs_s.nsets], gs_s.amap, stream, pdl_attr=gs_s.cfg.pdl)
                     if rc != 0:
                         raise RuntimeError(f"fused launch (lines) failed: cudaError {rc}")
-                graphs = capture(strong_lines, K)
+                graphs = capture(strong_lines, K2)
                 t_s_lines = timed(graphs)
                 del graphs
-                same_s = bool(torch.equal(fused_sl.output((K - 1) % 2, mm).view(torch.int16),
-                                          fused_s.output((K - 1) % 2, mm).view(torch.int16)))
+                same_s = bool(torch.equal(fused_sl.output((K2 - 1) % 2, mm).view(torch.int16),
+                                          fused_s.output((K2 - 1) % 2, mm).view(torch.int16)))
                 fused_sl.close()
                 fused_s.close()
                 gs_s.check_status()
@@ -603,10 +608,10 @@ def b200_arm(args, rank, world, local_rank):
                         "gemm_only": {"us_per_gemm": t_s / K * 1e6, "GBps_job": byt_layer / (t_s / K) / 1e9},
                         "with_gather": {"us_per_step": t_s_tp / K * 1e6,
                                         "GBps_job": byt_layer / (t_s_tp / K) / 1e9},
-                        "with_fused_gather": {"us_per_step": t_s_fused / K * 1e6,
-                                              "GBps_job": byt_layer / (t_s_fused / K) / 1e9},
-                        "with_fused_gather_lines": {"us_per_step": t_s_lines / K * 1e6,
-                                                    "GBps_job": byt_layer / (t_s_lines / K) / 1e9,
+                        "with_fused_gather": {"us_per_step": t_s_fused / K2 * 1e6,
+                                              "GBps_job": byt_layer / (t_s_fused / K2) / 1e9},
+                        "with_fused_gather_lines": {"us_per_step": t_s_lines / K2 * 1e6,
+                                                    "GBps_job": byt_layer / (t_s_lines / K2) / 1e9,
                                                     "output_equals_flags_protocol": same_s}}
 
             strong = strong_for(m, qx, ascale)
@@ -620,11 +625,11 @@ def b200_arm(args, rank, world, local_rank):
             del rot_cache
         tp = {"with_gather": {"us_per_step": t_tp / K * 1e6, "GBps_job": byt_job / (t_tp / K) / 1e9,
                               "collective": "NCCL all_gather_into_tensor of the bf16 [M, N/g] slices"},
-              "with_fused_gather": {"us_per_step": t_fused / K * 1e6, "GBps_job": byt_job / (t_fused / K) / 1e9,
+              "with_fused_gather": {"us_per_step": t_fused / K2 * 1e6, "GBps_job": byt_job / (t_fused / K2) / 1e9,
                                     "collective": "none: the GEMM stores its slices into every rank's "
                                                   "gathered [M, g*N] buffer over NVLink (dg_launch_gather)"},
-              "with_fused_gather_lines": {"us_per_step": t_fused_l / K * 1e6,
-                                          "GBps_job": byt_job / (t_fused_l / K) / 1e9,
+              "with_fused_gather_lines": {"us_per_step": t_fused_l / K2 * 1e6,
+                                          "GBps_job": byt_job / (t_fused_l / K2) / 1e9,
                                           "output_equals_flags_protocol": lines_match,
                                           "collective": "none: the GEMM stores its slices as tagged 16-byte lines "
                                                         "{2 bf16, epoch} x 2 into every rank's line buffer over "
@@ -825,7 +830,8 @@ def b200_arm(args, rank, world, local_rank):
             pipe = {"t": t_pipe, "depth": depth, "cfg": cfg_p, "plan": slots[0][1].plan,
                     "outs": h_outs, "setups": [sl[1] for sl in slots], "fused": fused_p}
 
-        te_serial = timed_serial(K)
+        K_ser = K2 if world > 1 else K          # two gather sets alternate on N GPUs
+        te_serial = timed_serial(K_ser) * K / K_ser
         te_serial_zc = timed_serial(K, e2e_step_zc) if world == 1 else None
         gs.check_status()
         gs_e2e.check_status()
@@ -1034,6 +1040,103 @@ def b200_arm(args, rank, world, local_rank):
                               "and 1x128 scales either in the GEMM's cluster reduction (fused, dg.launch_quantized: "
                               "one kernel, 256-row tiles) or by the GPU quantiser as a second PDL launch (separate)")
 
+    # ---- the 61-layer decode chain on N GPUs (tensor parallel, strong scaling):
+    # the same layers as chain_61, each full matrix N-sharded over the ranks;
+    # every layer is the fused GEMM + gather in tagged lines
+    # (dg_launch_gather_lines, dependent mode, PDL) followed by the GPU
+    # quantiser of the gathered [M, N] output into the next layer's activation
+    # on every rank.  Each shape has its own gather (two line-buffer sets
+    # alternating per use), every rank makes the same launches in the same
+    # order.  Rank 0 checks the last layer's gathered output against the
+    # oracle in the CPU leg below.
+    chain_tp = None
+    chain_tp_last = None
+    if not args.no_chain and world > 1 and n % (world * 128) == 0 and k % (world * 128) == 0:
+        from decode_opt_b200 import tp as dg_tp
+        layers = 61
+        passes = max(3, min(20, K // 500))
+        dn = (n, k)
+        up = (k, n)
+        shapes = [dn if li % 2 == 0 else up for li in range(layers)]
+        base = {}
+        for (nn, kk) in (dn, up):
+            gw = torch.Generator(device=dev).manual_seed(1000 + nn)      # the same full matrix on every rank
+            wq, ws_ = quantize_pertensor(torch.randn((nn, kk), device=dev, generator=gw), torch.float8_e4m3fn)
+            n_loc = nn // world
+            lo = rank * n_loc
+            sc_full = torch.full(((nn + 127) // 128, kk // 128), float(ws_) / math.sqrt(kk), device=dev)
+            cfg_l = default_config(m, n_loc, kk, layout=layout, pdl=pdl, independent_inputs=False)
+            w_loc = wq[lo:lo + n_loc].contiguous()
+            fg = dg_tp.FusedGather(m, n_loc, device=dev, protocol="lines")
+            base[(nn, kk)] = {"w": w_loc if layout == dg.LAYOUT_RAW else dg.prepack_weight(w_loc, cfg_l.block_n,
+                                                                                           layout),
+                              "sc": sc_full[lo // 128:(lo + n_loc) // 128].contiguous(), "cfg": cfg_l, "fg": fg,
+                              "desc": [fg.descriptor(0), fg.descriptor(1)], "n_loc": n_loc,
+                              "w_full": wq if rank == 0 else None, "sc_full": sc_full}
+        weights = [base[sh]["w"].clone() for sh in shapes]
+        act_in = {w_: torch.zeros((m, w_), dtype=torch.uint8, device=dev) for w_ in (k, n)}
+        act_sc = {w_: torch.zeros((m, w_ // 128), device=dev) for w_ in (k, n)}
+        q0, s0 = dg.quantize_activation(torch.randn((m, k), device=dev, generator=gx).bfloat16())
+        act_in[k].copy_(q0)
+        act_sc[k].copy_(s0)
+        st_t = torch.zeros(1, dtype=torch.int32, device=dev)
+        steps_t = []
+        for li, (nn, kk) in enumerate(shapes):
+            b = base[(nn, kk)]
+            pr = dg.Problem(m, b["n_loc"], kk, act_in[kk], weights[li], b["sc"], act_sc[kk], None, None, None, st_t)
+            steps_t.append((b, pr, dg.make_weight_tma(b["cfg"], pr), dg.make_activation_tma(b["cfg"], pr), nn))
+        uses = {dn: 0, up: 0}
+        last_set = {}
+
+        def chain_tp_step(i):
+            b, pr, wm_, am_, nn = steps_t[i % layers]
+            sh = shapes[i % layers]
+            j = uses[sh] % 2          # this gather's buffer set: alternates per use
+            uses[sh] += 1
+            last_set[sh] = j
+            rc = dg.launch_gather(b["cfg"], pr, b["desc"][j], wm_, am_, stream, pdl_attr=b["cfg"].pdl)
+            if rc != 0:
+                raise RuntimeError(f"tensor-parallel chain launch failed: cudaError {rc}")
+            dg.quantize_activation(b["fg"].output(j, m), out=act_in[nn], scales=act_sc[nn], stream=stream,
+                                   pdl_attr=True)
+        # A gather's two sets must alternate on every use, also across graph
+        # replays: an even number of passes and graphs of whole pairs of
+        # passes give every gather an even number of uses per graph (each
+        # graph starts on set 0 and ends on set 1).
+        passes_t = passes + passes % 2
+        graphs = []
+        with torch.cuda.stream(stream):
+            for base_i in range(0, layers * passes_t, 8 * layers):
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=stream):
+                    for i in range(base_i, min(layers * passes_t, base_i + 8 * layers)):
+                        chain_tp_step(i)
+                graphs.append(gr)
+        assert all(u % 2 == 0 for u in uses.values())
+        t_ct = timed(graphs)
+        del graphs
+        if int(st_t.item()) != 0:
+            raise RuntimeError(f"tensor-parallel chain status {dg.status_string(int(st_t.item()))}")
+        per_layer_t = t_ct / (layers * passes_t)
+        bytes_layer_t = sum(nn * kk + m * kk + 2 * m * nn for (nn, kk) in shapes) / layers
+        ln, lk = shapes[(layers * passes_t - 1) % layers]
+        if rank == 0:
+            bl = base[(ln, lk)]
+            chain_tp_last = {"shape": (ln, lk), "act": act_in[lk].clone(), "act_scales": act_sc[lk].clone(),
+                             "out": bl["fg"].output(last_set[(ln, lk)], m).clone(),
+                             "q": act_in[ln].clone(), "q_scales": act_sc[ln].clone(),
+                             "w": bl["w_full"], "w_scales": bl["sc_full"]}
+        chain_tp = {"layers": layers, "passes_timed": passes_t, "gpus": world,
+                    "shapes": "alternating 7168x16384 / 16384x7168, each N-sharded over the GPUs",
+                    "us_per_layer": per_layer_t * 1e6, "GBps_job": bytes_layer_t / per_layer_t / 1e9,
+                    "per_layer": "GEMM of this rank's N/g rows with the all-gather fused in tagged lines "
+                                 "(dg_launch_gather_lines, dependent mode, PDL) + GPU quantiser of the gathered "
+                                 "[M, N] output into the next layer's activation (PDL), on every rank"}
+        torch.cuda.synchronize(dev)
+        for sh in (dn, up):
+            base[sh]["fg"].close()
+        del weights, steps_t, base
+
     # ---- cuBLASLt FP8 (torch._scaled_mm) on the same cold weights: a reported
     # library baseline with per-tensor scales (no 128-block scales), M padded
     # to 16 rows.
@@ -1169,6 +1272,25 @@ def b200_arm(args, rank, world, local_rank):
         if chain is not None and "parity" in chain.get(chain.get("variant", ""), {}):
             chain["parity"] = chain[chain["variant"]]["parity"]
 
+    if rank == 0 and chain_tp_last is not None and not args.no_cpu_baseline:
+        # The tensor-parallel chain's last layer: its gathered output against
+        # the oracle on the full matrix and the bytes it read, and its
+        # quantisation bit for bit.
+        import oracle
+        cl = chain_tp_last
+        got_t = cl["out"].float().cpu().numpy()
+        want_t = oracle.compute_reference(cl["act"].cpu().numpy(), cl["act_scales"].cpu().numpy(),
+                                          cl["w"].view(torch.uint8).cpu().numpy(), cl["w_scales"].cpu().numpy(),
+                                          threads=os.cpu_count() or 1)
+        ok_t, worst_t = oracle.elementwise_ok(got_t, want_t)
+        rl2_t = oracle.rel_l2(got_t, want_t)
+        want_qt, want_st = oracle.quantize_rows(got_t)
+        q_ok_t = bool(np.array_equal(cl["q"].cpu().numpy(), want_qt) and
+                      np.array_equal(cl["q_scales"].cpu().numpy(), want_st))
+        chain_tp["parity"] = {"layer": f"last ({cl['shape'][0]}x{cl['shape'][1]}, gathered)", "rel_l2": rl2_t,
+                              "max_rel_err_floored": worst_t, "quantisation_bit_exact": q_ok_t,
+                              "ok": bool(ok_t and rl2_t <= oracle.REL_L2_GATE and q_ok_t)}
+
     if world > 1:
         dist.barrier()
     if rank != 0:
@@ -1229,6 +1351,7 @@ def b200_arm(args, rank, world, local_rank):
         # M = 1, 8, 64.
         "strong_scaling": tp.get("strong_scaling") if tp else None,
         "chain_61": chain,
+        "chain_61_tp": chain_tp,
     }
     print(json.dumps(line), file=JSON_OUT, flush=True)
 
