@@ -1050,92 +1050,109 @@ def b200_arm(args, rank, world, local_rank):
     # order.  Rank 0 checks the last layer's gathered output against the
     # oracle in the CPU leg below.
     chain_tp = None
-    chain_tp_last = None
+    chain_tp_last = {}
     if not args.no_chain and world > 1 and n % (world * 128) == 0 and k % (world * 128) == 0:
         from decode_opt_b200 import tp as dg_tp
         layers = 61
         passes = max(3, min(20, K // 500))
-        dn = (n, k)
-        up = (k, n)
-        shapes = [dn if li % 2 == 0 else up for li in range(layers)]
-        base = {}
-        for (nn, kk) in (dn, up):
-            gw = torch.Generator(device=dev).manual_seed(1000 + nn)      # the same full matrix on every rank
-            wq, ws_ = quantize_pertensor(torch.randn((nn, kk), device=dev, generator=gw), torch.float8_e4m3fn)
-            n_loc = nn // world
-            lo = rank * n_loc
-            sc_full = torch.full(((nn + 127) // 128, kk // 128), float(ws_) / math.sqrt(kk), device=dev)
-            cfg_l = default_config(m, n_loc, kk, layout=layout, pdl=pdl, independent_inputs=False)
-            w_loc = wq[lo:lo + n_loc].contiguous()
-            fg = dg_tp.FusedGather(m, n_loc, device=dev, protocol="lines")
-            base[(nn, kk)] = {"w": w_loc if layout == dg.LAYOUT_RAW else dg.prepack_weight(w_loc, cfg_l.block_n,
-                                                                                           layout),
-                              "sc": sc_full[lo // 128:(lo + n_loc) // 128].contiguous(), "cfg": cfg_l, "fg": fg,
-                              "desc": [fg.descriptor(0), fg.descriptor(1)], "n_loc": n_loc,
-                              "w_full": wq if rank == 0 else None, "sc_full": sc_full}
-        weights = [base[sh]["w"].clone() for sh in shapes]
-        act_in = {w_: torch.zeros((m, w_), dtype=torch.uint8, device=dev) for w_ in (k, n)}
-        act_sc = {w_: torch.zeros((m, w_ // 128), device=dev) for w_ in (k, n)}
-        q0, s0 = dg.quantize_activation(torch.randn((m, k), device=dev, generator=gx).bfloat16())
-        act_in[k].copy_(q0)
-        act_sc[k].copy_(s0)
-        st_t = torch.zeros(1, dtype=torch.int32, device=dev)
-        steps_t = []
-        for li, (nn, kk) in enumerate(shapes):
-            b = base[(nn, kk)]
-            pr = dg.Problem(m, b["n_loc"], kk, act_in[kk], weights[li], b["sc"], act_sc[kk], None, None, None, st_t)
-            steps_t.append((b, pr, dg.make_weight_tma(b["cfg"], pr), dg.make_activation_tma(b["cfg"], pr), nn))
-        uses = {dn: 0, up: 0}
-        last_set = {}
-
-        def chain_tp_step(i):
-            b, pr, wm_, am_, nn = steps_t[i % layers]
-            sh = shapes[i % layers]
-            j = uses[sh] % 2          # this gather's buffer set: alternates per use
-            uses[sh] += 1
-            last_set[sh] = j
-            rc = dg.launch_gather(b["cfg"], pr, b["desc"][j], wm_, am_, stream, pdl_attr=b["cfg"].pdl)
-            if rc != 0:
-                raise RuntimeError(f"tensor-parallel chain launch failed: cudaError {rc}")
-            dg.quantize_activation(b["fg"].output(j, m), out=act_in[nn], scales=act_sc[nn], stream=stream,
-                                   pdl_attr=True)
         # A gather's two sets must alternate on every use, also across graph
         # replays: an even number of passes and graphs of whole pairs of
         # passes give every gather an even number of uses per graph (each
         # graph starts on set 0 and ends on set 1).
         passes_t = passes + passes % 2
-        graphs = []
-        with torch.cuda.stream(stream):
-            for base_i in range(0, layers * passes_t, 8 * layers):
-                gr = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(gr, stream=stream):
-                    for i in range(base_i, min(layers * passes_t, base_i + 8 * layers)):
-                        chain_tp_step(i)
-                graphs.append(gr)
-        assert all(u % 2 == 0 for u in uses.values())
-        t_ct = timed(graphs)
-        del graphs
-        if int(st_t.item()) != 0:
-            raise RuntimeError(f"tensor-parallel chain status {dg.status_string(int(st_t.item()))}")
-        per_layer_t = t_ct / (layers * passes_t)
+        dn = (n, k)
+        up = (k, n)
+        shapes = [dn if li % 2 == 0 else up for li in range(layers)]
         bytes_layer_t = sum(nn * kk + m * kk + 2 * m * nn for (nn, kk) in shapes) / layers
-        ln, lk = shapes[(layers * passes_t - 1) % layers]
-        if rank == 0:
-            bl = base[(ln, lk)]
-            chain_tp_last = {"shape": (ln, lk), "act": act_in[lk].clone(), "act_scales": act_sc[lk].clone(),
-                             "out": bl["fg"].output(last_set[(ln, lk)], m).clone(),
-                             "q": act_in[ln].clone(), "q_scales": act_sc[ln].clone(),
-                             "w": bl["w_full"], "w_scales": bl["sc_full"]}
+        full = {}
+        for (nn, kk) in (dn, up):
+            gw = torch.Generator(device=dev).manual_seed(1000 + nn)      # the same full matrix on every rank
+            wq, ws_ = quantize_pertensor(torch.randn((nn, kk), device=dev, generator=gw), torch.float8_e4m3fn)
+            full[(nn, kk)] = (wq, torch.full(((nn + 127) // 128, kk // 128), float(ws_) / math.sqrt(kk), device=dev))
+        q0, s0 = dg.quantize_activation(torch.randn((m, k), device=dev, generator=gx).bfloat16())
         chain_tp = {"layers": layers, "passes_timed": passes_t, "gpus": world,
-                    "shapes": "alternating 7168x16384 / 16384x7168, each N-sharded over the GPUs",
-                    "us_per_layer": per_layer_t * 1e6, "GBps_job": bytes_layer_t / per_layer_t / 1e9,
-                    "per_layer": "GEMM of this rank's N/g rows with the all-gather fused in tagged lines "
-                                 "(dg_launch_gather_lines, dependent mode, PDL) + GPU quantiser of the gathered "
-                                 "[M, N] output into the next layer's activation (PDL), on every rank"}
-        torch.cuda.synchronize(dev)
-        for sh in (dn, up):
-            base[sh]["fg"].close()
-        del weights, steps_t, base
+                    "shapes": "alternating 7168x16384 / 16384x7168, each N-sharded over the GPUs"}
+        for variant in ("separate", "fused"):
+            fused_q = variant == "fused"
+            act_in = {w_: torch.zeros((m, w_), dtype=torch.uint8, device=dev) for w_ in (k, n)}
+            act_sc = {w_: torch.zeros((m, w_ // 128), device=dev) for w_ in (k, n)}
+            act_in[k].copy_(q0)
+            act_sc[k].copy_(s0)
+            base = {}
+            for (nn, kk) in (dn, up):
+                wq, sc_full = full[(nn, kk)]
+                n_loc = nn // world
+                lo = rank * n_loc
+                cfg_l = default_config(m, n_loc, kk, layout=layout, pdl=pdl, independent_inputs=False)
+                w_loc = wq[lo:lo + n_loc].contiguous()
+                fg = dg_tp.FusedGather(m, n_loc, device=dev, protocol="lines")
+                desc = [fg.descriptor(j, act_in[nn], act_sc[nn]) if fused_q else fg.descriptor(j) for j in (0, 1)]
+                base[(nn, kk)] = {"w": w_loc if layout == dg.LAYOUT_RAW else dg.prepack_weight(w_loc, cfg_l.block_n,
+                                                                                               layout),
+                                  "sc": sc_full[lo // 128:(lo + n_loc) // 128].contiguous(), "cfg": cfg_l,
+                                  "fg": fg, "desc": desc, "n_loc": n_loc}
+            weights = [base[sh]["w"].clone() for sh in shapes]
+            st_t = torch.zeros(1, dtype=torch.int32, device=dev)
+            steps_t = []
+            for li, (nn, kk) in enumerate(shapes):
+                b = base[(nn, kk)]
+                pr = dg.Problem(m, b["n_loc"], kk, act_in[kk], weights[li], b["sc"], act_sc[kk], None, None, None,
+                                st_t)
+                steps_t.append((b, pr, dg.make_weight_tma(b["cfg"], pr), dg.make_activation_tma(b["cfg"], pr), nn))
+            uses = {dn: 0, up: 0}
+            last_set = {}
+
+            def chain_tp_step(i, steps_t=steps_t, uses=uses, last_set=last_set, fused_q=fused_q, act_in=act_in,
+                              act_sc=act_sc):
+                b, pr, wm_, am_, nn = steps_t[i % layers]
+                sh = shapes[i % layers]
+                j = uses[sh] % 2          # this gather's buffer set: alternates per use
+                uses[sh] += 1
+                last_set[sh] = j
+                rc = dg.launch_gather(b["cfg"], pr, b["desc"][j], wm_, am_, stream, pdl_attr=b["cfg"].pdl)
+                if rc != 0:
+                    raise RuntimeError(f"tensor-parallel chain launch failed: cudaError {rc}")
+                if not fused_q:
+                    dg.quantize_activation(b["fg"].output(j, m), out=act_in[nn], scales=act_sc[nn], stream=stream,
+                                           pdl_attr=True)
+            graphs = []
+            with torch.cuda.stream(stream):
+                for base_i in range(0, layers * passes_t, 8 * layers):
+                    gr = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gr, stream=stream):
+                        for i in range(base_i, min(layers * passes_t, base_i + 8 * layers)):
+                            chain_tp_step(i)
+                    graphs.append(gr)
+            assert all(u % 2 == 0 for u in uses.values())
+            t_ct = timed(graphs)
+            del graphs
+            if int(st_t.item()) != 0:
+                raise RuntimeError(f"tensor-parallel chain status {dg.status_string(int(st_t.item()))}")
+            per_layer_t = t_ct / (layers * passes_t)
+            ln, lk = shapes[(layers * passes_t - 1) % layers]
+            if rank == 0:
+                bl = base[(ln, lk)]
+                chain_tp_last[variant] = {"shape": (ln, lk), "act": act_in[lk].clone(),
+                                          "act_scales": act_sc[lk].clone(),
+                                          "out": bl["fg"].output(last_set[(ln, lk)], m).clone(),
+                                          "q": act_in[ln].clone(), "q_scales": act_sc[ln].clone(),
+                                          "w": full[(ln, lk)][0], "w_scales": full[(ln, lk)][1]}
+            chain_tp[variant] = {
+                "us_per_layer": per_layer_t * 1e6, "GBps_job": bytes_layer_t / per_layer_t / 1e9,
+                "kernels_per_layer": 1 if fused_q else 2,
+                "per_layer": ("GEMM of this rank's N/g rows with the all-gather fused in tagged lines "
+                              "(dg_launch_gather_lines, dependent mode, PDL) whose unpack also writes the next "
+                              "layer's e4m3 activation and 1x128 scales, on every rank") if fused_q else
+                             ("the same GEMM + gather, then the GPU quantiser of the gathered [M, N] output "
+                              "(PDL), on every rank")}
+            torch.cuda.synchronize(dev)
+            for sh in (dn, up):
+                base[sh]["fg"].close()
+            del weights, steps_t, base
+        best_t = min(("separate", "fused"), key=lambda v: chain_tp[v]["us_per_layer"])
+        chain_tp.update({"us_per_layer": chain_tp[best_t]["us_per_layer"],
+                         "GBps_job": chain_tp[best_t]["GBps_job"], "variant": best_t})
+        del full
 
     # ---- cuBLASLt FP8 (torch._scaled_mm) on the same cold weights: a reported
     # library baseline with per-tensor scales (no 128-block scales), M padded
@@ -1272,24 +1289,26 @@ def b200_arm(args, rank, world, local_rank):
         if chain is not None and "parity" in chain.get(chain.get("variant", ""), {}):
             chain["parity"] = chain[chain["variant"]]["parity"]
 
-    if rank == 0 and chain_tp_last is not None and not args.no_cpu_baseline:
-        # The tensor-parallel chain's last layer: its gathered output against
-        # the oracle on the full matrix and the bytes it read, and its
-        # quantisation bit for bit.
+    if rank == 0 and chain_tp_last and not args.no_cpu_baseline:
+        # The tensor-parallel chain's last layer, each variant: its gathered
+        # output against the oracle on the full matrix and the bytes it read,
+        # and its quantisation bit for bit.
         import oracle
-        cl = chain_tp_last
-        got_t = cl["out"].float().cpu().numpy()
-        want_t = oracle.compute_reference(cl["act"].cpu().numpy(), cl["act_scales"].cpu().numpy(),
-                                          cl["w"].view(torch.uint8).cpu().numpy(), cl["w_scales"].cpu().numpy(),
-                                          threads=os.cpu_count() or 1)
-        ok_t, worst_t = oracle.elementwise_ok(got_t, want_t)
-        rl2_t = oracle.rel_l2(got_t, want_t)
-        want_qt, want_st = oracle.quantize_rows(got_t)
-        q_ok_t = bool(np.array_equal(cl["q"].cpu().numpy(), want_qt) and
-                      np.array_equal(cl["q_scales"].cpu().numpy(), want_st))
-        chain_tp["parity"] = {"layer": f"last ({cl['shape'][0]}x{cl['shape'][1]}, gathered)", "rel_l2": rl2_t,
-                              "max_rel_err_floored": worst_t, "quantisation_bit_exact": q_ok_t,
-                              "ok": bool(ok_t and rl2_t <= oracle.REL_L2_GATE and q_ok_t)}
+        for variant, cl in chain_tp_last.items():
+            got_t = cl["out"].float().cpu().numpy()
+            want_t = oracle.compute_reference(cl["act"].cpu().numpy(), cl["act_scales"].cpu().numpy(),
+                                              cl["w"].view(torch.uint8).cpu().numpy(), cl["w_scales"].cpu().numpy(),
+                                              threads=os.cpu_count() or 1)
+            ok_t, worst_t = oracle.elementwise_ok(got_t, want_t)
+            rl2_t = oracle.rel_l2(got_t, want_t)
+            want_qt, want_st = oracle.quantize_rows(got_t)
+            q_ok_t = bool(np.array_equal(cl["q"].cpu().numpy(), want_qt) and
+                          np.array_equal(cl["q_scales"].cpu().numpy(), want_st))
+            chain_tp[variant]["parity"] = {"layer": f"last ({cl['shape'][0]}x{cl['shape'][1]}, gathered)",
+                                           "rel_l2": rl2_t, "max_rel_err_floored": worst_t,
+                                           "quantisation_bit_exact": q_ok_t,
+                                           "ok": bool(ok_t and rl2_t <= oracle.REL_L2_GATE and q_ok_t)}
+        chain_tp["parity"] = chain_tp[chain_tp["variant"]].get("parity")
 
     if world > 1:
         dist.barrier()

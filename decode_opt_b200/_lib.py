@@ -13,7 +13,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libdecode_gemm_b200.so")
 
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 LAYOUT_RAW = 0
 LAYOUT_PACKED = 1
@@ -119,6 +119,8 @@ class DgGatherLines(ctypes.Structure):
         ("output", ctypes.c_void_p),
         ("lines", ctypes.c_void_p * MAX_RANKS),
         ("sync", ctypes.c_void_p),
+        ("q_out", ctypes.c_void_p),
+        ("q_scales", ctypes.c_void_p),
     ]
 
 

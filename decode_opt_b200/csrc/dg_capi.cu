@@ -197,7 +197,7 @@ cudaError_t apply_gather_lines(dg::KernelParams& p, const dg_gather_lines* gl) {
   p.output = static_cast<__nv_bfloat16*>(gl->output) + static_cast<size_t>(gl->rank) * p.N;
   p.outs[0] = p.output;
   p.ldo = gl->ldo;
-  if (gl->world == 1) return cudaSuccess;
+  if (gl->world == 1) return (gl->q_out != nullptr || gl->q_scales != nullptr) ? cudaErrorInvalidValue : cudaSuccess;
   if (gl->sync == nullptr || (p.flags & dg::kFlagCluster) == 0) return cudaErrorInvalidValue;
   for (int r = 0; r < gl->world; ++r)
     if (gl->lines[r] == nullptr || (reinterpret_cast<uintptr_t>(gl->lines[r]) & 15u) != 0)
@@ -211,6 +211,14 @@ cudaError_t apply_gather_lines(dg::KernelParams& p, const dg_gather_lines* gl) {
   p.lines_per_row = gl->world * p.N / 4;
   p.sync_ctr = gl->sync;
   p.flags |= dg::kFlagGatherLines;
+  if (gl->q_out != nullptr || gl->q_scales != nullptr) {
+    if (gl->q_out == nullptr || gl->q_scales == nullptr || (static_cast<long long>(gl->world) * p.N) % 128 != 0 ||
+        (reinterpret_cast<uintptr_t>(gl->q_out) & 3u) != 0 || (reinterpret_cast<uintptr_t>(gl->q_scales) & 3u) != 0)
+      return cudaErrorInvalidValue;
+    p.q_out = static_cast<uint8_t*>(gl->q_out);
+    p.q_scales = gl->q_scales;
+    p.flags |= dg::kFlagGatherLinesQuant;
+  }
   return cudaSuccess;
 }
 

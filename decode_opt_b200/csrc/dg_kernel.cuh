@@ -132,6 +132,10 @@ enum Flags : int {
   // and each CTA unpacks a slice of this rank's buffer once it is whole (no
   // flags, no system-scope fences).
   kFlagGatherLines = 128,
+  // With kFlagGatherLines (q_out / q_scales set): the unpack also writes the
+  // e4m3 block quantisation of the gathered output, one warp per 128-column
+  // block.
+  kFlagGatherLinesQuant = 256,
 };
 
 constexpr int kMaxClusterSplit = 16;   // CTAs per cluster (above 8: non-portable size)
@@ -1038,6 +1042,70 @@ __device__ __noinline__ inline void gather_complete(const KernelParams& p, bool 
 // gathered output is whole, which also keeps every rank within one launch of
 // the others (the two alternating line-buffer sets rely on it).  The last CTA
 // to finish stores the epoch for the next launch.
+// Waits (bounded) until line `i` of this rank's buffer carries `epoch`.
+__device__ __forceinline__ bool gather_lines_wait(const KernelParams& p, long long i, uint32_t epoch, uint64_t start,
+                                                  uint64_t& w0, uint64_t& w1) {
+  using namespace sm100;
+  for (;;) {
+    ld_volatile_line(p.lines[p.rank] + i, w0, w1);
+    if (static_cast<uint32_t>(w0 >> 32) == epoch && static_cast<uint32_t>(w1 >> 32) == epoch) return true;
+    if (global_timer_ns() - start > p.timeout_ns) return false;
+  }
+}
+
+// kFlagGatherLinesQuant: the unpack by 128-column blocks of the gathered row
+// (32 lines, one per lane; world * N % 128 == 0, checked on the host), each
+// warp also quantising its block the way dg_quantize_act does
+// (bench/bench_decode.cu:459-467 of the reference): amax of the block's bf16
+// values (each lane's four in order, then a shuffle tree), scale =
+// max(amax, 1e-4) / 448, q = e4m3(clamp(v / scale, +-448)) -- the bytes and
+// scales the standalone quantiser makes from the gathered output.  q_out is
+// [M, world * N], q_scales [M, world * N / 128].
+__device__ __noinline__ inline void gather_lines_poll_quant(const KernelParams& p, long long cta, int tid,
+                                                            int nthreads) {
+  using namespace sm100;
+  griddep_wait();
+  const uint32_t epoch = gather_lines_epoch(p);
+  const int bpr = p.lines_per_row / 32;
+  const long long total = static_cast<long long>(p.M) * bpr;
+  const long long lo = cta * total / p.num_ctas;
+  const long long hi = (cta + 1) * total / p.num_ctas;
+  const int lane = tid & 31;
+  const uint64_t start = global_timer_ns();
+  for (long long b = lo + tid / 32; b < hi; b += nthreads / 32) {
+    uint64_t w0 = 0, w1 = 0;
+    const bool ok = gather_lines_wait(p, b * 32 + lane, epoch, start, w0, w1);
+    if (!__all_sync(0xffffffffu, ok)) {
+      if (lane == 0 && p.status != nullptr) atomicCAS(p.status, 0, kErrGatherWait);
+      break;
+    }
+    const int m = static_cast<int>(b / bpr);
+    const int jb = static_cast<int>(b - static_cast<long long>(m) * bpr);
+    const int col = jb * 128 + lane * 4;
+    uint2 v;
+    v.x = static_cast<uint32_t>(w0);
+    v.y = static_cast<uint32_t>(w1);
+    *reinterpret_cast<uint2*>(p.output + static_cast<size_t>(m) * p.ldo + col) = v;
+    const __nv_bfloat162 lo2 = *reinterpret_cast<const __nv_bfloat162*>(&v.x);
+    const __nv_bfloat162 hi2 = *reinterpret_cast<const __nv_bfloat162*>(&v.y);
+    const float v4[4] = {__low2float(lo2), __high2float(lo2), __low2float(hi2), __high2float(hi2)};
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) amax = quant_max(amax, fabsf(v4[j]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = quant_max(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = quant_max(amax, 1.0e-4f) / 448.0f;
+    uint32_t packed = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float c = quant_min(quant_max(v4[j] / scale, -448.0f), 448.0f);
+      packed |= static_cast<uint32_t>(__nv_fp8_e4m3(c).__x) << (8 * j);
+    }
+    *reinterpret_cast<uint32_t*>(p.q_out + static_cast<size_t>(m) * bpr * 128 + col) = packed;
+    if (lane == 0) p.q_scales[static_cast<size_t>(m) * bpr + jb] = scale;
+  }
+}
+
 __device__ __noinline__ inline void gather_lines_poll(const KernelParams& p, long long cta, int tid, int nthreads) {
   using namespace sm100;
   griddep_wait();
@@ -1045,20 +1113,10 @@ __device__ __noinline__ inline void gather_lines_poll(const KernelParams& p, lon
   const long long total = static_cast<long long>(p.M) * p.lines_per_row;
   const long long lo = cta * total / p.num_ctas;
   const long long hi = (cta + 1) * total / p.num_ctas;
-  const uint4* mine = p.lines[p.rank];
   const uint64_t start = global_timer_ns();
   for (long long i = lo + tid; i < hi; i += nthreads) {
     uint64_t w0 = 0, w1 = 0;
-    bool ok = true;
-    for (;;) {
-      ld_volatile_line(mine + i, w0, w1);
-      if (static_cast<uint32_t>(w0 >> 32) == epoch && static_cast<uint32_t>(w1 >> 32) == epoch) break;
-      if (global_timer_ns() - start > p.timeout_ns) {
-        ok = false;
-        break;
-      }
-    }
-    if (!ok) {
+    if (!gather_lines_wait(p, i, epoch, start, w0, w1)) {
       if (p.status != nullptr) atomicCAS(p.status, 0, kErrGatherWait);
       break;
     }
@@ -1571,8 +1629,12 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   tc_fence_after();
   if (warp == Tr::kMmaWarp) tmem_dealloc(tmem_base, Tr::kTmemCols);
   if (p.world > 1 && (p.flags & kFlagGatherLines)) {
-    if (warp < static_cast<uint32_t>(Tr::kEpiWarps))
-      gather_lines_poll(p, cta, static_cast<int>(threadIdx.x), Tr::kEpiWarps * 32);
+    if (warp < static_cast<uint32_t>(Tr::kEpiWarps)) {
+      if (p.flags & kFlagGatherLinesQuant)
+        gather_lines_poll_quant(p, cta, static_cast<int>(threadIdx.x), Tr::kEpiWarps * 32);
+      else
+        gather_lines_poll(p, cta, static_cast<int>(threadIdx.x), Tr::kEpiWarps * 32);
+    }
     __syncthreads();
     if (threadIdx.x == 0) gather_lines_count(p);
   } else if (p.world > 1 && threadIdx.x == 0) {

@@ -131,10 +131,12 @@ def gather_descriptor(world: int, rank: int, n_loc: int, out_bases, flag_ptrs, s
     return g
 
 
-def lines_descriptor(world: int, rank: int, n_loc: int, output, line_bases, sync_ptr):
+def lines_descriptor(world: int, rank: int, n_loc: int, output, line_bases, sync_ptr, q_out=0, q_scales=0):
     """The dg_gather_lines for rank `rank`: `output` is this rank's gathered
     [M, world*n_loc] bf16 buffer, line_bases[q] rank q's line buffer of the
-    launch's set as mapped in this process."""
+    launch's set as mapped in this process; q_out / q_scales (optional) the
+    e4m3 [M, world*n_loc] and fp32 [M, world*n_loc/128] quantisation of the
+    gathered output the unpack also writes."""
     from ._lib import DgGatherLines, MAX_RANKS
     if not 1 <= world <= MAX_RANKS or not 0 <= rank < world:
         raise ValueError("bad world/rank")
@@ -146,6 +148,8 @@ def lines_descriptor(world: int, rank: int, n_loc: int, output, line_bases, sync
     for q in range(world):
         g.lines[q] = int(line_bases[q])
     g.sync = int(sync_ptr)
+    g.q_out = int(q_out)
+    g.q_scales = int(q_scales)
     return g
 
 
@@ -277,10 +281,18 @@ class FusedGather:
         self._imported.append(ptr.value)
         return ptr.value
 
-    def descriptor(self, i: int):
+    def descriptor(self, i: int, q_out=None, q_scales=None):
+        """The launch descriptor of buffer set i.  Lines protocol only:
+        q_out (uint8 [M, world*n_loc]) and q_scales (fp32 [M, world*n_loc/128])
+        make the launch also write the gathered output's e4m3 block
+        quantisation (the next layer's activation)."""
         if self.protocol == "lines":
             return lines_descriptor(self.world, self.rank, self.n_loc, self.buffers[i].data_ptr(),
-                                    self.peer_lines[i], self.sync.data_ptr())
+                                    self.peer_lines[i], self.sync.data_ptr(),
+                                    q_out.data_ptr() if q_out is not None else 0,
+                                    q_scales.data_ptr() if q_scales is not None else 0)
+        if q_out is not None or q_scales is not None:
+            raise ValueError("a quantised gather needs protocol='lines'")
         return gather_descriptor(self.world, self.rank, self.n_loc, self.peer_bufs[i], self.peer_flags,
                                  self.sync.data_ptr())
 

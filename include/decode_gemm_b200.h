@@ -57,7 +57,7 @@
 extern "C" {
 #endif
 
-#define DG_ABI_VERSION 7
+#define DG_ABI_VERSION 8
 
 /* Weight layouts. */
 #define DG_LAYOUT_RAW 0             /* W[N,K], K contiguous (checkpoint layout) */
@@ -247,6 +247,11 @@ typedef struct dg_gather_lines {
   void* lines[DG_MAX_RANKS];  /* rank q's line buffer of this launch's set (as mapped here):
                                  M * world * N * 4 bytes, zeroed once                          */
   int* sync;                  /* this rank's int[2] (CTA done count, last epoch), zeroed once  */
+  void* q_out;                /* optional (NULL: none): e4m3 [M, world * N] block quantisation
+                                 of the gathered output, written by the unpack -- the bytes
+                                 dg_quantize_act would make from it (world > 1, world * N a
+                                 multiple of 128, 4-byte aligned)                              */
+  float* q_scales;            /* with q_out: fp32 [M, world * N / 128]                          */
 } dg_gather_lines;
 
 int dg_launch_gather_lines(const dg_config* cfg, const dg_problem* p, const dg_gather_lines* g,

@@ -121,6 +121,14 @@ def test_lines_world_one_and_rejections():
     assert dg.launch_gather(cfg, p, desc(output=out2.data_ptr() + 2), wm, am) == dg.CUDA_ERROR_INVALID_VALUE
     assert dg.launch_gather(cfg, p, desc(ldo=2 * n - 4), wm, am) == dg.CUDA_ERROR_INVALID_VALUE
     assert dg.launch_gather(cfg, p, desc(sync=0), wm, am) == dg.CUDA_ERROR_INVALID_VALUE
+    qb = torch.zeros((m, 2 * n), dtype=torch.uint8, device=dev)
+    qsb = torch.zeros((m, 2 * n // 128), device=dev)
+    g1q = tp.lines_descriptor(1, 0, n, wide.data_ptr(), [0], sync.data_ptr(), qb.data_ptr(), qsb.data_ptr())
+    g1q.ldo = ldo
+    assert dg.launch_gather(cfg, p, g1q, wm, am) == dg.CUDA_ERROR_INVALID_VALUE        # no quantised world of one
+    assert dg.launch_gather(cfg, p, desc(q_out=qb.data_ptr()), wm, am) == dg.CUDA_ERROR_INVALID_VALUE
+    assert dg.launch_gather(cfg, p, desc(q_out=qb.data_ptr() + 1, q_scales=qsb.data_ptr()), wm, am) == \
+        dg.CUDA_ERROR_INVALID_VALUE
     n6 = n - 2
     p6 = dg.Problem(m, n6, k, p.activation, wt, p.weight_scales, p.activation_scales, None, None, None, status)
     g6 = tp.lines_descriptor(2, 0, n6, out2.data_ptr(), [lines[0].data_ptr(), lines[1].data_ptr()], sync.data_ptr())
@@ -128,7 +136,14 @@ def test_lines_world_one_and_rejections():
         dg.CUDA_ERROR_INVALID_VALUE
     torch.cuda.synchronize()
     assert int(status.item()) == 0
+    p8 = dg.Problem(m, n - 4, k, p.activation, wt, p.weight_scales, p.activation_scales, None, None, None, status)
+    g8 = tp.lines_descriptor(2, 0, n - 4, out2.data_ptr(), [lines[0].data_ptr(), lines[1].data_ptr()],
+                             sync.data_ptr(), qb.data_ptr(), qsb.data_ptr())        # 2 * 1020 % 128 != 0
+    assert dg.launch_gather(cfg, p8, g8, dg.make_weight_tma(cfg, p8), dg.make_activation_tma(cfg, p8)) == \
+        dg.CUDA_ERROR_INVALID_VALUE
+    torch.cuda.synchronize()
     assert not bool(out2.view(torch.int16).any()) and not bool(lines.any()) and not bool(sync.any())
+    assert not bool(qb.any()) and not bool(qsb.any())
 
 
 def _free_port():
@@ -139,7 +154,7 @@ def _free_port():
     return port
 
 
-def _rank_main(rank, world, port, m, n, k, result_dir, protocol="flags", steps=2):
+def _rank_main(rank, world, port, m, n, k, result_dir, protocol="flags", steps=2, quant=False):
     import torch.distributed as dist
     import oracle
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -160,20 +175,26 @@ def _rank_main(rank, world, port, m, n, k, result_dir, protocol="flags", steps=2
         sem = torch.zeros(max(plan.sem_ints, 1), dtype=torch.int32, device=dev)
         status = torch.zeros(1, dtype=torch.int32, device=dev)
         fg = tp.FusedGather(m, n_loc, device=dev, protocol=protocol)
-        results = []
+        results, qs_bytes, qs_scales = [], [], []
         for step in range(steps):
             a, as_ = oracle.gen_activation_smoke(m, k, 200 + step)
             act = torch.from_numpy(a).to(dev)
             p = dg.Problem(m, n_loc, k, act, wt, wsc, torch.from_numpy(as_).to(dev), None, ws_buf, sem, status)
+            q = torch.full((m, n), 0x55, dtype=torch.uint8, device=dev)
+            qs = torch.full((m, n // 128), -1.0, device=dev)
+            desc = fg.descriptor(step % 2, q, qs) if quant else fg.descriptor(step % 2)
             dist.barrier()
-            rc = dg.launch_gather(cfg, p, fg.descriptor(step % 2), dg.make_weight_tma(cfg, p),
-                                  dg.make_activation_tma(cfg, p))
+            rc = dg.launch_gather(cfg, p, desc, dg.make_weight_tma(cfg, p), dg.make_activation_tma(cfg, p))
             assert rc == 0, rc
             fg.wait(step % 2, status=status)
             torch.cuda.synchronize(dev)
             assert int(status.item()) == 0, dg.status_string(int(status.item()))
             results.append(fg.output(step % 2, m).float().cpu().numpy())
+            qs_bytes.append(q.cpu().numpy())
+            qs_scales.append(qs.cpu().numpy())
         np.save(os.path.join(result_dir, f"rank{rank}.npy"), np.stack(results))
+        np.save(os.path.join(result_dir, f"q{rank}.npy"), np.stack(qs_bytes))
+        np.save(os.path.join(result_dir, f"qs{rank}.npy"), np.stack(qs_scales))
         dist.barrier()
     finally:
         if fg is not None:
@@ -182,19 +203,23 @@ def _rank_main(rank, world, port, m, n, k, result_dir, protocol="flags", steps=2
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("protocol", ["flags", "lines"])
+@pytest.mark.parametrize("protocol", ["flags", "lines", "lines_quant"])
 @pytest.mark.parametrize("m", [1, 8])
 def test_two_gpu_fused_gather_matches_oracle(tmp_path, m, protocol):
     """Four consecutive launches (buffer sets 0, 1, 0, 1; under the lines
     protocol epochs 1..4, so a set's stale lines from two launches back must
-    not be taken for the current ones)."""
+    not be taken for the current ones).  lines_quant: the unpack also writes
+    the gathered output's e4m3 block quantisation, which must equal the
+    oracle's quantisation of that output bit for bit."""
     import torch.multiprocessing as mp
     import oracle
     from helpers import check_against_oracle
     n, k, world, steps = 2048, 4096, 2, 4
+    quant = protocol == "lines_quant"
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, m, n, k, str(tmp_path), protocol, steps))
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, m, n, k, str(tmp_path),
+                                                  "lines" if quant else protocol, steps, quant))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -212,6 +237,10 @@ def test_two_gpu_fused_gather_matches_oracle(tmp_path, m, protocol):
             got = np.load(os.path.join(str(tmp_path), f"rank{r}.npy"))[step]
             ok, rl2, worst = check_against_oracle(got, ref)
             assert ok, (r, step, rl2, worst)
+            if quant:
+                want_q, want_s = oracle.quantize_rows(got)
+                assert np.array_equal(np.load(os.path.join(str(tmp_path), f"q{r}.npy"))[step], want_q), (r, step)
+                assert np.array_equal(np.load(os.path.join(str(tmp_path), f"qs{r}.npy"))[step], want_s), (r, step)
 
 
 def _serve_main(rank, world, port, m, n, k, group, count, distinct, result_dir, protocol="flags"):
