@@ -945,11 +945,11 @@ def b200_arm(args, rank, world, local_rank):
     # dependent mode (its activation is read only after the previous grid
     # completes, its weights are prefetched before) whose bf16 output is
     # quantised into the next layer's e4m3 activation and 1x128 block scales.
-    # Two variants: "fused" (the headline) quantises in the GEMM's cluster
-    # reduction (dg.launch_quantized, one kernel per layer, 256-row tiles);
-    # "separate" runs the GPU quantiser as its own PDL launch after the GEMM
-    # (two kernels per layer, the default tiles).  Each layer has its own
-    # weight copy (7.2 GB, cold).
+    # Two variants, the faster one the headline: "fused" quantises in the
+    # GEMM's cluster reduction (dg.launch_quantized, one kernel per layer,
+    # 256-row tiles); "separate" runs the GPU quantiser as its own PDL launch
+    # after the GEMM (two kernels per layer, the default tiles).  Each layer
+    # has its own weight copy (7.2 GB, cold).
     chain = None
     chain_last = {}
     if not args.no_chain and world == 1:
@@ -969,15 +969,11 @@ def b200_arm(args, rank, world, local_rank):
             raw[(nn, kk)] = (wq, torch.full(((nn + 127) // 128, kk // 128), float(ws_) / math.sqrt(kk), device=dev))
         q0, s0 = dg.quantize_activation(torch.randn((m, k), device=dev, generator=gx).bfloat16())
         chain = {"layers": layers, "passes_timed": passes, "shapes": "alternating 7168x16384 / 16384x7168"}
-        for variant in ("separate", "fused", "mixed"):
+        for variant in ("separate", "fused"):
             base = {}
             for sh in (dn, up):
                 cfg_l = default_config(m, *sh, layout=layout, pdl=pdl, independent_inputs=False)
-                plan_l = cfg_l.plan(m, *sh)
-                # mixed: fuse where the default schedule already has tiles
-                # of whole 128-column blocks, else the separate quantiser
-                fq = variant == "fused" or (variant == "mixed" and cfg_l.grid_ctas == dg.GRID_CLUSTER and
-                                            plan_l.cluster >= 2 and cfg_l.block_n % 128 == 0 and sh[0] % 128 == 0)
+                fq = variant == "fused"
                 if fq:
                     cfg_l = default_config(m, *sh, layout=layout, pdl=pdl, independent_inputs=False,
                                            quantized_output=True)
@@ -1032,7 +1028,7 @@ def b200_arm(args, rank, world, local_rank):
                 "quantisation": {f"{sh[0]}x{sh[1]}": "fused" if base[sh][2] else "separate" for sh in (dn, up)}}
             del weights, steps_c, base
         # headline: the fastest variant (all three are checked against the oracle)
-        best = min(("separate", "fused", "mixed"), key=lambda v: chain[v]["us_per_layer"])
+        best = min(("separate", "fused"), key=lambda v: chain[v]["us_per_layer"])
         chain.update({key: chain[best][key] for key in ("us_per_layer", "GBps", "frac_of_peak")})
         chain["variant"] = best
         chain["per_layer"] = ("GEMM launched with PDL in the dependent mode (weights before griddepcontrol.wait, "

@@ -147,13 +147,15 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
       each tile's K range split over the CTAs of one thread-block cluster,
       reduced through distributed shared memory; the library picks the split
       from the device's cluster occupancy (one wave of clusters: the most
-      SMs for dependent launches, 32 CTAs for independent inputs) and the
-      ring as deep as shared memory allows.  224-row tiles instead of 256
-      when 224 divides N and they allow a deeper ring (M <= 16: three 56 KiB
-      stages in flight instead of two of 64 KiB) or, for dependent launches
-      of a large matrix, at least 10% more CTAs in one wave (7168 rows:
-      32 x 4 = 128 CTAs instead of 28 x 4 = 112).  Falls back to stream-K
-      where the cluster plan does not apply.
+      SMs for dependent launches, with clusters of up to 16 CTAs; 32 CTAs
+      for independent inputs) and the ring as deep as shared memory allows.
+      Dependent launches take the split and tile width (256 or 224 rows)
+      whose busiest CTA streams the least, block_n x ceil(chunks / S)
+      (7168 rows: 32 x 4 CTAs of 224 instead of 28 x 4 of 256; a 3584-row
+      shard: 14 x 8 of 256 instead of 16 x 6 of 224).  Independent inputs take 224
+      rows when 224 divides N and they allow a deeper ring (M <= 16: three
+      56 KiB stages in flight instead of two of 64 KiB).  Falls back to
+      stream-K where the cluster plan does not apply.
     * ``schedule="stream_k"``: a stream-K grid of one CTA per SM with the
       workspace reduction (two 64 KiB stages).
 
@@ -186,16 +188,24 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
             if err is not None:
                 raise ValueError(f"no quantized-output plan for M={m} N={n} K={k}: {err}")
         return base
+    if not independent_inputs:
+        # Dependent launches stream at ~50 GB/s per SM: the tile width whose
+        # busiest CTA streams the fewest weight rows x chunks (block_n x
+        # ceil(C / S)), fewer CTAs on a tie.
+        alt = replace(base, block_n=224)
+        p224 = alt.plan(m, n, k)
+        chunks = (k // K_BLOCK) // base.subs
+        cands = [(c, pl) for c, pl in ((base, p256), (alt, p224)) if pl.error is None and pl.cluster >= 2]
+        if not cands:
+            return stream_k
+        return min(cands, key=lambda cp: (cp[0].block_n * -(-chunks // cp[1].cluster), cp[1].num_ctas))[0]
     if p256.error is not None or p256.cluster < 2:
         return stream_k
     if n % 224 == 0:
         alt = replace(base, block_n=224)
         p224 = alt.plan(m, n, k)
         if p224.error is None and p224.cluster >= 2:
-            deeper = p224.stages > p256.stages
-            wider = (not independent_inputs and n * k >= 512 * 1024 * p256.num_ctas
-                     and p224.num_ctas * 10 >= p256.num_ctas * 11)
-            if deeper or wider:
+            if p224.stages > p256.stages:
                 return alt
     return base
 

@@ -64,23 +64,40 @@ constexpr int kB200ClusterOccupancy[kMaxClusterSplit + 1] = {0,  148, 74, 45, 33
                                                              15, 11,  7,  7,  7,  7,  7,  7};
 
 // The planner's cluster split for T tiles of C chunks, given occ[S] = the
-// clusters of S CTAs that fit at once (portable sizes only, S <= 8; every
-// CTA gets a chunk, S <= C).  A grid that needs a second wave of clusters
-// measured 40-70% slower, so only one-wave splits are taken:
+// clusters of S CTAs that fit at once (every CTA gets a chunk, S <= C).  A
+// grid that needs a second wave of clusters measured 40-70% slower, so only
+// one-wave splits are taken:
 //   dependent launches (each GEMM waits for the previous one before reading
-//   its activation): the largest S whose T clusters fit at once, i.e. as
-//   many SMs streaming as one wave allows;
-//   independent inputs (consecutive GEMMs may overlap): the smallest S that
-//   still gives 32 CTAs, so that more GEMMs stream side by side.
+//   its activation): a dependent GEMM streams at ~50 GB/s per SM, so its time
+//   follows the chunks its busiest CTA streams, ceil(C/S): the smallest
+//   one-wave S <= 16 that minimises ceil(C/S).  The non-portable sizes above
+//   8 pay off where tiles are few (tensor-parallel shards: 896 x 16384 on
+//   4 x 16 CTAs instead of 4 x 8 took 11.8 -> 9.4 us, 1792 x 16384 on 7 x 16
+//   instead of 8 x 8 13.3 -> 11.2); a ragged split (16 chunks over 10 CTAs)
+//   measured slower than the even one with the same busiest CTA (over 8);
+//   independent inputs (consecutive GEMMs may overlap): the smallest S <= 8
+//   that still gives 32 CTAs, so that more GEMMs stream side by side.
 // 1 (no split) when not even clusters of two fit in one wave.
 __host__ __device__ inline int choose_cluster_split(int T, int C, bool independent, const int* occ) {
-  const int s_max = C < 8 ? C : 8;
-  if (independent)
+  if (independent) {
+    const int s_max = C < 8 ? C : 8;
     for (int s = 2; s <= s_max; ++s)
       if (T <= occ[s] && static_cast<long long>(T) * s >= 32) return s;
-  for (int s = s_max; s >= 2; --s)
-    if (T <= occ[s]) return s;
-  return 1;
+    for (int s = s_max; s >= 2; --s)
+      if (T <= occ[s]) return s;
+    return 1;
+  }
+  const int s_max = C < kMaxClusterSplit ? C : kMaxClusterSplit;
+  int best = 1;
+  int best_chunks = C;
+  for (int s = 2; s <= s_max; ++s) {
+    const int chunks = (C + s - 1) / s;
+    if (T <= occ[s] && chunks < best_chunks) {
+      best = s;
+      best_chunks = chunks;
+    }
+  }
+  return best;
 }
 
 struct Plan {

@@ -93,8 +93,20 @@ def test_default_plan_c2_cluster(m):
     pi = ci.plan(m, 7168, 16384)
     assert ci.block_n == (224 if m <= 32 else 256) and pi.cluster == 2
     assert pi.num_ctas == (64 if m <= 32 else 56)
-    small = dg.default_config(m, 2048, 4096).plan(m, 2048, 4096)
-    assert small.cluster == 8 and small.num_ctas == 64
+    # a small matrix: 16 chunks per tile, so 8 CTAs per tile (two chunks
+    # each) rather than the ragged 10; 10 ragged 224-row tiles stream
+    # 224 x 2 rows-chunks per CTA against 256 x 2
+    sc = dg.default_config(m, 2048, 4096)
+    small = sc.plan(m, 2048, 4096)
+    assert sc.block_n == 224 and small.cluster == 8 and small.num_ctas == 80
+    # tensor-parallel shards: 896 x 16384 (8 GPUs) on 4 tiles x 16 (a
+    # non-portable cluster size), 3584 x 16384 (2 GPUs) on 14 tiles x 8 of
+    # 256 rows (8 chunks per CTA) rather than 16 x 6 of 224 (11)
+    s8 = dg.default_config(m, 896, 16384).plan(m, 896, 16384)
+    assert s8.cluster == 16 and s8.num_ctas == 64
+    c2 = dg.default_config(m, 3584, 16384)
+    s2 = c2.plan(m, 3584, 16384)
+    assert c2.block_n == 256 and s2.cluster == 8 and s2.num_ctas == 112
 
 
 @pytest.mark.parametrize("m", [1, 8, 16, 32, 64, 128])
@@ -216,13 +228,21 @@ def test_kernel_config_maps_onto_b200_config():
     assert dg.make_launch_plan(kr, dg.Problem(128, 7168, 16384)).error is None
 
 
-B200_CLUSTER_OCC = [0, 148, 74, 45, 33, 26, 22, 15, 15]   # clusters of S CTAs resident at once (measured)
+B200_CLUSTER_OCC = [0, 148, 74, 45, 33, 26, 22, 15, 15,      # clusters of S CTAs resident at once (measured)
+                    15, 11, 7, 7, 7, 7, 7, 7]
 
 
 def _rule_split(t, c, independent):
     """The split rule restated: independent inputs -> the smallest one-wave S
-    giving >= 32 CTAs; dependent -> the largest one-wave S (S <= 8, S <= C)."""
-    s_max = min(c, 8)
+    giving >= 32 CTAs (S <= 8); dependent -> the smallest one-wave S (S <= 16)
+    with the fewest chunks for the busiest CTA, ceil(C / S); both S <= C."""
+    s_max = min(c, 8 if independent else 16)
+    if not independent:
+        best, best_chunks = 1, c
+        for s in range(2, s_max + 1):
+            if t <= B200_CLUSTER_OCC[s] and -(-c // s) < best_chunks:
+                best, best_chunks = s, -(-c // s)
+        return best
     if independent:
         for s in range(2, s_max + 1):
             if t <= B200_CLUSTER_OCC[s] and t * s >= 32:
