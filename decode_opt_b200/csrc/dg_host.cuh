@@ -75,10 +75,17 @@ constexpr int kB200ClusterOccupancy[kMaxClusterSplit + 1] = {0,  148, 74, 45, 33
 //   4 x 16 CTAs instead of 4 x 8 took 11.8 -> 9.4 us, 1792 x 16384 on 7 x 16
 //   instead of 8 x 8 13.3 -> 11.2); a ragged split (16 chunks over 10 CTAs)
 //   measured slower than the even one with the same busiest CTA (over 8);
+//   Dependent grids also leave kSpareSms SMs free (at most SMs - 20 CTAs):
+//   the kernel between two GEMMs of a layer chain (the quantiser) and the
+//   next GEMM's early CTAs start there while this grid runs; 16384 x 7168 on
+//   all 148 SMs (74 x 2 CTAs of 224 rows) took 25.4 us per layer of the
+//   61-layer chain against 23.6 on 128 (64 x 2 of 256);
 //   independent inputs (consecutive GEMMs may overlap): the smallest S <= 8
 //   that still gives 32 CTAs, so that more GEMMs stream side by side.
 // 1 (no split) when not even clusters of two fit in one wave.
-__host__ __device__ inline int choose_cluster_split(int T, int C, bool independent, const int* occ) {
+constexpr int kSpareSms = 20;
+__host__ __device__ inline int choose_cluster_split(int T, int C, bool independent, const int* occ,
+                                                    int num_sms = 148) {
   if (independent) {
     const int s_max = C < 8 ? C : 8;
     for (int s = 2; s <= s_max; ++s)
@@ -88,11 +95,12 @@ __host__ __device__ inline int choose_cluster_split(int T, int C, bool independe
     return 1;
   }
   const int s_max = C < kMaxClusterSplit ? C : kMaxClusterSplit;
+  const long long max_ctas = (num_sms > 0 ? num_sms : 148) - kSpareSms;
   int best = 1;
   int best_chunks = C;
   for (int s = 2; s <= s_max; ++s) {
     const int chunks = (C + s - 1) / s;
-    if (T <= occ[s] && chunks < best_chunks) {
+    if (T <= occ[s] && static_cast<long long>(T) * s <= max_ctas && chunks < best_chunks) {
       best = s;
       best_chunks = chunks;
     }
@@ -262,7 +270,7 @@ __host__ __device__ inline Plan make_plan(const Config& c, int M, int N, int K, 
 #endif
     if (c.split_k <= 1 && occ == nullptr) return plan.error = "cluster split: give split_k", plan;
     const int S = c.split_k > 1 ? c.split_k
-                                : choose_cluster_split(T, C, (c.flags & kFlagIndependentInputs) != 0, occ);
+                                : choose_cluster_split(T, C, (c.flags & kFlagIndependentInputs) != 0, occ, num_sms);
     if (S > kMaxClusterSplit) return plan.error = "cluster split: split_k must be <= 16", plan;
     // A given split may exceed the chunks of a tile: the CTAs left without a
     // chunk contribute zero partials.

@@ -234,13 +234,14 @@ B200_CLUSTER_OCC = [0, 148, 74, 45, 33, 26, 22, 15, 15,      # clusters of S CTA
 
 def _rule_split(t, c, independent):
     """The split rule restated: independent inputs -> the smallest one-wave S
-    giving >= 32 CTAs (S <= 8); dependent -> the smallest one-wave S (S <= 16)
-    with the fewest chunks for the busiest CTA, ceil(C / S); both S <= C."""
+    giving >= 32 CTAs (S <= 8); dependent -> the smallest one-wave S (S <= 16,
+    at most 148 - 20 CTAs) with the fewest chunks for the busiest CTA,
+    ceil(C / S); both S <= C."""
     s_max = min(c, 8 if independent else 16)
     if not independent:
         best, best_chunks = 1, c
         for s in range(2, s_max + 1):
-            if t <= B200_CLUSTER_OCC[s] and -(-c // s) < best_chunks:
+            if t <= B200_CLUSTER_OCC[s] and t * s <= 128 and -(-c // s) < best_chunks:
                 best, best_chunks = s, -(-c // s)
         return best
     if independent:
