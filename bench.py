@@ -73,6 +73,9 @@ def parse_args():
                          "timed; this picks the headline.")
     ap.add_argument("--schedule", choices=["cluster", "stream_k"], default="cluster",
                     help="default_config's schedule: cluster split-K (default) or stream-K over one CTA per SM")
+    ap.add_argument("--batch-class", choices=["default", "swap_ab"], default="default",
+                    help="kernel class for M <= 16 on the cluster schedule: the default (batch on the MMA's M "
+                         "side, padded to 64) or swap-AB (weights on the M side, batch padded to 16 on N)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-depth", type=int, default=4,
                     help="e2e loop on 1 GPU: requests in flight, one stream each (1: no pipelined loop)")
@@ -347,6 +350,8 @@ def b200_arm(args, rank, world, local_rank):
     independent = args.pdl_mode == "independent"
 
     def default_config(*a, **kw):
+        if args.batch_class == "swap_ab" and a[0] <= 16 and args.schedule == "cluster":
+            kw.setdefault("swap_ab", True)
         return dg.default_config(*a, schedule=args.schedule, **kw)
 
     stream = torch.cuda.Stream(device=dev)
@@ -1329,6 +1334,8 @@ def b200_arm(args, rank, world, local_rank):
                            if world > 1 else ""),
             "M": m, "N": n, "K": k, "layout": args.layout, "block_n": cfg.block_n, "subs": cfg.subs,
             "stages": gs.plan.stages, "grid": list(gs.plan.grid), "threads_per_cta": gs.plan.block[0],
+            "batch_class": ("swap_ab" if cfg.flags & dg.FLAG_SWAP_AB else "default"),
+            "mma": f"{gs.plan.mma_m}x{gs.plan.n_mma}x32",
             "pdl": cfg.pdl, "pdl_mode": args.pdl_mode, "rotation_sets": rot.nsets,
             "working_set_bytes": rot.nsets * rot.set_bytes, "l2_bytes": rot.l2,
             "cold": "inputs larger than L2 (rotated weight copies), no flush",

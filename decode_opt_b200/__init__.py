@@ -38,8 +38,9 @@ from dataclasses import dataclass, field
 from typing import Optional
 
 from . import _lib
-from ._lib import (ERR_INJECTED_TIMEOUT, FLAG_INDEPENDENT_INPUTS, FLAG_INJECT_TIMEOUT, GRID_CLUSTER, LAYOUT_PACKED,
-                   LAYOUT_PACKED_SWIZZLED, LAYOUT_RAW, STATUS_OK, DgConfig, DgPlanInfo, DgProblem, TensorMap)
+from ._lib import (ERR_INJECTED_TIMEOUT, FLAG_INDEPENDENT_INPUTS, FLAG_INJECT_TIMEOUT, FLAG_SWAP_AB, GRID_CLUSTER,
+                   LAYOUT_PACKED, LAYOUT_PACKED_SWIZZLED, LAYOUT_RAW, STATUS_OK, DgConfig, DgPlanInfo, DgProblem,
+                   TensorMap)
 
 __all__ = [
     "cluster_min_stages",
@@ -48,6 +49,7 @@ __all__ = [
     "packed_weight_bytes",
     "launch_prepack_weight", "prepack_weight", "fp8_decode_gemm", "default_config", "status_string",
     "LAYOUT_RAW", "LAYOUT_PACKED", "LAYOUT_PACKED_SWIZZLED", "FLAG_INJECT_TIMEOUT", "FLAG_INDEPENDENT_INPUTS",
+    "FLAG_SWAP_AB",
     "ERR_INJECTED_TIMEOUT", "STATUS_OK", "m_tile_for", "flush_l2", "GRID_CLUSTER",
 ]
 
@@ -137,7 +139,7 @@ class B200Config:
 
 def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool = True,
                    independent_inputs: bool = False, schedule: str = "cluster",
-                   quantized_output: bool = False) -> B200Config:
+                   quantized_output: bool = False, swap_ab: bool = False) -> B200Config:
     """The B200 schedule used by :func:`fp8_decode_gemm` and the benchmark.
 
     Two 128-K blocks per stage and weight tiles on the tcgen05 N side, 256
@@ -164,17 +166,24 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
     :func:`launch_quantized` accepts: the cluster schedule on 256-row tiles
     (whole 128-column quantisation blocks per tile) with at least two CTAs
     per tile; ValueError where the cluster plan does not apply or N is not a
-    multiple of 128.
+    multiple of 128.  `swap_ab` (M <= 16, cluster schedule) selects the
+    swap-AB batch class (FLAG_SWAP_AB): the weights on the MMA's M side, 128
+    rows per tcgen05.mma, the batch padded to 16 on its N side, with the
+    tile width and split chosen as above; ValueError where it does not apply.
     """
     from dataclasses import replace
     flags = FLAG_INDEPENDENT_INPUTS if independent_inputs else 0
     stream_k = B200Config(m_tile=m_tile_for(m), block_n=256, subs=2, stages=2, layout=layout, pdl=pdl,
                           split_k=1, grid_ctas=-1, flags=flags)
+    if swap_ab and (schedule != "cluster" or m > 16):
+        raise ValueError(f"no swap-AB plan for M={m}: needs M <= 16 and the cluster schedule")
     if schedule == "stream_k" and not quantized_output:
         return stream_k
     if schedule not in ("cluster", "stream_k"):
         raise ValueError("schedule must be 'cluster' or 'stream_k'")
     base = replace(stream_k, grid_ctas=GRID_CLUSTER, stages=0)
+    if swap_ab:
+        base = replace(base, flags=base.flags | FLAG_SWAP_AB)
     p256 = base.plan(m, n, k)
     if quantized_output:
         if schedule != "cluster" or n % 128 != 0 or p256.error is not None:
@@ -197,10 +206,10 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
         chunks = (k // K_BLOCK) // base.subs
         cands = [(c, pl) for c, pl in ((base, p256), (alt, p224)) if pl.error is None and pl.cluster >= 2]
         if not cands:
-            return stream_k
+            return _no_swap_fallback(swap_ab, stream_k, base, m, n, k, p256.error)
         return min(cands, key=lambda cp: (cp[0].block_n * -(-chunks // cp[1].cluster), cp[1].num_ctas))[0]
     if p256.error is not None or p256.cluster < 2:
-        return stream_k
+        return _no_swap_fallback(swap_ab, stream_k, base, m, n, k, p256.error)
     if n % 224 == 0:
         alt = replace(base, block_n=224)
         p224 = alt.plan(m, n, k)
@@ -208,6 +217,17 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
             if p224.stages > p256.stages:
                 return alt
     return base
+
+
+def _no_swap_fallback(swap_ab, stream_k, base, m, n, k, err):
+    """default_config's stream-K fallback where no cluster split applies.  The
+    swap-AB class has no stream-K schedule: it keeps the cluster schedule
+    (one CTA per tile, stored directly, when no split fits) or raises."""
+    if swap_ab:
+        if err is not None:
+            raise ValueError(f"no swap-AB cluster plan for M={m} N={n} K={k} ({err})")
+        return base
+    return stream_k
 
 
 def cluster_min_stages(m: int, subs: int, block_n: int, mma_m: int) -> int:

@@ -13,7 +13,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libdecode_gemm_b200.so")
 
-ABI_VERSION = 8
+ABI_VERSION = 9
 
 LAYOUT_RAW = 0
 LAYOUT_PACKED = 1
@@ -22,6 +22,7 @@ GRID_CLUSTER = -2              # DG_GRID_CLUSTER
 
 FLAG_INJECT_TIMEOUT = 2
 FLAG_INDEPENDENT_INPUTS = 4
+FLAG_SWAP_AB = 512              # DG_FLAG_SWAP_AB
 STATIC_SEM_INTS = 4096          # DG_STATIC_SEM_INTS
 STATIC_WS_FLOATS = 2097152      # DG_STATIC_WS_FLOATS
 

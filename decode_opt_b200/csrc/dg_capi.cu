@@ -82,6 +82,16 @@ KernelEntry* select_kernel(int mma_m, int copies, int epw) {
   return nullptr;
 }
 
+// The swap-AB class (no register reallocation, so no pool check).
+KernelEntry* swap_entry() {
+  static KernelEntry e{dg::swap_kernel_ptr(), {0}, cudaSuccess, {0}};
+  return &e;
+}
+
+KernelEntry* select_kernel(const Plan& plan) {
+  return plan.swap ? swap_entry() : select_kernel(plan.mma_m, plan.copies, plan.epw);
+}
+
 // Cluster occupancy of the current device: occ[S] clusters of S CTAs at one
 // CTA per SM (every batch-class kernel holds an SM alone: its registers
 // exceed half the register file), from cudaOccupancyMaxActiveClusters, asked
@@ -259,7 +269,7 @@ int launch_impl(const dg_config* cfg, const dg_problem* prob, const CUtensorMap*
     p.q_scales = q_scales;
     p.flags |= dg::kFlagQuantizeOut;
   }
-  KernelEntry* k = select_kernel(plan.mma_m, plan.copies, plan.epw);
+  KernelEntry* k = select_kernel(plan);
   if (k == nullptr) return cudaErrorInvalidValue;
   if (k->pool_check != cudaSuccess) return k->pool_check;
   const cudaError_t attr_err = dg::ensure_smem(reinterpret_cast<const void*>(k->fn), &k->smem_set);
@@ -398,7 +408,7 @@ int dg_max_active_clusters(const dg_config* cfg, int M, int N, int K, int* out) 
   *out = 0;
   const Plan plan = plan_for(to_config(cfg), M, N, K);
   if (plan.error != nullptr) return cudaErrorInvalidValue;
-  KernelEntry* k = select_kernel(plan.mma_m, plan.copies, plan.epw);
+  KernelEntry* k = select_kernel(plan);
   if (k == nullptr) return cudaErrorInvalidValue;
   cudaError_t err = dg::ensure_smem(reinterpret_cast<const void*>(k->fn), &k->smem_set);
   if (err != cudaSuccess) return err;

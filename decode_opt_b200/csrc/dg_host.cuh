@@ -122,6 +122,7 @@ struct Plan {
   int sem_ints = 0;         // num_tiles when max_slabs > 1
   int padded_n = 0;
   int cluster = 1;          // CTAs per cluster along grid y (cluster split-K)
+  bool swap = false;        // swap-AB class (SwapTraits)
   const char* error = nullptr;
 };
 
@@ -138,10 +139,15 @@ struct Plan {
 // 0.5-2 us faster than MMA M 128 at M = 17..32.  One 64-row copy at M = 64
 // halves the epilogue's active lanes and measured slower than two copies
 // at MMA M 128.
+// With kFlagSwapAB (M <= 16) the class is SwapTraits instead: the weights
+// on the MMA's M side (two 128-row MMAs per tile of 136..256 rows), the
+// batch padded to 16 on its N side, 4 epilogue warps and two MMA-issuing
+// warps.
 struct BatchClass {
   int mma_m;
   int copies;
   int epw;
+  bool swap = false;
 };
 
 __host__ __device__ inline BatchClass batch_class_for(int M) {
@@ -236,23 +242,33 @@ __host__ __device__ inline Plan make_plan(const Config& c, int M, int N, int K, 
 
   // kFlagClassFromMTile: the class of m_tile rather than of M (the C++
   // header's kernel entry is compiled for its KernelConfig's M_TILE).
-  const BatchClass bc = batch_class_for((c.flags & kFlagClassFromMTile) ? c.m_tile : M);
+  BatchClass bc = batch_class_for((c.flags & kFlagClassFromMTile) ? c.m_tile : M);
+  if (c.flags & kFlagSwapAB) {
+    if (((c.flags & kFlagClassFromMTile) ? c.m_tile : M) > SwapTraits::kMmaN)
+      return plan.error = "swap-AB: M must be <= 16", plan;
+    if (c.block_n <= SwapTraits::kMmaM) return plan.error = "swap-AB: block_n must be in [136, 256]", plan;
+    if (c.grid_ctas != kGridCluster) return plan.error = "swap-AB: cluster split-K schedule only", plan;
+    bc = {SwapTraits::kMmaM, 1, 1, true};
+  }
   const int mma_m = bc.mma_m;
   const int epw = bc.epw;
   const int copies = bc.copies;
-  const int n_mma = ((c.block_n + 15) / 16) * 16;
+  // Activation rows per 128-K block in shared memory: the MMA M (batch
+  // copies included), or the swap class's 16-row MMA N.
+  const int act_rows = bc.swap ? SwapTraits::kActRows : mma_m;
+  const int n_mma = bc.swap ? SwapTraits::kMmaN : ((c.block_n + 15) / 16) * 16;
   const int a_rows = ((M + 7) / 8) * 8;
-  if (a_rows > mma_m / copies) return plan.error = "batch does not fit its activation copy", plan;
+  if (a_rows > act_rows / copies) return plan.error = "batch does not fit its activation copy", plan;
   const int bufs = kAccumBuffers;
   const uint32_t w_stage = static_cast<uint32_t>(c.subs * c.block_n * kKBlock);
-  const uint32_t a_stage = static_cast<uint32_t>(c.subs * mma_m * kKBlock);
+  const uint32_t a_stage = static_cast<uint32_t>(c.subs * act_rows * kKBlock);
   const uint32_t a_tx = static_cast<uint32_t>(c.subs * copies * a_rows * kKBlock);
   // The MMA reads n_mma weight rows from each 128-K block; rows past those
   // loaded come from the next block or this tail pad and only feed output
-  // columns that are never stored.
-  const uint32_t w_pad = static_cast<uint32_t>((n_mma - c.block_n) * kKBlock);
+  // columns that are never stored.  (The swap class reads exactly block_n.)
+  const uint32_t w_pad = bc.swap ? 0u : static_cast<uint32_t>((n_mma - c.block_n) * kKBlock);
   (void)bufs;
-  auto smem_for = [&](int stages) -> uint32_t { return pipeline_smem_bytes(stages, c.subs, c.block_n, mma_m); };
+  auto smem_for = [&](int stages) -> uint32_t { return pipeline_smem_bytes(stages, c.subs, c.block_n, act_rows); };
   int stages = c.stages;
   if (stages == 0) {
     stages = 1;
@@ -341,7 +357,8 @@ __host__ __device__ inline Plan make_plan(const Config& c, int M, int N, int K, 
   p.rank = 0;
 
   plan.epi_warps = 4 * epw;
-  plan.block = dim3(static_cast<unsigned>(block_threads(copies, epw)), 1u, 1u);
+  plan.block = dim3(static_cast<unsigned>(bc.swap ? SwapTraits::kThreads : block_threads(copies, epw)), 1u, 1u);
+  plan.swap = bc.swap;
   plan.smem_bytes = p.smem_bytes;
   plan.mma_m = mma_m;
   plan.copies = copies;
@@ -453,6 +470,8 @@ template <int MMA_M, int COPIES, int EPW>
 inline KernelFn kernel_ptr() {
   return reinterpret_cast<KernelFn>(&dg_decode_gemm_kernel<MMA_M, COPIES, EPW>);
 }
+
+inline KernelFn swap_kernel_ptr() { return reinterpret_cast<KernelFn>(&dg_decode_gemm_swap_kernel<SwapTraits>); }
 
 // A kernel that reallocates registers (setmaxnreg) needs a launch register
 // pool, threads x registers per thread at launch, that covers the split;

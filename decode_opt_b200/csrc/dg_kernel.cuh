@@ -136,6 +136,9 @@ enum Flags : int {
   // e4m3 block quantisation of the gathered output, one warp per 128-column
   // block.
   kFlagGatherLinesQuant = 256,
+  // Host planning only: the swap-AB batch class (SwapTraits; M <= 16,
+  // block_n 256, cluster split-K schedule).
+  kFlagSwapAB = 512,
 };
 
 constexpr int kMaxClusterSplit = 16;   // CTAs per cluster (above 8: non-portable size)
@@ -274,10 +277,49 @@ struct KernelTraits {
   static constexpr int kDeferUnits = 4;
   static constexpr int kNumBufs = 2;                 // 2 x 256 columns = all of TMEM
   static constexpr uint32_t kTmemCols = 512u;
+  static constexpr bool kSwap = false;
+  static constexpr int kActRows = kMmaM;             // activation rows per 128-K block in smem
+  static constexpr int kMmaIssuers = 1;
   static_assert(kColsPerCopy == kEpw * kColsPerWarp, "column split");
   static_assert((kColsPerWarp / 16) % kLdBatch == 0, "whole load batches");
   static_assert(!kRegRealloc || (kEpiWarps % 4 == 0 && kThreads == (kEpiWarps + 4) * 32),
                 "register reallocation needs whole warpgroups");
+};
+
+// Swap-AB batch class (M <= 16): the weights are the MMA's M side and the
+// batch its N side, tcgen05.mma M = 128 weight rows x N = 16 batch rows x
+// K = 32, so an instruction multiplies 4 KiB of weights by the batch padded to
+// 16 instead of padding the batch to 64 rows: a quarter of the multiply-adds
+// per weight byte of the M = 64 class, and with them the tensor pipe's power
+// draw.  A tile of block_n = 136..256 rows is covered by two 128-row halves,
+// rows [0, 128) and [block_n - 128, block_n) (they overlap for block_n < 256;
+// the overlap is folded once); two MMA warps issue one half each into their
+// own 16 accumulator columns (one issuing thread needs ~72 cycles per MMA,
+// two bring the pair to ~39 each, so a 128-K block takes ~4 x 78 cycles
+// against 448 for the M = 64 x N = 224 class).  TMEM lane = row within a
+// half, column = batch row: epilogue warp q folds lanes 32q..32q+31 of both
+// halves, 2 x 16 values per thread, and writes them transposed into the same
+// [M][block_n] shared-memory partial the cluster reduction of the other
+// classes reads.
+struct SwapTraits {
+  static constexpr bool kSwap = true;
+  static constexpr int kMmaM = 128;                  // weight rows per MMA (one tile half)
+  static constexpr int kMmaN = 16;                   // batch rows per MMA, padded
+  static constexpr int kActRows = kMmaN;             // activation rows per 128-K block in smem
+  static constexpr int kCopies = 1;
+  static constexpr int kRowsPerCopy = kMmaN;
+  static constexpr int kEpw = 1;
+  static constexpr int kEpiWarps = 4;
+  static constexpr int kEpiThreads = kEpiWarps * 32;
+  static constexpr bool kRegRealloc = false;
+  static constexpr int kProducerWarp = kEpiWarps;
+  static constexpr int kMmaWarp = kEpiWarps + 1;     // issues tile rows 0..127
+  static constexpr int kMmaIssuers = 2;              // warp kMmaWarp + 1 issues rows 128..255
+  static constexpr int kThreads = (kEpiWarps + 2 + 1) * 32;
+  static constexpr int kBnMax = 2 * kMmaN;           // accumulator columns per buffer
+  static constexpr int kNumBufs = 2;
+  static constexpr uint32_t kTmemCols = 64u;
+  static constexpr int kDeferUnits = 4;              // as the other classes (M <= 16: <= 4 units)
 };
 
 // Where epilogue warp w works: lane quarter, batch rows, weight columns.
@@ -299,17 +341,25 @@ struct EpiWarp {
 
 template <class Tr>
 __host__ __device__ __forceinline__ int active_epilogue_warps(int M, int block_n) {
-  int n = 0;
-  for (int w = 0; w < Tr::kEpiWarps; ++w) n += EpiWarp<Tr>(w, M, block_n).active ? 1 : 0;
-  return n;
+  if constexpr (Tr::kSwap) {
+    return Tr::kEpiWarps;   // every lane quarter holds tile rows
+  } else {
+    int n = 0;
+    for (int w = 0; w < Tr::kEpiWarps; ++w) n += EpiWarp<Tr>(w, M, block_n).active ? 1 : 0;
+    return n;
+  }
 }
 
 // Rank of warp w among the active epilogue warps.
 template <class Tr>
 __device__ __forceinline__ int active_epilogue_rank(int w, int M, int block_n) {
-  int n = 0;
-  for (int v = 0; v < w; ++v) n += EpiWarp<Tr>(v, M, block_n).active ? 1 : 0;
-  return n;
+  if constexpr (Tr::kSwap) {
+    return w;
+  } else {
+    int n = 0;
+    for (int v = 0; v < w; ++v) n += EpiWarp<Tr>(v, M, block_n).active ? 1 : 0;
+    return n;
+  }
 }
 
 // mbarriers (ring full/empty, accumulator full/empty, drain, test hook, two
@@ -1142,6 +1192,188 @@ __device__ __noinline__ inline void gather_lines_count(const KernelParams& p) {
   }
 }
 
+// Cluster split-K after the main loop, for every active epilogue thread: the
+// tile's S partials (each CTA's in its own shared memory at w_region, rows of
+// cluster_partial_stride floats) are summed in rank order and stored -- plain,
+// quantised or as gather lines.  Takes part in both cluster barriers.  With
+// independent inputs a thread whose share fits in registers reduces before
+// waiting on the preceding grid.
+template <class Tr>
+__device__ __forceinline__ void cluster_epilogue(const KernelParams& p, uint8_t* w_region, bool waited,
+                                                 int active_tid, int epi_threads, bool leader, bool out_vec,
+                                                 volatile int* abort_flag, volatile int* wrote_output) {
+  using namespace sm100;
+  const int tile = static_cast<int>(blockIdx.x);
+  const bool quant = (p.flags & kFlagQuantizeOut) != 0;
+  const bool defer = !waited && !quant && !(p.flags & kFlagGatherLines) &&
+                     cluster_units_per_thread(p, tile, epi_threads) <= Tr::kDeferUnits;
+  if (!waited && !defer) griddep_wait();   // a CTA without units still stores its share
+  cluster_sync_acq_rel();        // every partial of the tile is in place
+  if (defer) {
+    uint2 staged[Tr::kDeferUnits];
+    const bool live = *abort_flag == 0;
+    if (live) cluster_sum_units<Tr::kDeferUnits>(p, smem_addr(w_region), tile, active_tid, epi_threads, staged);
+    cluster_sync_acq_rel();      // no peer reads this CTA's partial any more
+    griddep_wait();              // the stores follow the preceding grid
+    if (live) {
+      if (leader) *wrote_output = 1;
+      cluster_store_units<Tr::kDeferUnits>(p, tile, active_tid, epi_threads, out_vec, staged);
+    }
+  } else {
+    if (*abort_flag == 0) {
+      if (leader) *wrote_output = 1;
+      if (quant)
+        cluster_reduce_tile_quant(p, smem_addr(w_region), tile, active_tid / 32, active_tid & 31, epi_threads / 32);
+      else
+        cluster_reduce_tile(p, smem_addr(w_region), tile, active_tid, epi_threads, out_vec);
+    }
+    cluster_sync_acq_rel();      // no peer reads this CTA's partial any more
+  }
+}
+
+// Epilogue of the swap-AB class (SwapTraits), run by its four epilogue warps.
+// Warp q reads TMEM lane quarter q: thread (q, lane) holds tile rows (output
+// columns) r = 32q + lane and h1 + r (h1 = block_n - 128; only where that row
+// is not also in half 0, h1 + r >= 128), each for the 16 batch rows in the
+// accumulator's columns, and folds every 128-K block with the other classes'
+// arithmetic (combined = w_s * a_s, then one fma per element), each row with
+// the weight scale of its own 128-row group.  Under cluster split-K the
+// partial goes to shared memory in the [M][block_n] layout of the other
+// classes and cluster_epilogue reduces it; a tile with one contributor (no
+// split) is stored directly.
+template <class Tr>
+__device__ __forceinline__ void swap_epilogue(const KernelParams& p, uint32_t tmem_base, uint64_t* accum_full,
+                                              uint64_t* accum_empty, volatile int* abort_flag,
+                                              volatile int* wrote_output, uint8_t* w_region, long long u_begin,
+                                              long long u_end) {
+  using namespace sm100;
+  const uint32_t warp = threadIdx.x / 32u;
+  const uint32_t lane = threadIdx.x & 31u;
+  const int M = p.M;
+  const int N = p.N;
+  const int KB = p.num_kb;
+  const int bn = p.block_n;
+  const int C = p.chunks_per_tile;
+  const int r = static_cast<int>(warp * 32u + lane);   // tile row in half 0
+  const int h1 = bn - Tr::kMmaM;                       // first tile row of half 1
+  const bool has1 = h1 + r >= Tr::kMmaM;               // half 1's row is not in half 0
+  const uint32_t t_lane = tmem_base + ((warp * 32u) << 16);
+  const bool leader = threadIdx.x == 0;
+  const bool cluster = (p.flags & kFlagCluster) != 0;
+  bool out_vec = (p.ldo & 7) == 0;
+  for (int o = 0; o < p.n_outs; ++o) out_vec = out_vec && (reinterpret_cast<uintptr_t>(p.outs[o]) & 15u) == 0;
+  bool waited = !(p.flags & kFlagIndependentInputs);
+  if (waited) griddep_wait();
+
+  float* const part_rows = reinterpret_cast<float*>(w_region);
+  const int stride = cluster_partial_stride(bn);
+  // Column c of batch row j in the shared-memory partial: float4 unit c/4 of
+  // the row at unit (c/4) xor (j mod 8), as the other classes store it.
+  auto part_at = [&](int j, int c) -> float* {
+    return part_rows + static_cast<size_t>(j) * stride + 4 * ((c >> 2) ^ (j & 7)) + (c & 3);
+  };
+
+  int acc = 0;
+  long long u = u_begin;
+  while (u < u_end) {
+    const int tile = static_cast<int>(u / C);
+    const long long tile_first = static_cast<long long>(tile) * C;
+    const long long seg_end = (tile_first + C) < u_end ? (tile_first + C) : u_end;
+    const int last_g = (N - 1) / kKBlock;
+    const int g0 = min((tile * bn + r) / kKBlock, last_g);
+    const int g1 = min((tile * bn + h1 + r) / kKBlock, last_g);
+    const float* w0 = p.w_scales + static_cast<size_t>(g0) * KB;
+    const float* w1 = p.w_scales + static_cast<size_t>(g1) * KB;
+    float part0[Tr::kMmaN];
+    float part1[Tr::kMmaN];
+#pragma unroll
+    for (int j = 0; j < Tr::kMmaN; ++j) part0[j] = part1[j] = 0.0f;
+
+    for (long long uu = u; uu < seg_end; ++uu) {
+      const int chunk = static_cast<int>(uu - tile_first);
+      for (int s = 0; s < p.subs; ++s, ++acc) {
+        const int kb = chunk * p.subs + s;
+        const int buf = acc % Tr::kNumBufs;
+        // Scales before the accumulator wait, so their latency hides behind it.
+        float a_s[Tr::kMmaN];
+#pragma unroll
+        for (int j = 0; j < Tr::kMmaN; ++j) a_s[j] = __ldg(p.a_scales + static_cast<size_t>(min(j, M - 1)) * KB + kb);
+        const float ws0 = __ldg(w0 + kb);
+        const float ws1 = __ldg(w1 + kb);
+        int ready = 0;
+        if (lane == 0) {
+          ready = mbar_wait_bounded(&accum_full[buf], static_cast<uint32_t>((acc / Tr::kNumBufs) & 1), abort_flag,
+                                    p.status, kErrEpilogueAccumWait, p.timeout_ns)
+                      ? 1
+                      : 0;
+        }
+        ready = __shfl_sync(0xffffffffu, ready, 0);
+        if (!ready) continue;
+        tc_fence_after();
+        uint32_t raw0[Tr::kMmaN];
+        uint32_t raw1[Tr::kMmaN];
+        const uint32_t t = t_lane + static_cast<uint32_t>(buf * Tr::kBnMax);
+        tmem_ld_x16(t, raw0);
+        tmem_ld_x16(t + static_cast<uint32_t>(Tr::kMmaN), raw1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < Tr::kMmaN; ++j) {
+          part0[j] = fmaf(ws0 * a_s[j], __uint_as_float(raw0[j]), part0[j]);
+          part1[j] = fmaf(ws1 * a_s[j], __uint_as_float(raw1[j]), part1[j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&accum_empty[buf]);
+      }
+    }
+
+    // ------------------------------------------------------------ emit ----
+    if (cluster) {
+      if (*abort_flag == 0) {
+#pragma unroll
+        for (int j = 0; j < Tr::kMmaN; ++j) {
+          if (j < M) {
+            *part_at(j, r) = part0[j];
+            if (has1) *part_at(j, h1 + r) = part1[j];
+          }
+        }
+      }
+    } else {
+      // One contributor per tile: the tile's output, after the preceding grid.
+      if (!waited) {
+        griddep_wait();
+        waited = true;
+      }
+      if (leader) *wrote_output = 1;
+      const int n0 = tile * bn + r;
+      if (*abort_flag == 0) {
+        for (int o = 0; o < p.n_outs; ++o) {
+          __nv_bfloat16* out = p.outs[o];
+#pragma unroll
+          for (int j = 0; j < Tr::kMmaN; ++j) {
+            if (j < M) {
+              if (n0 < N) out[static_cast<size_t>(j) * p.ldo + n0] = __float2bfloat16_rn(part0[j]);
+              if (has1 && n0 + h1 < N) out[static_cast<size_t>(j) * p.ldo + n0 + h1] = __float2bfloat16_rn(part1[j]);
+            }
+          }
+        }
+      }
+    }
+    u = seg_end;
+  }
+  if (!cluster) return;
+  // A cluster CTA without units (a split finer than the tile's chunks)
+  // contributes a zero partial.
+  if (u_begin == u_end && *abort_flag == 0) {
+    for (int j = 0; j < M; ++j) {
+      *part_at(j, r) = 0.0f;
+      if (has1) *part_at(j, h1 + r) = 0.0f;
+    }
+  }
+  cluster_epilogue<Tr>(p, w_region, waited, static_cast<int>(threadIdx.x), Tr::kEpiThreads, leader, out_vec,
+                       abort_flag, wrote_output);
+}
+
 template <class Tr>
 __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
                                                  const CUtensorMap* w_map,
@@ -1191,10 +1423,10 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   if (warp == Tr::kProducerWarp && lane == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], 1);
+      mbar_init(&empty_bar[s], Tr::kMmaIssuers);
     }
     for (int b = 0; b < Tr::kNumBufs; ++b) {
-      mbar_init(&accum_full[b], 1);
+      mbar_init(&accum_full[b], Tr::kMmaIssuers);
       mbar_init(&accum_empty[b], static_cast<uint32_t>(active_warps));
     }
     mbar_init(drain_bar, 1);
@@ -1261,7 +1493,7 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
 #pragma unroll
           for (int c = 0; c < Tr::kCopies; ++c)
             tma_load_3d(a_map, &full_bar[slot],
-                        a_stage + (s * Tr::kMmaM + c * Tr::kRowsPerCopy) * kKBlock, 0, 0,
+                        a_stage + (s * Tr::kActRows + c * Tr::kRowsPerCopy) * kKBlock, 0, 0,
                         chunk * p.subs + s, pol_a);
       };
       // First ring pass: weights before the grid dependency resolves.
@@ -1304,12 +1536,21 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
       }
     }
     __syncwarp();
-  } else if (warp == Tr::kMmaWarp) {
+  } else if (warp >= static_cast<uint32_t>(Tr::kMmaWarp) &&
+             warp < static_cast<uint32_t>(Tr::kMmaWarp + Tr::kMmaIssuers)) {
     // ============================================================= MMA ====
+    // Swap-AB: issuer `half` multiplies tile rows [half (block_n - 128),
+    // + 128) into accumulator columns [16 half, 16 half + 16) of each buffer; the
+    // ring and accumulator barriers count one commit per issuer.  It drains
+    // its own MMAs after an abort on its own barrier (the swap class has no
+    // workspace reduction, so red_bar[1] is free for issuer 1).
+    const int half = static_cast<int>(warp) - Tr::kMmaWarp;
+    uint64_t* my_drain = half == 0 ? drain_bar : &red_bar[1];
     if (lane == 0) {
-      const uint32_t idesc = make_idesc_e4m3_f32(Tr::kMmaM, static_cast<uint32_t>(p.n_mma));
+      const uint32_t idesc = Tr::kSwap ? make_idesc_e4m3_f32(Tr::kMmaM, 16u)
+                                       : make_idesc_e4m3_f32(Tr::kMmaM, static_cast<uint32_t>(p.n_mma));
       const uint32_t w_sub_bytes = static_cast<uint32_t>(p.block_n) * kKBlock;
-      const uint32_t a_sub_bytes = static_cast<uint32_t>(Tr::kMmaM) * kKBlock;
+      const uint32_t a_sub_bytes = static_cast<uint32_t>(Tr::kActRows) * kKBlock;
       const uint32_t w_base = smem_addr(w_region);
       const uint32_t a_base = smem_addr(a_region);
       bool any_issued = false;
@@ -1338,14 +1579,28 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
             break;
           }
           tc_fence_after();
-          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * Tr::kBnMax);
-          // A = activation rows (MMA M side), B = weight rows (MMA N side).
           const uint32_t a_addr = a_base + slot * p.a_stage_bytes + s * a_sub_bytes;
           const uint32_t b_addr = w_base + slot * p.w_stage_bytes + s * w_sub_bytes;
+          if constexpr (Tr::kSwap) {
+            // A = this half's 128 weight rows (MMA M side), B = the batch
+            // rows (MMA N side).  block_n - 128 is a multiple of 8 rows, so
+            // half 1 starts on a 1 KiB swizzle-atom boundary.
+            const uint32_t d_tmem =
+                tmem_base + static_cast<uint32_t>(buf * Tr::kBnMax + half * Tr::kMmaN);
+            const uint32_t w_half = b_addr + static_cast<uint32_t>(half * (p.block_n - Tr::kMmaM) * kKBlock);
 #pragma unroll
-          for (int k = 0; k < kKBlock / 32; ++k) {
-            mma_f8f6f4(d_tmem, make_desc_k_sw128(a_addr + 32u * k),
-                       make_desc_k_sw128(b_addr + 32u * k), idesc, k > 0 ? 1u : 0u);
+            for (int k = 0; k < kKBlock / 32; ++k) {
+              mma_f8f6f4(d_tmem, make_desc_k_sw128(w_half + 32u * k),
+                         make_desc_k_sw128(a_addr + 32u * k), idesc, k > 0 ? 1u : 0u);
+            }
+          } else {
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * Tr::kBnMax);
+            // A = activation rows (MMA M side), B = weight rows (MMA N side).
+#pragma unroll
+            for (int k = 0; k < kKBlock / 32; ++k) {
+              mma_f8f6f4(d_tmem, make_desc_k_sw128(a_addr + 32u * k),
+                         make_desc_k_sw128(b_addr + 32u * k), idesc, k > 0 ? 1u : 0u);
+            }
           }
           any_issued = true;
           mma_commit(&accum_full[buf]);
@@ -1354,8 +1609,8 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         mma_commit(&empty_bar[slot]);
       }
       if (*abort_flag != 0 && any_issued) {
-        mma_commit(drain_bar);
-        if (!wait_for_completion(drain_bar, 0, timeout) && p.status != nullptr)
+        mma_commit(my_drain);
+        if (!wait_for_completion(my_drain, 0, timeout) && p.status != nullptr)
           atomicCAS(p.status, 0, kErrDrainMma);
       }
     }
@@ -1369,6 +1624,9 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   }
   } else {
     // ======================================================== EPILOGUE ====
+    if constexpr (Tr::kSwap) {
+      swap_epilogue<Tr>(p, tmem_base, accum_full, accum_empty, abort_flag, wrote_output, w_region, u_begin, u_end);
+    } else {
     if constexpr (Tr::kRegRealloc) regs_increase<kEpiRegs>();
     const int M = p.M;
     const int N = p.N;
@@ -1584,42 +1842,13 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
         reduce_split_tiles<Tr::kRedGroups>(p, split_tile, split_contrib, n_split, completed, leader,
                                            active_tid, static_cast<int>(epi_threads), ws_vec, out_vec, smem,
                                            p.w_region_bytes + p.a_region_bytes, red_bar, red_mailbox, abort_flag);
-      if (p.flags & kFlagCluster) {
-        const int tile = static_cast<int>(blockIdx.x);
-        // Independent inputs: reduce before waiting on the preceding grid
-        // when this thread's units fit in registers.
-        const bool quant = (p.flags & kFlagQuantizeOut) != 0;
-        const bool defer = !waited && !quant && !(p.flags & kFlagGatherLines) &&
-                           cluster_units_per_thread(p, tile, static_cast<int>(epi_threads)) <= Tr::kDeferUnits;
-        if (!waited && !defer) griddep_wait();   // a CTA without units still stores its share
-        cluster_sync_acq_rel();        // every partial of the tile is in place
-        if (defer) {
-          uint2 staged[Tr::kDeferUnits];
-          const bool live = *abort_flag == 0;
-          if (live)
-            cluster_sum_units<Tr::kDeferUnits>(p, smem_addr(w_region), tile, active_tid, static_cast<int>(epi_threads),
-                                               staged);
-          cluster_sync_acq_rel();      // no peer reads this CTA's partial any more
-          griddep_wait();              // the stores follow the preceding grid
-          if (live) {
-            if (leader) *wrote_output = 1;
-            cluster_store_units<Tr::kDeferUnits>(p, tile, active_tid, static_cast<int>(epi_threads), out_vec, staged);
-          }
-        } else {
-          if (*abort_flag == 0) {
-            if (leader) *wrote_output = 1;
-            if (quant)
-              cluster_reduce_tile_quant(p, smem_addr(w_region), tile, active_tid / 32, active_tid & 31,
-                                        static_cast<int>(epi_threads) / 32);
-            else
-              cluster_reduce_tile(p, smem_addr(w_region), tile, active_tid, static_cast<int>(epi_threads), out_vec);
-          }
-          cluster_sync_acq_rel();      // no peer reads this CTA's partial any more
-        }
-      }
+      if (p.flags & kFlagCluster)
+        cluster_epilogue<Tr>(p, w_region, waited, active_tid, static_cast<int>(epi_threads), leader, out_vec,
+                             abort_flag, wrote_output);
     } else if (p.flags & kFlagCluster) {
       cluster_sync_acq_rel();
       cluster_sync_acq_rel();
+    }
     }
   }
 
@@ -1640,6 +1869,19 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   } else if (p.world > 1 && threadIdx.x == 0) {
     gather_complete(p, *wrote_output != 0);
   }
+}
+
+// The swap-AB batch class (Tr = SwapTraits: M <= 16, 256-row tiles).
+template <class Tr>
+__global__ void __launch_bounds__(Tr::kThreads, 1)
+    dg_decode_gemm_swap_kernel(const __grid_constant__ KernelParams p,
+                               const __grid_constant__ CUtensorMap w_map,
+                               const __grid_constant__ CUtensorMap a_map) {
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
+  decode_gemm_body<Tr>(p, &w_map, &a_map);
+#else
+  if (threadIdx.x == 0 && p.status != nullptr) atomicCAS(p.status, 0, kErrBadLaunchShape);
+#endif
 }
 
 template <int MMA_M, int COPIES, int EPW>

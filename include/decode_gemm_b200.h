@@ -57,7 +57,7 @@
 extern "C" {
 #endif
 
-#define DG_ABI_VERSION 8
+#define DG_ABI_VERSION 9
 
 /* Weight layouts. */
 #define DG_LAYOUT_RAW 0             /* W[N,K], K contiguous (checkpoint layout) */
@@ -83,6 +83,14 @@ extern "C" {
                                         batch copies; 64, 128: MMA M 128 with 2, 1),
                                         as the
                                         C++ header's fp8_decode_gemm<Cfg> is compiled */
+#define DG_FLAG_SWAP_AB 512          /* (new) swap-AB batch class for M <= 16: the weights
+                                        on the MMA's M side (tcgen05.mma M = 128 weight
+                                        rows x N = 16 batch rows, two MMAs from two
+                                        issuing warps per tile), a quarter of the
+                                        multiply-adds per weight byte of the default
+                                        M <= 16 class; needs block_n in [136, 256] and
+                                        grid_ctas DG_GRID_CLUSTER
+                                        (dg_plan reports mma_m 128, n_mma 16) */
 
 /* Device status codes written to dg_problem.status (first error wins). */
 #define DG_STATUS_OK 0

@@ -1,6 +1,7 @@
 """CPU tests of the C ABI library and the host logic (no kernel launches)."""
 
 import ctypes
+from dataclasses import replace
 import os
 import re
 
@@ -134,6 +135,41 @@ def test_plan_rejections():
     assert "block_n" in B(m_tile=8, block_n=12).validate(1, 256, 512)
     assert "227" in B(m_tile=128, subs=4, stages=16).validate(128, 256, 4096)
     assert "epi_warps" in B(m_tile=8, epi_warps=5).validate(1, 256, 512)
+
+
+@pytest.mark.parametrize("m", [1, 4, 16])
+@pytest.mark.parametrize("independent", [False, True])
+@pytest.mark.parametrize("n,k", [(7168, 16384), (16384, 7168), (2048, 4096), (896, 16384)])
+def test_swap_ab_plans(m, n, k, independent):
+    """The swap-AB class (FLAG_SWAP_AB): tcgen05.mma M = 128 weight rows x
+    N = 16 batch rows, 7 warps (4 epilogue, producer, two MMA issuers), the
+    cluster schedule with the split and tile width the default class gets
+    for dependent launches, no workspace, one wave, within 227 KiB."""
+    sw = dg.default_config(m, n, k, layout=dg.LAYOUT_PACKED_SWIZZLED, independent_inputs=independent, swap_ab=True)
+    assert sw.flags & dg.FLAG_SWAP_AB and sw.grid_ctas == dg.GRID_CLUSTER
+    p = sw.plan(m, n, k)
+    assert p.error is None, p.error
+    assert (p.mma_m, p.n_mma, p.block[0], p.epi_warps) == (128, 16, 224, 4)
+    assert p.ws_floats == 0 and p.sem_ints == 0
+    assert p.smem_bytes <= dg.MAX_DYNAMIC_SMEM
+    assert 136 <= sw.block_n <= 256 and sw.block_n % 8 == 0
+    assert p.grid[0] * p.grid[1] <= 148
+    if not independent:
+        d = dg.default_config(m, n, k, layout=dg.LAYOUT_PACKED_SWIZZLED, independent_inputs=False)
+        pd = d.plan(m, n, k)
+        assert (sw.block_n, p.grid) == (d.block_n, pd.grid)
+        assert p.stages >= pd.stages
+
+
+def test_swap_ab_plan_rejections():
+    sw = dg.default_config(8, 2048, 4096, layout=dg.LAYOUT_RAW, swap_ab=True)
+    assert "M must be <= 16" in replace(sw, m_tile=32).validate(17, 2048, 4096)
+    assert "block_n" in replace(sw, block_n=128).validate(8, 2048, 4096)
+    assert "cluster" in replace(sw, grid_ctas=-1).validate(8, 2048, 4096)
+    with pytest.raises(ValueError):
+        dg.default_config(17, 2048, 4096, swap_ab=True)
+    with pytest.raises(ValueError):
+        dg.default_config(8, 2048, 4096, schedule="stream_k", swap_ab=True)
 
 
 def test_launch_rejections_need_no_gpu():

@@ -54,7 +54,7 @@ class Chain:
     """Weights of `layers` layers alternating (n, k) and (k, n), their
     configurations, plans and packed copies."""
 
-    def __init__(self, m, n, k, layers, seed):
+    def __init__(self, m, n, k, layers, seed, swap_ab=False):
         self.m = m
         self.shapes = [(n, k) if i % 2 == 0 else (k, n) for i in range(layers)]
         self.dev = torch.device("cuda")
@@ -63,7 +63,8 @@ class Chain:
         for (nn, kk) in self.shapes:
             # 1/sqrt(K) keeps every layer's output the size of its input.
             q, s = quantize_blocks(torch.randn((nn, kk), device=self.dev, generator=g) / kk ** 0.5)
-            cfg = dg.default_config(m, nn, kk, layout=dg.LAYOUT_PACKED_SWIZZLED, pdl=True, independent_inputs=False)
+            cfg = dg.default_config(m, nn, kk, layout=dg.LAYOUT_PACKED_SWIZZLED, pdl=True, independent_inputs=False,
+                                    swap_ab=swap_ab)
             self.w_raw.append(q)
             self.w_sc.append(s)
             self.w_packed.append(dg.prepack_weight(q, cfg.block_n, cfg.layout))
@@ -115,10 +116,12 @@ def run_graph(stream, graph):
     torch.cuda.synchronize()
 
 
-@pytest.mark.parametrize("m,n,k,layers", [(1, 7168, 16384, 8), (8, 7168, 16384, 6), (32, 7168, 16384, 4),
-                                          (128, 2048, 4096, 6)])
-def test_pdl_chain_in_graph_matches_oracle_layer_by_layer(m, n, k, layers):
-    ch = Chain(m, n, k, layers, seed=4242 + m)
+@pytest.mark.parametrize("m,n,k,layers,swap_ab", [(1, 7168, 16384, 8, False), (8, 7168, 16384, 6, False),
+                                                  (32, 7168, 16384, 4, False), (128, 2048, 4096, 6, False),
+                                                  (1, 7168, 16384, 8, True), (16, 2048, 4096, 6, True)])
+def test_pdl_chain_in_graph_matches_oracle_layer_by_layer(m, n, k, layers, swap_ab):
+    """swap_ab: every layer on the swap-AB batch class (FLAG_SWAP_AB)."""
+    ch = Chain(m, n, k, layers, seed=4242 + m, swap_ab=swap_ab)
     total = 2 * layers                       # two passes over the layer list
     order = [i % layers for i in range(total)]
     widths = [ch.shapes[li][1] for li in order] + [ch.shapes[order[-1]][0]]
