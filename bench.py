@@ -73,9 +73,10 @@ def parse_args():
                          "timed; this picks the headline.")
     ap.add_argument("--schedule", choices=["cluster", "stream_k"], default="cluster",
                     help="default_config's schedule: cluster split-K (default) or stream-K over one CTA per SM")
-    ap.add_argument("--batch-class", choices=["default", "swap_ab"], default="default",
-                    help="kernel class for M <= 16 on the cluster schedule: the default (batch on the MMA's M "
-                         "side, padded to 64) or swap-AB (weights on the M side, batch padded to 16 on N)")
+    ap.add_argument("--batch-class", choices=["auto", "default", "swap_ab"], default="auto",
+                    help="kernel class for M <= 16 on the cluster schedule: auto (default_config's measured "
+                         "choice), the default class (batch on the MMA's M side, padded to 64) or swap-AB "
+                         "(weights on the M side, batch padded to 16 on N)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-depth", type=int, default=4,
                     help="e2e loop on 1 GPU: requests in flight, one stream each (1: no pipelined loop)")
@@ -352,6 +353,8 @@ def b200_arm(args, rank, world, local_rank):
     def default_config(*a, **kw):
         if args.batch_class == "swap_ab" and a[0] <= 16 and args.schedule == "cluster":
             kw.setdefault("swap_ab", True)
+        elif args.batch_class == "default":
+            kw.setdefault("swap_ab", False)
         return dg.default_config(*a, schedule=args.schedule, **kw)
 
     stream = torch.cuda.Stream(device=dev)
@@ -494,7 +497,7 @@ def b200_arm(args, rank, world, local_rank):
     value = byt_job / (t_gemm / K) / 1e9
     peak, peak_kind = measured_peaks()
     achieved = byt_gpu / (t_gemm / K) / 1e9
-    workload_key = f"N{n}_K{k}_M{m}_{args.layout}"
+    workload_key = f"N{n}_K{k}_M{m}_{args.layout}" + ("_swap_ab" if cfg.flags & dg.FLAG_SWAP_AB else "")
 
     # ---- multi-GPU: with the NCCL gather, and the strong-scaling layer ---------
     tp = None

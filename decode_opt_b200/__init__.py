@@ -139,7 +139,7 @@ class B200Config:
 
 def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool = True,
                    independent_inputs: bool = False, schedule: str = "cluster",
-                   quantized_output: bool = False, swap_ab: bool = False) -> B200Config:
+                   quantized_output: bool = False, swap_ab: Optional[bool] = None) -> B200Config:
     """The B200 schedule used by :func:`fp8_decode_gemm` and the benchmark.
 
     Two 128-K blocks per stage and weight tiles on the tcgen05 N side, 256
@@ -166,12 +166,39 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
     :func:`launch_quantized` accepts: the cluster schedule on 256-row tiles
     (whole 128-column quantisation blocks per tile) with at least two CTAs
     per tile; ValueError where the cluster plan does not apply or N is not a
-    multiple of 128.  `swap_ab` (M <= 16, cluster schedule) selects the
-    swap-AB batch class (FLAG_SWAP_AB): the weights on the MMA's M side, 128
-    rows per tcgen05.mma, the batch padded to 16 on its N side, with the
-    tile width and split chosen as above; ValueError where it does not apply.
+    multiple of 128.
+
+    `swap_ab` picks the batch class for M <= 16.  True: the swap-AB class
+    (FLAG_SWAP_AB: the weights on the MMA's M side, 128 rows per
+    tcgen05.mma, the batch padded to 16 on its N side, a quarter of the
+    multiply-adds per weight byte) with the tile width and split chosen as
+    above, ValueError where it does not apply; False: the default class
+    (batch on the M side, padded to 64); None (default): the faster of the
+    two as measured at C2 on B200 -- swap-AB for independent inputs (256-row
+    tiles, 56 CTAs with 192 KiB in flight each: 16.3 against 17.4 us per
+    GEMM over 1,000 launches, 17.3 against 19.4 over 10,000 where the power
+    limit lowers the clock) and for quantised output (three 64 KiB stages
+    where the default class fits two: 22.8 against 23.9 us per layer of the
+    61-layer chain); for dependent launches the default class (22.5 against
+    23.3 us at 224-row tiles) unless its plan takes 256-row tiles, where the
+    swap class keeps a third stage.  Only cluster plans with at least two
+    CTAs per tile are switched.
     """
     from dataclasses import replace
+    if swap_ab is None:
+        plain = default_config(m, n, k, layout=layout, pdl=pdl, independent_inputs=independent_inputs,
+                               schedule=schedule, quantized_output=quantized_output, swap_ab=False)
+        if m > 16 or schedule != "cluster" or plain.grid_ctas != GRID_CLUSTER:
+            return plain
+        if not (independent_inputs or quantized_output or plain.block_n == 256):
+            return plain
+        try:
+            sw = default_config(m, n, k, layout=layout, pdl=pdl, independent_inputs=independent_inputs,
+                                schedule=schedule, quantized_output=quantized_output, swap_ab=True)
+        except ValueError:
+            return plain
+        psw = sw.plan(m, n, k)
+        return sw if psw.error is None and psw.cluster >= 2 and sw.block_n == 256 else plain
     flags = FLAG_INDEPENDENT_INPUTS if independent_inputs else 0
     stream_k = B200Config(m_tile=m_tile_for(m), block_n=256, subs=2, stages=2, layout=layout, pdl=pdl,
                           split_k=1, grid_ctas=-1, flags=flags)

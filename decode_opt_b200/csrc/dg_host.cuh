@@ -173,9 +173,14 @@ __host__ __device__ constexpr uint32_t align1k(uint32_t v) { return (v + 1023u) 
 // (stages x subs x block_n x 128 bytes, plus the MMA's read-ahead pad when
 // block_n is not a multiple of 16), the activation ring (stages x subs x
 // MMA-M rows x 128 bytes) and the barrier block.
-__host__ __device__ constexpr uint32_t pipeline_smem_bytes(int stages, int subs, int block_n, int mma_m) {
+// mma_rows: weight rows the MMA reads per 128-K block (0: block_n rounded up
+// to 16; the swap-AB class reads two 128-row halves); the rows past block_n
+// of the ring's last block come from a tail pad.
+__host__ __device__ constexpr uint32_t pipeline_smem_bytes(int stages, int subs, int block_n, int mma_m,
+                                                           int mma_rows = 0) {
   return 1024u +
-         align1k(static_cast<uint32_t>(stages * subs * block_n * kKBlock + (((block_n + 15) / 16) * 16 - block_n) * kKBlock)) +
+         align1k(static_cast<uint32_t>(stages * subs * block_n * kKBlock +
+                                       ((mma_rows > 0 ? mma_rows : ((block_n + 15) / 16) * 16) - block_n) * kKBlock)) +
          align1k(static_cast<uint32_t>(stages * subs * mma_m * kKBlock)) + SmemBarriers::bytes(stages, kAccumBuffers);
 }
 
@@ -263,12 +268,16 @@ __host__ __device__ inline Plan make_plan(const Config& c, int M, int N, int K, 
   const uint32_t w_stage = static_cast<uint32_t>(c.subs * c.block_n * kKBlock);
   const uint32_t a_stage = static_cast<uint32_t>(c.subs * act_rows * kKBlock);
   const uint32_t a_tx = static_cast<uint32_t>(c.subs * copies * a_rows * kKBlock);
-  // The MMA reads n_mma weight rows from each 128-K block; rows past those
-  // loaded come from the next block or this tail pad and only feed output
-  // columns that are never stored.  (The swap class reads exactly block_n.)
-  const uint32_t w_pad = bc.swap ? 0u : static_cast<uint32_t>((n_mma - c.block_n) * kKBlock);
+  // The MMA reads n_mma weight rows from each 128-K block (the swap class:
+  // two 128-row halves, 256 rows); rows past those loaded come from the next
+  // block or this tail pad and only feed output columns that are never
+  // stored.
+  const int mma_rows = bc.swap ? 2 * SwapTraits::kMmaM : n_mma;
+  const uint32_t w_pad = static_cast<uint32_t>((mma_rows - c.block_n) * kKBlock);
   (void)bufs;
-  auto smem_for = [&](int stages) -> uint32_t { return pipeline_smem_bytes(stages, c.subs, c.block_n, act_rows); };
+  auto smem_for = [&](int stages) -> uint32_t {
+    return pipeline_smem_bytes(stages, c.subs, c.block_n, act_rows, mma_rows);
+  };
   int stages = c.stages;
   if (stages == 0) {
     stages = 1;

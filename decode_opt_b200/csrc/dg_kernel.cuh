@@ -292,13 +292,15 @@ struct KernelTraits {
 // 16 instead of padding the batch to 64 rows: a quarter of the multiply-adds
 // per weight byte of the M = 64 class, and with them the tensor pipe's power
 // draw.  A tile of block_n = 136..256 rows is covered by two 128-row halves,
-// rows [0, 128) and [block_n - 128, block_n) (they overlap for block_n < 256;
-// the overlap is folded once); two MMA warps issue one half each into their
+// rows [0, 128) and [128, 256): below 256 rows the second half also reads
+// the 256 - block_n rows after the tile (the next block of the ring, or its
+// tail pad), whose accumulator lanes are never folded; two MMA warps issue one half each into their
 // own 16 accumulator columns (one issuing thread needs ~72 cycles per MMA,
 // two bring the pair to ~39 each, so a 128-K block takes ~4 x 78 cycles
 // against 448 for the M = 64 x N = 224 class).  TMEM lane = row within a
 // half, column = batch row: epilogue warp q folds lanes 32q..32q+31 of both
-// halves, 2 x 16 values per thread, and writes them transposed into the same
+// halves (of half 1 only the rows inside the tile), 2 x 16 values per thread,
+// and writes them transposed into the same
 // [M][block_n] shared-memory partial the cluster reduction of the other
 // classes reads.
 struct SwapTraits {
@@ -1233,8 +1235,8 @@ __device__ __forceinline__ void cluster_epilogue(const KernelParams& p, uint8_t*
 
 // Epilogue of the swap-AB class (SwapTraits), run by its four epilogue warps.
 // Warp q reads TMEM lane quarter q: thread (q, lane) holds tile rows (output
-// columns) r = 32q + lane and h1 + r (h1 = block_n - 128; only where that row
-// is not also in half 0, h1 + r >= 128), each for the 16 batch rows in the
+// columns) r = 32q + lane and 128 + r (only where that row is inside the
+// tile, 128 + r < block_n), each for the 16 batch rows in the
 // accumulator's columns, and folds every 128-K block with the other classes'
 // arithmetic (combined = w_s * a_s, then one fma per element), each row with
 // the weight scale of its own 128-row group.  Under cluster split-K the
@@ -1255,8 +1257,8 @@ __device__ __forceinline__ void swap_epilogue(const KernelParams& p, uint32_t tm
   const int bn = p.block_n;
   const int C = p.chunks_per_tile;
   const int r = static_cast<int>(warp * 32u + lane);   // tile row in half 0
-  const int h1 = bn - Tr::kMmaM;                       // first tile row of half 1
-  const bool has1 = h1 + r >= Tr::kMmaM;               // half 1's row is not in half 0
+  const int h1 = Tr::kMmaM;                            // first tile row of half 1
+  const bool has1 = h1 + r < bn;                       // half 1's row is inside the tile
   const uint32_t t_lane = tmem_base + ((warp * 32u) << 16);
   const bool leader = threadIdx.x == 0;
   const bool cluster = (p.flags & kFlagCluster) != 0;
@@ -1539,8 +1541,8 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
   } else if (warp >= static_cast<uint32_t>(Tr::kMmaWarp) &&
              warp < static_cast<uint32_t>(Tr::kMmaWarp + Tr::kMmaIssuers)) {
     // ============================================================= MMA ====
-    // Swap-AB: issuer `half` multiplies tile rows [half (block_n - 128),
-    // + 128) into accumulator columns [16 half, 16 half + 16) of each buffer; the
+    // Swap-AB: issuer `half` multiplies tile rows [128 half, 128 half + 128)
+    // into accumulator columns [16 half, 16 half + 16) of each buffer; the
     // ring and accumulator barriers count one commit per issuer.  It drains
     // its own MMAs after an abort on its own barrier (the swap class has no
     // workspace reduction, so red_bar[1] is free for issuer 1).
@@ -1583,11 +1585,12 @@ __device__ __forceinline__ void decode_gemm_body(const KernelParams& p,
           const uint32_t b_addr = w_base + slot * p.w_stage_bytes + s * w_sub_bytes;
           if constexpr (Tr::kSwap) {
             // A = this half's 128 weight rows (MMA M side), B = the batch
-            // rows (MMA N side).  block_n - 128 is a multiple of 8 rows, so
-            // half 1 starts on a 1 KiB swizzle-atom boundary.
+            // rows (MMA N side).  Rows past the tile (block_n < 256) come
+            // from the next block of the ring or its tail pad and only feed
+            // accumulator lanes the epilogue never folds.
             const uint32_t d_tmem =
                 tmem_base + static_cast<uint32_t>(buf * Tr::kBnMax + half * Tr::kMmaN);
-            const uint32_t w_half = b_addr + static_cast<uint32_t>(half * (p.block_n - Tr::kMmaM) * kKBlock);
+            const uint32_t w_half = b_addr + static_cast<uint32_t>(half * Tr::kMmaM * kKBlock);
 #pragma unroll
             for (int k = 0; k < kKBlock / 32; ++k) {
               mma_f8f6f4(d_tmem, make_desc_k_sw128(w_half + 32u * k),

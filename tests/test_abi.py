@@ -82,18 +82,25 @@ def test_status_strings():
 def test_default_plan_c2_cluster(m):
     """Default schedule (no GPU: the measured B200 cluster occupancy): cluster
     split-K, 224-row tiles x 4 K-splits = 128 CTAs in one wave for dependent
-    launches; for independent inputs 2 K-splits, 224-row tiles where they
-    allow three ring stages (M <= 32, MMA M 64), else 256; no workspace."""
+    launches (the default batch class); for independent inputs 2 K-splits:
+    M <= 16 the swap-AB class on 256-row tiles (three 64 KiB stages), M = 32
+    224-row tiles (three ring stages, MMA M 64), else 256; no workspace."""
     c = dg.default_config(m, 7168, 16384)
     p = c.plan(m, 7168, 16384)
     assert p.error is None and c.grid_ctas == dg.GRID_CLUSTER and c.block_n == 224
+    assert not c.flags & dg.FLAG_SWAP_AB
     assert p.cluster == 4 and p.grid == (32, 4, 1) and p.num_ctas == 128 and p.n_mma == 224
     assert p.stages == (3 if m <= 32 else 2)
     assert p.ws_floats == 0 and p.sem_ints == 0 and p.max_slabs == 1
     ci = dg.default_config(m, 7168, 16384, independent_inputs=True)
     pi = ci.plan(m, 7168, 16384)
-    assert ci.block_n == (224 if m <= 32 else 256) and pi.cluster == 2
-    assert pi.num_ctas == (64 if m <= 32 else 56)
+    assert bool(ci.flags & dg.FLAG_SWAP_AB) == (m <= 16)
+    assert ci.block_n == (224 if m == 32 else 256) and pi.cluster == 2
+    assert pi.num_ctas == (64 if m == 32 else 56)
+    if m <= 16:
+        assert (pi.mma_m, pi.n_mma, pi.stages) == (128, 16, 3)
+    assert dg.default_config(m, 7168, 16384, independent_inputs=True, swap_ab=False).block_n == (
+        224 if m <= 32 else 256)
     # a small matrix: 16 chunks per tile, so 8 CTAs per tile (two chunks
     # each) rather than the ragged 10; 10 ragged 224-row tiles stream
     # 224 x 2 rows-chunks per CTA against 256 x 2
@@ -108,6 +115,8 @@ def test_default_plan_c2_cluster(m):
     c2 = dg.default_config(m, 3584, 16384)
     s2 = c2.plan(m, 3584, 16384)
     assert c2.block_n == 256 and s2.cluster == 8 and s2.num_ctas == 112
+    # there the default class fits two 64 KiB stages, the swap-AB class three
+    assert bool(c2.flags & dg.FLAG_SWAP_AB) == (m <= 16) and s2.stages == (3 if m <= 16 else 2)
 
 
 @pytest.mark.parametrize("m", [1, 8, 16, 32, 64, 128])
@@ -308,8 +317,15 @@ def test_default_plans_follow_the_split_rule(n, k, m, independent):
     assert tiles <= B200_CLUSTER_OCC[p.cluster]                  # one wave of clusters
     assert p.ws_floats == 0 and p.sem_ints == 0
     assert p.stages >= 2 and p.smem_bytes <= 227 * 1024
-    assert p.mma_m == (64 if m <= 32 else 128)
-    assert p.block[0] == (192 if m <= 16 else 320 if m <= 64 else 384)
+    if c.flags & dg.FLAG_SWAP_AB:
+        # swap-AB (M <= 16; independent inputs, or a 256-row dependent plan):
+        # MMA M = 128 weight rows x N = 16 batch rows, 7 warps
+        assert m <= 16 and c.block_n == 256 and (independent or p.stages == 3)
+        assert (p.mma_m, p.n_mma, p.block[0]) == (128, 16, 224)
+    else:
+        assert not (independent and m <= 16)
+        assert p.mma_m == (64 if m <= 32 else 128)
+        assert p.block[0] == (192 if m <= 16 else 320 if m <= 64 else 384)
     if independent:
         assert p.num_ctas >= 32 or p.cluster == min(chunks, 8)
 
