@@ -78,8 +78,9 @@ def parse_args():
                          "choice), the default class (batch on the MMA's M side, padded to 64) or swap-AB "
                          "(weights on the M side, batch padded to 16 on N)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--e2e-depth", type=int, default=4,
-                    help="e2e loop on 1 GPU: requests in flight, one stream each (1: no pipelined loop)")
+    ap.add_argument("--e2e-depth", type=int, default=8,
+                    help="e2e loop on 1 GPU: requests in flight, one stream each (1: no pipelined loop); "
+                         "the independent schedule's 28-CTA GEMMs need about five in flight to fill the GPU")
     ap.add_argument("--e2e-group", type=int, default=16,
                     help="e2e loop on N GPUs: fused GEMMs per group that chain under PDL, the group's "
                          "first waiting on the copy streams (1: no pipelined loop)")
@@ -433,6 +434,15 @@ def b200_arm(args, rank, world, local_rank):
             rotations[key] = Rotation(qw, layout, block_n, dev)
         return rotations[key]
 
+    def lines_ready(setup, mm, nn, rot_fn, qx_m, ws_m, as_m, indep):
+        """A setup the tagged-lines gather accepts: `setup` itself where its
+        plan splits every tile over at least two CTAs (the gather stores from
+        the cluster reduction), else one on default_config(gather_lines=True)."""
+        if setup.plan.cluster >= 2:
+            return setup
+        cfg_l = default_config(mm, nn, k, layout=layout, pdl=pdl, independent_inputs=indep, gather_lines=True)
+        return GemmSetup(rot_fn(cfg_l.block_n), cfg_l, mm, qx_m, ws_m, as_m, dev)
+
     # The headline mode's schedule and the other PDL mode's, each with its own
     # weight copies (packed for its tile width) and tensor maps.
     cfg = default_config(m, n, k, layout=layout, pdl=pdl, independent_inputs=independent)
@@ -509,10 +519,13 @@ def b200_arm(args, rank, world, local_rank):
         del graphs
         # The all-gather fused into the GEMM: every rank stores its slices into
         # all ranks' gathered buffers over NVLink (two buffer sets alternate).
+        # Both protocols run on one setup that the tagged-lines gather accepts
+        # (at least two CTAs per tile), so their outputs can be compared.
+        gs_g = lines_ready(gs, m, n, rotation, qx, wscale, ascale, independent)
         fused = dg_tp.FusedGather(m, n, device=dev)
         fdesc = [fused.descriptor(0), fused.descriptor(1)]
 
-        def fused_step(i, setup=gs):
+        def fused_step(i, setup=gs_g):
             rc = dg.launch_gather(setup.cfg, setup.probs[i % setup.nsets], fdesc[i % 2],
                                   setup.wmaps[i % setup.nsets], setup.amap, stream, pdl_attr=setup.cfg.pdl)
             if rc != 0:
@@ -520,24 +533,24 @@ def b200_arm(args, rank, world, local_rank):
         def fused_steps(i):
             fused_step(i)
             if i == K2 - 1:      # the last launch's gather completes inside the timed region
-                fused.wait((K2 - 1) % 2, stream=stream, status=gs.status)
+                fused.wait((K2 - 1) % 2, stream=stream, status=gs_g.status)
         graphs = capture(fused_steps, K2)
         t_fused = timed(graphs)
         del graphs
-        gs.check_status()
+        gs_g.check_status()
         # The same with the gather in tagged lines (no flags, no fences).
         fused_l = dg_tp.FusedGather(m, n, device=dev, protocol="lines")
         ldesc = [fused_l.descriptor(0), fused_l.descriptor(1)]
 
         def lines_steps(i):
-            rc = dg.launch_gather(gs.cfg, gs.probs[i % gs.nsets], ldesc[i % 2], gs.wmaps[i % gs.nsets], gs.amap,
-                                  stream, pdl_attr=gs.cfg.pdl)
+            rc = dg.launch_gather(gs_g.cfg, gs_g.probs[i % gs_g.nsets], ldesc[i % 2], gs_g.wmaps[i % gs_g.nsets],
+                                  gs_g.amap, stream, pdl_attr=gs_g.cfg.pdl)
             if rc != 0:
                 raise RuntimeError(f"fused launch (lines) failed: cudaError {rc}")
         graphs = capture(lines_steps, K2)
         t_fused_l = timed(graphs)
         del graphs
-        gs.check_status()
+        gs_g.check_status()
         # Both protocols gathered the same product of the same inputs.
         lines_match = bool(torch.equal(fused_l.output((K2 - 1) % 2, m).view(torch.int16),
                                        fused.output((K2 - 1) % 2, m).view(torch.int16)))
@@ -579,19 +592,20 @@ def b200_arm(args, rank, world, local_rank):
                 graphs = capture(strong_tp, K)
                 t_s_tp = timed(graphs)
                 del graphs
+                gs_sg = lines_ready(gs_s, mm, n_s, rot_for, qx_m, ws_s, ascale_m, independent)
                 fused_s = dg_tp.FusedGather(mm, n_s, device=dev)
                 fdesc_s = [fused_s.descriptor(0), fused_s.descriptor(1)]
 
                 def strong_fused(i):
-                    rc = dg.launch_gather(gs_s.cfg, gs_s.probs[i % gs_s.nsets], fdesc_s[i % 2],
-                                          gs_s.wmaps[i % gs_s.nsets], gs_s.amap, stream, pdl_attr=gs_s.cfg.pdl)
+                    rc = dg.launch_gather(gs_sg.cfg, gs_sg.probs[i % gs_sg.nsets], fdesc_s[i % 2],
+                                          gs_sg.wmaps[i % gs_sg.nsets], gs_sg.amap, stream, pdl_attr=gs_sg.cfg.pdl)
                     if rc != 0:
                         raise RuntimeError(f"fused launch failed: cudaError {rc}")
 
                 def strong_fused_steps(i):
                     strong_fused(i)
                     if i == K2 - 1:
-                        fused_s.wait((K2 - 1) % 2, stream=stream, status=gs_s.status)
+                        fused_s.wait((K2 - 1) % 2, stream=stream, status=gs_sg.status)
                 graphs = capture(strong_fused_steps, K2)
                 t_s_fused = timed(graphs)
                 del graphs
@@ -599,8 +613,8 @@ def b200_arm(args, rank, world, local_rank):
                 ldesc_s = [fused_sl.descriptor(0), fused_sl.descriptor(1)]
 
                 def strong_lines(i):
-                    rc = dg.launch_gather(gs_s.cfg, gs_s.probs[i % gs_s.nsets], ldesc_s[i % 2],
-                                          gs_s.wmaps[i % gs_s.nsets], gs_s.amap, stream, pdl_attr=gs_s.cfg.pdl)
+                    rc = dg.launch_gather(gs_sg.cfg, gs_sg.probs[i % gs_sg.nsets], ldesc_s[i % 2],
+                                          gs_sg.wmaps[i % gs_sg.nsets], gs_sg.amap, stream, pdl_attr=gs_sg.cfg.pdl)
                     if rc != 0:
                         raise RuntimeError(f"fused launch (lines) failed: cudaError {rc}")
                 graphs = capture(strong_lines, K2)
@@ -611,6 +625,7 @@ def b200_arm(args, rank, world, local_rank):
                 fused_sl.close()
                 fused_s.close()
                 gs_s.check_status()
+                gs_sg.check_status()
                 byt_layer = n * k + mm * k + 2 * mm * n
                 return {"M": mm, "N_layer": n, "rows_per_gpu": n_s,
                         "gemm_only": {"us_per_gemm": t_s / K * 1e6, "GBps_job": byt_layer / (t_s / K) / 1e9},
@@ -659,6 +674,8 @@ def b200_arm(args, rank, world, local_rank):
         act_in = dev_in[: m * k].view(m, k)
         sc_in = dev_in[m * k:].view(torch.float32).view(m, kb)
         gs_e2e = GemmSetup(rotation(gs_dep.cfg.block_n), gs_dep.cfg, m, act_in, wscale, sc_in, dev)
+        if world > 1 and args.gather_protocol == "lines":
+            gs_e2e = lines_ready(gs_e2e, m, n, rotation, act_in, wscale, sc_in, False)
         hy = torch.empty((m, world * n), dtype=torch.bfloat16).pin_memory()
 
         fused_e = None
@@ -777,7 +794,8 @@ def b200_arm(args, rank, world, local_rank):
             nset = 2 * grp
             depth = nset
             cfg_p = default_config(m, n, k, layout=layout, pdl=pdl,
-                                      independent_inputs=args.e2e_schedule == "independent")
+                                   independent_inputs=args.e2e_schedule == "independent",
+                                   gather_lines=args.gather_protocol == "lines")
             fused_p = dg_tp.FusedGather(m, n, buffers=nset, device=dev, protocol=args.gather_protocol)
             pdesc = [fused_p.descriptor(j) for j in range(nset)]
             slots = []
@@ -1087,7 +1105,8 @@ def b200_arm(args, rank, world, local_rank):
                 wq, sc_full = full[(nn, kk)]
                 n_loc = nn // world
                 lo = rank * n_loc
-                cfg_l = default_config(m, n_loc, kk, layout=layout, pdl=pdl, independent_inputs=False)
+                cfg_l = default_config(m, n_loc, kk, layout=layout, pdl=pdl, independent_inputs=False,
+                                       gather_lines=True)
                 w_loc = wq[lo:lo + n_loc].contiguous()
                 fg = dg_tp.FusedGather(m, n_loc, device=dev, protocol="lines")
                 desc = [fg.descriptor(j, act_in[nn], act_sc[nn]) if fused_q else fg.descriptor(j) for j in (0, 1)]

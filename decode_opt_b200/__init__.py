@@ -56,6 +56,7 @@ __all__ = [
 CUDA_SUCCESS = 0
 CUDA_ERROR_INVALID_VALUE = 1
 K_BLOCK = 128
+INDEPENDENT_TILE_CTAS = 24     # dg::kIndependentTileCtas: independent inputs run one CTA per tile from here
 MAX_DYNAMIC_SMEM = 227 * 1024
 
 
@@ -139,24 +140,25 @@ class B200Config:
 
 def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool = True,
                    independent_inputs: bool = False, schedule: str = "cluster",
-                   quantized_output: bool = False, swap_ab: Optional[bool] = None) -> B200Config:
+                   quantized_output: bool = False, swap_ab: Optional[bool] = None,
+                   gather_lines: bool = False) -> B200Config:
     """The B200 schedule used by :func:`fp8_decode_gemm` and the benchmark.
 
-    Two 128-K blocks per stage and weight tiles on the tcgen05 N side, 256
-    rows (8 KiB of weights per MMA instruction) unless 224 serves better:
+    Two 128-K blocks per stage and weight tiles of 256 rows unless 224 serves
+    better:
 
     * ``schedule="cluster"`` (default): cluster split-K (``GRID_CLUSTER``):
       each tile's K range split over the CTAs of one thread-block cluster,
       reduced through distributed shared memory; the library picks the split
-      from the device's cluster occupancy (one wave of clusters: the most
-      SMs for dependent launches, with clusters of up to 16 CTAs; 32 CTAs
-      for independent inputs) and the ring as deep as shared memory allows.
-      Dependent launches take the split and tile width (256 or 224 rows)
-      whose busiest CTA streams the least, block_n x ceil(chunks / S)
-      (7168 rows: 32 x 4 CTAs of 224 instead of 28 x 4 of 256; a 3584-row
-      shard: 14 x 8 of 256 instead of 16 x 6 of 224).  Independent inputs take 224
-      rows when 224 divides N and they allow a deeper ring (M <= 16: three
-      56 KiB stages in flight instead of two of 64 KiB).  Falls back to
+      from the device's cluster occupancy (one wave of clusters).  Dependent
+      launches take the split and tile width (256 or 224 rows) whose busiest
+      CTA streams the least, block_n x ceil(chunks / S), with clusters of up
+      to 16 CTAs (7168 rows: 32 x 4 CTAs of 224 instead of 28 x 4 of 256; a
+      3584-row shard: 14 x 8 of 256 instead of 16 x 6 of 224).  Independent
+      inputs take 256-row tiles and one CTA per tile where that gives at
+      least 24 CTAs (no split, no reduction: C2 runs 28 CTAs per GEMM and
+      about five GEMMs stream side by side), else the smallest split giving
+      32 CTAs (224 rows where that allows a deeper ring).  Falls back to
       stream-K where the cluster plan does not apply.
     * ``schedule="stream_k"``: a stream-K grid of one CTA per SM with the
       workspace reduction (two 64 KiB stages).
@@ -164,9 +166,12 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
     `independent_inputs` sets FLAG_INDEPENDENT_INPUTS (see
     include/decode_gemm_b200.h).  `quantized_output` asks for a configuration
     :func:`launch_quantized` accepts: the cluster schedule on 256-row tiles
-    (whole 128-column quantisation blocks per tile) with at least two CTAs
-    per tile; ValueError where the cluster plan does not apply or N is not a
-    multiple of 128.
+    (whole 128-column quantisation blocks per tile) with at least two CTAs per
+    tile; ValueError where the cluster plan does not apply or N is not a
+    multiple of 128.  `gather_lines` asks for one the tagged-lines gather
+    accepts (``FusedGather(protocol="lines")``): the configuration chosen as
+    above with at least two CTAs per tile (the gather stores from the cluster
+    reduction), ValueError where the cluster schedule does not apply.
 
     `swap_ab` picks the batch class for M <= 16.  True: the swap-AB class
     (FLAG_SWAP_AB: the weights on the MMA's M side, 128 rows per
@@ -175,36 +180,50 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
     above, ValueError where it does not apply; False: the default class
     (batch on the M side, padded to 64); None (default): the faster of the
     two as measured at C2 on B200 -- swap-AB for independent inputs (256-row
-    tiles, 56 CTAs with 192 KiB in flight each: 16.3 against 17.4 us per
-    GEMM over 1,000 launches, 17.3 against 19.4 over 10,000 where the power
-    limit lowers the clock) and for quantised output (three 64 KiB stages
-    where the default class fits two: 22.8 against 23.9 us per layer of the
-    61-layer chain); for dependent launches the default class (22.5 against
-    23.3 us at 224-row tiles) unless its plan takes 256-row tiles, where the
-    swap class keeps a third stage.  Only cluster plans with at least two
-    CTAs per tile are switched.
+    tiles with 192 KiB in flight each: 16.3 against 17.4 us per GEMM over
+    1,000 launches at a split of 2, 17.3 against 19.4 over 10,000 where the
+    power limit lowers the clock) and for quantised output (three 64 KiB
+    stages where the default class fits two: 22.8 against 23.9 us per layer
+    of the 61-layer chain); for dependent launches the default class (22.5
+    against 23.3 us at 224-row tiles) unless its plan takes 256-row tiles,
+    where the swap class keeps a third stage.
     """
     from dataclasses import replace
+    if gather_lines and not quantized_output:
+        cfg = default_config(m, n, k, layout=layout, pdl=pdl, independent_inputs=independent_inputs,
+                             schedule=schedule, swap_ab=swap_ab)
+        pl = cfg.plan(m, n, k)
+        if cfg.grid_ctas != GRID_CLUSTER or pl.error is not None:
+            raise ValueError(f"no tagged-lines plan for M={m} N={n} K={k}: needs the cluster schedule ({pl.error})")
+        if pl.cluster < 2:
+            cfg = replace(cfg, split_k=2)
+            err = cfg.plan(m, n, k).error
+            if err is not None:
+                raise ValueError(f"no tagged-lines plan for M={m} N={n} K={k}: {err}")
+        return cfg
+    reduce_in_cluster = quantized_output
     if swap_ab is None:
-        plain = default_config(m, n, k, layout=layout, pdl=pdl, independent_inputs=independent_inputs,
-                               schedule=schedule, quantized_output=quantized_output, swap_ab=False)
+        kw = dict(layout=layout, pdl=pdl, independent_inputs=independent_inputs, schedule=schedule,
+                  quantized_output=quantized_output)
+        plain = default_config(m, n, k, swap_ab=False, **kw)
         if m > 16 or schedule != "cluster" or plain.grid_ctas != GRID_CLUSTER:
             return plain
-        if not (independent_inputs or quantized_output or plain.block_n == 256):
+        if not (independent_inputs or reduce_in_cluster or plain.block_n == 256):
             return plain
         try:
-            sw = default_config(m, n, k, layout=layout, pdl=pdl, independent_inputs=independent_inputs,
-                                schedule=schedule, quantized_output=quantized_output, swap_ab=True)
+            sw = default_config(m, n, k, swap_ab=True, **kw)
         except ValueError:
             return plain
         psw = sw.plan(m, n, k)
-        return sw if psw.error is None and psw.cluster >= 2 and sw.block_n == 256 else plain
+        ok = psw.error is None and sw.block_n == 256 and (psw.cluster >= 2 or (independent_inputs and not
+                                                                                 reduce_in_cluster))
+        return sw if ok else plain
+    if swap_ab and (schedule != "cluster" or m > 16):
+        raise ValueError(f"no swap-AB plan for M={m}: needs M <= 16 and the cluster schedule")
     flags = FLAG_INDEPENDENT_INPUTS if independent_inputs else 0
     stream_k = B200Config(m_tile=m_tile_for(m), block_n=256, subs=2, stages=2, layout=layout, pdl=pdl,
                           split_k=1, grid_ctas=-1, flags=flags)
-    if swap_ab and (schedule != "cluster" or m > 16):
-        raise ValueError(f"no swap-AB plan for M={m}: needs M <= 16 and the cluster schedule")
-    if schedule == "stream_k" and not quantized_output:
+    if schedule == "stream_k" and not reduce_in_cluster:
         return stream_k
     if schedule not in ("cluster", "stream_k"):
         raise ValueError("schedule must be 'cluster' or 'stream_k'")
@@ -212,17 +231,18 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
     if swap_ab:
         base = replace(base, flags=base.flags | FLAG_SWAP_AB)
     p256 = base.plan(m, n, k)
-    if quantized_output:
-        if schedule != "cluster" or n % 128 != 0 or p256.error is not None:
-            raise ValueError(f"no quantized-output plan for M={m} N={n} K={k}: needs the cluster schedule "
-                             f"and N a multiple of 128 ({p256.error})")
+    if reduce_in_cluster:
+        if schedule != "cluster" or (quantized_output and n % 128 != 0) or p256.error is not None:
+            raise ValueError(f"no cluster-reduction plan for M={m} N={n} K={k}: needs the cluster schedule "
+                             f"(and N a multiple of 128 for quantised output) ({p256.error})")
         if p256.cluster < 2:
-            # The quantisation runs in the cluster reduction: at least two
-            # CTAs per tile (a CTA without a K chunk adds a zero partial).
+            # The quantisation and the lines gather run in the cluster
+            # reduction: at least two CTAs per tile (a CTA without a K chunk
+            # adds a zero partial).
             base = replace(base, split_k=2)
             err = base.plan(m, n, k).error
             if err is not None:
-                raise ValueError(f"no quantized-output plan for M={m} N={n} K={k}: {err}")
+                raise ValueError(f"no cluster-reduction plan for M={m} N={n} K={k}: {err}")
         return base
     if not independent_inputs:
         # Dependent launches stream at ~50 GB/s per SM: the tile width whose
@@ -235,6 +255,8 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
         if not cands:
             return _no_swap_fallback(swap_ab, stream_k, base, m, n, k, p256.error)
         return min(cands, key=lambda cp: (cp[0].block_n * -(-chunks // cp[1].cluster), cp[1].num_ctas))[0]
+    if p256.error is None and p256.cluster == 1 and -(-n // 256) >= INDEPENDENT_TILE_CTAS:
+        return base                      # one CTA per 256-row tile
     if p256.error is not None or p256.cluster < 2:
         return _no_swap_fallback(swap_ab, stream_k, base, m, n, k, p256.error)
     if n % 224 == 0:

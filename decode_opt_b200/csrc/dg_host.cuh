@@ -80,13 +80,21 @@ constexpr int kB200ClusterOccupancy[kMaxClusterSplit + 1] = {0,  148, 74, 45, 33
 //   next GEMM's early CTAs start there while this grid runs; 16384 x 7168 on
 //   all 148 SMs (74 x 2 CTAs of 224 rows) took 25.4 us per layer of the
 //   61-layer chain against 23.6 on 128 (64 x 2 of 256);
-//   independent inputs (consecutive GEMMs may overlap): the smallest S <= 8
-//   that still gives 32 CTAs, so that more GEMMs stream side by side.
+//   independent inputs (consecutive GEMMs may overlap): one CTA per tile
+//   (no split, no reduction) when there are at least kIndependentTileCtas
+//   tiles -- at C2 (28 tiles of 256 rows) about five GEMMs then stream side
+//   by side, and against a split of 2 (56 CTAs) a GEMM took 15.6 / 15.9 /
+//   17.3 / 19.1 / 20.3 us instead of 15.9 / 16.4 / 18.5 / 20.8 / 23.2 at
+//   M = 1 / 16 / 32 / 64 / 128 over 1,000 launches, and 17.3 / 17.4 / 18.5 /
+//   21.4 / 22.6 instead of 18.1 / 18.9 / 20.5 / 22.2 / 28.8 over 20; with
+//   fewer tiles the smallest S <= 8 that still gives 32 CTAs.
 // 1 (no split) when not even clusters of two fit in one wave.
 constexpr int kSpareSms = 20;
+constexpr int kIndependentTileCtas = 24;
 __host__ __device__ inline int choose_cluster_split(int T, int C, bool independent, const int* occ,
                                                     int num_sms = 148) {
   if (independent) {
+    if (T >= kIndependentTileCtas) return 1;
     const int s_max = C < 8 ? C : 8;
     for (int s = 2; s <= s_max; ++s)
       if (T <= occ[s] && static_cast<long long>(T) * s >= 32) return s;
@@ -252,7 +260,8 @@ __host__ __device__ inline Plan make_plan(const Config& c, int M, int N, int K, 
     if (((c.flags & kFlagClassFromMTile) ? c.m_tile : M) > SwapTraits::kMmaN)
       return plan.error = "swap-AB: M must be <= 16", plan;
     if (c.block_n <= SwapTraits::kMmaM) return plan.error = "swap-AB: block_n must be in [136, 256]", plan;
-    if (c.grid_ctas != kGridCluster) return plan.error = "swap-AB: cluster split-K schedule only", plan;
+    if (c.grid_ctas != kGridCluster && !(c.grid_ctas == 0 && c.split_k == 1))
+      return plan.error = "swap-AB: cluster split-K or one CTA per tile (grid_ctas 0, split_k 1)", plan;
     bc = {SwapTraits::kMmaM, 1, 1, true};
   }
   const int mma_m = bc.mma_m;

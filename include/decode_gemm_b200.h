@@ -89,7 +89,8 @@ extern "C" {
                                         issuing warps per tile), a quarter of the
                                         multiply-adds per weight byte of the default
                                         M <= 16 class; needs block_n in [136, 256] and
-                                        grid_ctas DG_GRID_CLUSTER
+                                        grid_ctas DG_GRID_CLUSTER (or 0 with split_k 1:
+                                        one CTA per tile)
                                         (dg_plan reports mma_m 128, n_mma 16) */
 
 /* Device status codes written to dg_problem.status (first error wins). */

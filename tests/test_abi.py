@@ -82,9 +82,10 @@ def test_status_strings():
 def test_default_plan_c2_cluster(m):
     """Default schedule (no GPU: the measured B200 cluster occupancy): cluster
     split-K, 224-row tiles x 4 K-splits = 128 CTAs in one wave for dependent
-    launches (the default batch class); for independent inputs 2 K-splits:
-    M <= 16 the swap-AB class on 256-row tiles (three 64 KiB stages), M = 32
-    224-row tiles (three ring stages, MMA M 64), else 256; no workspace."""
+    launches (the default batch class); for independent inputs one CTA per
+    256-row tile (28 CTAs, no split; M <= 16 on the swap-AB class with three
+    64 KiB stages), and with the tagged-lines gather 2 K-splits; no
+    workspace."""
     c = dg.default_config(m, 7168, 16384)
     p = c.plan(m, 7168, 16384)
     assert p.error is None and c.grid_ctas == dg.GRID_CLUSTER and c.block_n == 224
@@ -95,12 +96,13 @@ def test_default_plan_c2_cluster(m):
     ci = dg.default_config(m, 7168, 16384, independent_inputs=True)
     pi = ci.plan(m, 7168, 16384)
     assert bool(ci.flags & dg.FLAG_SWAP_AB) == (m <= 16)
-    assert ci.block_n == (224 if m == 32 else 256) and pi.cluster == 2
-    assert pi.num_ctas == (64 if m == 32 else 56)
+    assert ci.block_n == 256 and pi.cluster == 1 and pi.grid == (28, 1, 1) and pi.num_ctas == 28
     if m <= 16:
         assert (pi.mma_m, pi.n_mma, pi.stages) == (128, 16, 3)
-    assert dg.default_config(m, 7168, 16384, independent_inputs=True, swap_ab=False).block_n == (
-        224 if m <= 32 else 256)
+    cl = dg.default_config(m, 7168, 16384, independent_inputs=True, gather_lines=True)
+    pl = cl.plan(m, 7168, 16384)
+    assert cl.block_n == 256 and pl.cluster == 2 and pl.num_ctas == 56
+    assert dg.default_config(m, 7168, 16384, independent_inputs=True, swap_ab=False).block_n == 256
     # a small matrix: 16 chunks per tile, so 8 CTAs per tile (two chunks
     # each) rather than the ragged 10; 10 ragged 224-row tiles stream
     # 224 x 2 rows-chunks per CTA against 256 x 2
@@ -175,6 +177,8 @@ def test_swap_ab_plan_rejections():
     assert "M must be <= 16" in replace(sw, m_tile=32).validate(17, 2048, 4096)
     assert "block_n" in replace(sw, block_n=128).validate(8, 2048, 4096)
     assert "cluster" in replace(sw, grid_ctas=-1).validate(8, 2048, 4096)
+    assert "cluster" in replace(sw, grid_ctas=0, split_k=2).validate(8, 2048, 4096)
+    assert replace(sw, grid_ctas=0, split_k=1).validate(8, 2048, 4096) is None
     with pytest.raises(ValueError):
         dg.default_config(17, 2048, 4096, swap_ab=True)
     with pytest.raises(ValueError):
@@ -278,10 +282,12 @@ B200_CLUSTER_OCC = [0, 148, 74, 45, 33, 26, 22, 15, 15,      # clusters of S CTA
 
 
 def _rule_split(t, c, independent):
-    """The split rule restated: independent inputs -> the smallest one-wave S
-    giving >= 32 CTAs (S <= 8); dependent -> the smallest one-wave S (S <= 16,
-    at most 148 - 20 CTAs) with the fewest chunks for the busiest CTA,
-    ceil(C / S); both S <= C."""
+    """The split rule restated: independent inputs -> one CTA per tile from 24
+    tiles, else the smallest one-wave S giving >= 32 CTAs (S <= 8); dependent
+    -> the smallest one-wave S (S <= 16, at most 148 - 20 CTAs) with the
+    fewest chunks for the busiest CTA, ceil(C / S); both S <= C."""
+    if independent and t >= dg.INDEPENDENT_TILE_CTAS:
+        return 1
     s_max = min(c, 8 if independent else 16)
     if not independent:
         best, best_chunks = 1, c
@@ -327,7 +333,9 @@ def test_default_plans_follow_the_split_rule(n, k, m, independent):
         assert p.mma_m == (64 if m <= 32 else 128)
         assert p.block[0] == (192 if m <= 16 else 320 if m <= 64 else 384)
     if independent:
-        assert p.num_ctas >= 32 or p.cluster == min(chunks, 8)
+        # one CTA per 256-row tile from 24 tiles, else >= 32 CTAs if a split allows
+        assert (p.cluster == 1 and c.block_n == 256 and tiles >= dg.INDEPENDENT_TILE_CTAS) or \
+            p.num_ctas >= 32 or p.cluster == min(chunks, 8)
 
 
 @pytest.mark.parametrize("bn", list(range(32, 257, 8)))

@@ -167,7 +167,7 @@ def _rank_main(rank, world, port, m, n, k, result_dir, protocol="flags", steps=2
         w, ws = oracle.gen_weight_smoke(n, k, 91)
         n_loc = n // world
         lo, hi = tp.shard_rows(n, world, rank)
-        cfg = dg.default_config(m, n_loc, k, layout=dg.LAYOUT_PACKED_SWIZZLED)
+        cfg = dg.default_config(m, n_loc, k, layout=dg.LAYOUT_PACKED_SWIZZLED, gather_lines=protocol == "lines")
         plan = cfg.plan(m, n_loc, k)
         wt = dg.prepack_weight(torch.from_numpy(np.ascontiguousarray(w[lo:hi])).to(dev), cfg.block_n, cfg.layout)
         wsc = torch.from_numpy(np.ascontiguousarray(tp.shard_scales(ws, world, rank, n))).to(dev)
@@ -261,7 +261,8 @@ def _serve_main(rank, world, port, m, n, k, group, count, distinct, result_dir, 
         w, ws = oracle.gen_weight_smoke(n, k, 91)
         n_loc = n // world
         lo, hi = tp.shard_rows(n, world, rank)
-        cfg = dg.default_config(m, n_loc, k, layout=dg.LAYOUT_PACKED_SWIZZLED, independent_inputs=True)
+        cfg = dg.default_config(m, n_loc, k, layout=dg.LAYOUT_PACKED_SWIZZLED, independent_inputs=True,
+                                gather_lines=protocol == "lines")
         plan = cfg.plan(m, n_loc, k)
         wt = dg.prepack_weight(torch.from_numpy(np.ascontiguousarray(w[lo:hi])).to(dev), cfg.block_n, cfg.layout)
         wsc = torch.from_numpy(np.ascontiguousarray(tp.shard_scales(ws, world, rank, n))).to(dev)
