@@ -60,6 +60,8 @@ CASES = [
     (13, 584, 1024, dg.LAYOUT_PACKED_SWIZZLED, False, 256, 8),     # split 8 > 4 chunks: zero partials
     (16, 2048, 4096, dg.LAYOUT_PACKED_SWIZZLED, False, None, None),
     (16, 7168, 16384, dg.LAYOUT_PACKED_SWIZZLED, True, None, None),
+    (1, 1792, 16384, dg.LAYOUT_PACKED_SWIZZLED, False, None, None),  # 4-GPU shard: clusters of 16 (non-portable)
+    (8, 896, 16384, dg.LAYOUT_PACKED_SWIZZLED, False, 256, None),    # 8-GPU shard: 4 tiles x 16
     (4, 20480, 1024, dg.LAYOUT_RAW, True, 256, None),              # 80 tiles: no split fits, one CTA per tile
     (9, 20480, 1024, dg.LAYOUT_PACKED_SWIZZLED, False, 256, None),
 ]
@@ -75,6 +77,8 @@ def test_swap_ab_matches_oracle(m, n, k, layout, independent, block_n, split_k):
     assert plan.mma_m == 128 and plan.n_mma == 16 and plan.ws_floats == 0
     if n == 20480:
         assert plan.cluster == 1          # the direct-store path
+    if n in (896, 1792) and not independent:
+        assert plan.cluster == 16         # a non-portable cluster size
     rc, got, status = dc.run(cfg)
     assert rc == 0 and status == 0, (rc, dg.status_string(status))
     ok, rl2, worst = check_against_oracle(got, ref)
