@@ -183,13 +183,14 @@ __host__ __device__ constexpr uint32_t align1k(uint32_t v) { return (v + 1023u) 
 // MMA-M rows x 128 bytes) and the barrier block.
 // mma_rows: weight rows the MMA reads per 128-K block (0: block_n rounded up
 // to 16; the swap-AB class reads two 128-row halves); the rows past block_n
-// of the ring's last block come from a tail pad.
+// of the ring's last block come from a tail pad.  bufs: accumulator buffers
+// (their barriers are in the block).
 __host__ __device__ constexpr uint32_t pipeline_smem_bytes(int stages, int subs, int block_n, int mma_m,
-                                                           int mma_rows = 0) {
+                                                           int mma_rows = 0, int bufs = kAccumBuffers) {
   return 1024u +
          align1k(static_cast<uint32_t>(stages * subs * block_n * kKBlock +
                                        ((mma_rows > 0 ? mma_rows : ((block_n + 15) / 16) * 16) - block_n) * kKBlock)) +
-         align1k(static_cast<uint32_t>(stages * subs * mma_m * kKBlock)) + SmemBarriers::bytes(stages, kAccumBuffers);
+         align1k(static_cast<uint32_t>(stages * subs * mma_m * kKBlock)) + SmemBarriers::bytes(stages, bufs);
 }
 
 // The shallowest ring whose drained buffers hold the fp32 partial of M rows
@@ -285,7 +286,8 @@ __host__ __device__ inline Plan make_plan(const Config& c, int M, int N, int K, 
   const uint32_t w_pad = static_cast<uint32_t>((mma_rows - c.block_n) * kKBlock);
   (void)bufs;
   auto smem_for = [&](int stages) -> uint32_t {
-    return pipeline_smem_bytes(stages, c.subs, c.block_n, act_rows, mma_rows);
+    return pipeline_smem_bytes(stages, c.subs, c.block_n, act_rows, mma_rows,
+                               bc.swap ? SwapTraits::kNumBufs : kAccumBuffers);
   };
   int stages = c.stages;
   if (stages == 0) {

@@ -319,8 +319,10 @@ struct SwapTraits {
   static constexpr int kMmaIssuers = 2;              // warp kMmaWarp + 1 issues rows 128..255
   static constexpr int kThreads = (kEpiWarps + 2 + 1) * 32;
   static constexpr int kBnMax = 2 * kMmaN;           // accumulator columns per buffer
-  static constexpr int kNumBufs = 2;
-  static constexpr uint32_t kTmemCols = 64u;
+  // Four 32-column buffers: the MMA warps run up to three 128-K blocks ahead
+  // of the epilogue's fold (MMA issue is on the critical path).
+  static constexpr int kNumBufs = 4;
+  static constexpr uint32_t kTmemCols = 128u;
   static constexpr int kDeferUnits = 4;              // as the other classes (M <= 16: <= 4 units)
 };
 
