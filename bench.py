@@ -720,6 +720,20 @@ def b200_arm(args, rank, world, local_rank):
             dev_in.copy_(hin, non_blocking=True)
             gs_zc.launch(i, stream)
 
+        # The same with the input copied by a kernel (dg.copy_from_host) under
+        # programmatic dependent launch instead of a copy node: it waits for
+        # the previous request's GEMM before writing the input, so requests
+        # still run one at a time, but each GEMM launches and prefetches its
+        # weights while the previous one runs.
+        hy_zk = torch.empty((m, n), dtype=torch.bfloat16).pin_memory() if world == 1 else None
+        gs_zk = (GemmSetup(rotation(gs_dep.cfg.block_n), gs_dep.cfg, m, act_in, wscale, sc_in, dev, host_out=hy_zk)
+                 if world == 1 else None)
+        hin_dev = dg.host_device_pointer(hin) if world == 1 else None
+
+        def e2e_step_zk(i):
+            dg.copy_from_host(dev_in, hin, stream, pdl_attr=True, src_device=hin_dev)
+            gs_zk.launch(i, stream)
+
         pipe = None
         if world == 1:
             # A serving loop keeps `depth` requests in flight: request i runs
@@ -859,6 +873,7 @@ def b200_arm(args, rank, world, local_rank):
         K_ser = K2 if world > 1 else K          # two gather sets alternate on N GPUs
         te_serial = timed_serial(K_ser) * K / K_ser
         te_serial_zc = timed_serial(K, e2e_step_zc) if world == 1 else None
+        te_serial_zk = timed_serial(K, e2e_step_zk) if world == 1 else None
         gs.check_status()
         gs_e2e.check_status()
         # Output checks.  The serial path runs the dependent schedule and the
@@ -878,6 +893,8 @@ def b200_arm(args, rank, world, local_rank):
             e2e_check["serial_bit_exact"] = bool(torch.equal(hy.view(torch.int16), want_s))
             gs_zc.check_status()
             e2e_check["serial_zero_copy_bit_exact"] = bool(torch.equal(hy_zc.view(torch.int16), want_s))
+            gs_zk.check_status()
+            e2e_check["serial_copy_kernel_bit_exact"] = bool(torch.equal(hy_zk.view(torch.int16), want_s))
             if pipe is not None:
                 g0 = pipe_copy["setups"][0]
                 g0.out.zero_()
@@ -914,9 +931,12 @@ def b200_arm(args, rank, world, local_rank):
                "requests_in_flight": pipe["depth"] if pipe is not None else 1,
                "serial": {"us_per_step": te_serial / K * 1e6,
                           "zero_copy_us_per_step": te_serial_zc / K * 1e6 if te_serial_zc is not None else None,
+                          "copy_kernel_us_per_step": te_serial_zk / K * 1e6 if te_serial_zk is not None else None,
                           "note": "one request at a time on one stream, dependent schedule, CUDA graphs"
                                   + ("; zero_copy: the kernel writes the bf16 result into pinned host memory, "
-                                     "no D2H copy node" if te_serial_zc is not None else "")},
+                                     "no D2H copy node; copy_kernel: zero-copy output and the input copied by "
+                                     "dg.copy_from_host under PDL instead of a copy node"
+                                     if te_serial_zc is not None else "")},
                "output_to_host": ("zero-copy: the GEMM stores the bf16 result straight into pinned host "
                                   "memory over PCIe (dg.host_device_pointer), no D2H copy node; the result's "
                                   "bytes still cross PCIe every step"

@@ -50,7 +50,7 @@ __all__ = [
     "launch_prepack_weight", "prepack_weight", "fp8_decode_gemm", "default_config", "status_string",
     "LAYOUT_RAW", "LAYOUT_PACKED", "LAYOUT_PACKED_SWIZZLED", "FLAG_INJECT_TIMEOUT", "FLAG_INDEPENDENT_INPUTS",
     "FLAG_SWAP_AB",
-    "ERR_INJECTED_TIMEOUT", "STATUS_OK", "m_tile_for", "flush_l2", "GRID_CLUSTER",
+    "ERR_INJECTED_TIMEOUT", "STATUS_OK", "m_tile_for", "flush_l2", "GRID_CLUSTER", "copy_from_host",
 ]
 
 CUDA_SUCCESS = 0
@@ -700,6 +700,26 @@ def host_device_pointer(t) -> int:
     if rc != 0 or out.value is None:
         raise RuntimeError(f"dg_host_device_pointer failed: cudaError {rc}")
     return int(out.value)
+
+
+def copy_from_host(dst, src, stream=None, pdl_attr: bool = True, src_device: Optional[int] = None) -> None:
+    """dst (device tensor) <- src (pinned host tensor, same number of bytes),
+    copied by a kernel that reads the host memory over PCIe
+    (``dg_copy_from_host``).  Launched with ``pdl_attr`` it releases the next
+    kernel at once and waits for the previous one before writing dst, so a
+    stream of "copy request i's input, GEMM request i" stays one request at a
+    time while every GEMM's launch and weight prefetch overlap the one before
+    it.  ``src_device``: src's device address from :func:`host_device_pointer`,
+    looked up once (e.g. before a CUDA graph capture) instead of per call."""
+    nbytes = dst.numel() * dst.element_size()
+    if src.numel() * src.element_size() != nbytes or not dst.is_cuda or not dst.is_contiguous() \
+            or not src.is_contiguous():
+        raise ValueError("copy_from_host: contiguous device dst and pinned host src of the same size")
+    src_dev = src_device if src_device is not None else host_device_pointer(src)
+    rc = _lib.lib().dg_copy_from_host(ctypes.c_void_p(dst.data_ptr()), ctypes.c_void_p(src_dev), nbytes,
+                                      _stream_handle(stream), int(bool(pdl_attr)))
+    if rc != 0:
+        raise RuntimeError(f"dg_copy_from_host failed: cudaError {rc}")
 
 
 def launch(cfg, p: Problem, stream=None) -> int:

@@ -37,7 +37,7 @@ EXPORTED_SYMBOLS = (
     "dg_probe_naive_read", "dg_num_sms", "dg_launch_static_scratch", "dg_probe_mma",
     "dg_launch_gather", "dg_gather_wait", "dg_ipc_export", "dg_ipc_import", "dg_ipc_release",
     "dg_quantize_act", "dg_max_active_clusters", "dg_launch_quantized", "dg_launch_gather_lines",
-    "dg_host_device_pointer",
+    "dg_host_device_pointer", "dg_copy_from_host",
 )
 
 
@@ -175,6 +175,8 @@ def lib():
     L.dg_launch_gather_lines.argtypes = [cfgp, probp, ctypes.POINTER(DgGatherLines), ctypes.c_void_p,
                                          ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
     L.dg_host_device_pointer.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+    L.dg_copy_from_host.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_void_p,
+                                    ctypes.c_int]
     L.dg_gather_wait.argtypes = [ctypes.POINTER(DgGather), ctypes.c_void_p, ctypes.c_ulonglong, ctypes.c_void_p]
     L.dg_ipc_export.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_ulonglong)]
     L.dg_ipc_import.argtypes = [ctypes.c_void_p, ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_void_p)]

@@ -17,6 +17,12 @@
 // Under programmatic dependent launch the kernel releases its dependents at
 // once (the next GEMM may prefetch its weights) and waits for the grid that
 // produced its input before reading it.
+//
+// dg_copy_from_host is the same pattern for a request's input: a copy of
+// pinned host memory (through its device address) into device memory done
+// by GPU loads, so that it sits between two GEMMs as a kernel with
+// programmatic dependent launch instead of a copy node (which a graph orders
+// after the preceding GEMM's completion and before the next GEMM's launch).
 
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
@@ -78,9 +84,55 @@ __global__ void __launch_bounds__(kQuantThreads)
   if (lane == 0) scales[static_cast<size_t>(m) * kb + b] = scale;
 }
 
+constexpr int kCopyThreads = 256;
+constexpr unsigned kCopyMaxBlocks = 592;   // 4 per SM on a 148-SM part
+
+// dst[0, bytes) = src[0, bytes), src in mapped pinned host memory.  Loads are
+// volatile (ld.global.cv): every launch reads the host's current bytes over
+// PCIe, nothing cached from an earlier launch.  vec: both pointers 16-byte
+// aligned (16-byte loads and stores, then the tail byte by byte).
+__global__ void __launch_bounds__(kCopyThreads)
+    copy_from_host_kernel(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, unsigned long long bytes,
+                          int vec) {
+  dg::sm100::griddep_launch_dependents();
+  dg::sm100::griddep_wait();
+  const unsigned long long tid = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
+  unsigned long long done = 0;
+  if (vec) {
+    const unsigned long long n16 = bytes / 16;
+    for (unsigned long long i = tid; i < n16; i += stride)
+      reinterpret_cast<uint4*>(dst)[i] = __ldcv(reinterpret_cast<const uint4*>(src) + i);
+    done = n16 * 16;
+  }
+  for (unsigned long long i = done + tid; i < bytes; i += stride) dst[i] = __ldcv(src + i);
+}
+
 }  // namespace
 
 extern "C" {
+
+int dg_copy_from_host(void* dst, const void* src, unsigned long long bytes, void* stream, int pdl_attr) {
+  if (dst == nullptr || src == nullptr || bytes == 0) return cudaErrorInvalidValue;
+  const int vec = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15u) == 0 ? 1 : 0;
+  const unsigned long long units = vec ? (bytes + 15) / 16 : bytes;
+  unsigned long long blocks = (units + kCopyThreads - 1) / kCopyThreads;
+  if (blocks > kCopyMaxBlocks) blocks = kCopyMaxBlocks;
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1]{};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
+  cfg.blockDim = dim3(kCopyThreads, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 0;
+  if (pdl_attr) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, copy_from_host_kernel, static_cast<uint8_t*>(dst),
+                            static_cast<const uint8_t*>(src), bytes, vec);
+}
 
 int dg_quantize_act(const void* x, int ldx, int M, int K, void* q, float* scales, void* stream, int pdl_attr) {
   if (x == nullptr || q == nullptr || scales == nullptr || M < 1 || K < 128 || K % 128 != 0 || ldx < K)

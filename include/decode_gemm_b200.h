@@ -46,6 +46,8 @@
  *   dg_ipc_export / dg_ipc_import / dg_ipc_release  (new) peer buffers for it
  *   dg_num_sms              (new) SM count of the current device
  *   dg_host_device_pointer  (new) device address of pinned host memory (zero-copy output)
+ *   dg_copy_from_host       (new) a request's input copied from pinned host memory by a
+ *                           kernel that can sit under programmatic dependent launch
  *   dg_probe_mma            (new) tcgen05.mma issue / completion cost per shape
  */
 #ifndef DECODE_GEMM_B200_H_
@@ -350,6 +352,18 @@ int dg_num_sms(void);
    launch has completed.  Returns a cudaError_t value (an error, and *device
    untouched, for memory that is not mapped pinned memory). */
 int dg_host_device_pointer(void* host, void** device);
+
+/* (new) dst[0, bytes) = src[0, bytes) on `stream`, done by a small kernel whose
+   loads read `src`, mapped pinned host memory given by its device address
+   (dg_host_device_pointer), over PCIe.  With pdl_attr the kernel is launched
+   with programmatic stream serialization: it releases its dependents at once
+   (the next GEMM may prefetch its weights before its griddepcontrol.wait)
+   and waits for the preceding grid before it writes dst, so a chain of
+   "copy request i's input, GEMM request i" keeps one request at a time while
+   every GEMM's launch and weight prefetch overlap the previous one, where a
+   copy node would order the next launch after the previous GEMM's end.
+   Returns a cudaError_t value. */
+int dg_copy_from_host(void* dst, const void* src, unsigned long long bytes, void* stream, int pdl_attr);
 
 /* tcgen05.mma cost probe: in each of `ctas` CTAs (at most one per SM)
    `issuers` warps (1..4) issue iters / issuers kind::f8f6f4 MMAs each, of
