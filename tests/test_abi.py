@@ -190,6 +190,11 @@ def test_launch_rejections_need_no_gpu():
     p = dg.Problem(9, 256, 512)
     assert dg.launch(B(m_tile=8), p) == 1
     assert dg.launch(B(m_tile=8), dg.Problem(1, 256, 500)) == 1
+    # the input copy kernel refuses null pointers and empty copies before any CUDA call
+    L = _lib.lib()
+    assert L.dg_copy_from_host(None, ctypes.c_void_p(16), 16, None, 1) == dg.CUDA_ERROR_INVALID_VALUE
+    assert L.dg_copy_from_host(ctypes.c_void_p(16), None, 16, None, 1) == dg.CUDA_ERROR_INVALID_VALUE
+    assert L.dg_copy_from_host(ctypes.c_void_p(16), ctypes.c_void_p(32), 0, None, 0) == dg.CUDA_ERROR_INVALID_VALUE
 
 
 def _units(G, U):
