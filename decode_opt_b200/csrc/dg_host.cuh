@@ -47,7 +47,8 @@ struct Config {
                           // kGridCluster: cluster split-K
   int epi_warps = 0;      // informational; the tile width fixes the epilogue warps
   unsigned long long timeout_ns = 0;  // bounded-wait limit; 0 = 2 s
-  int flags = 0;          // extra kernel flags (kFlagInjectTimeout: tests only)
+  int flags = 0;          // kFlagIndependentInputs, kFlagSwapAB, kFlagClassFromMTile (planning),
+                          // kFlagInjectTimeout (a test hook)
   int pack_rows = 0;      // kLayoutPacked: rows per tile of the packed weights when a
                           // CTA tile spans several (block_n a multiple of it); 0 = block_n
 };

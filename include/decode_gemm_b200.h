@@ -130,7 +130,8 @@ typedef struct dg_config {
                     the S CTAs of a tile form a thread-block cluster and reduce
                     through distributed shared memory -- no workspace          */
   int epi_warps; /* 0 (or the value block_n implies: 4 per 64 tile columns)            */
-  int flags;     /* DG_FLAG_* (tests only)                                              */
+  int flags;     /* DG_FLAG_*: INDEPENDENT_INPUTS, SWAP_AB, CLASS_FROM_M_TILE; and
+                    INJECT_TIMEOUT, a test hook                                         */
   unsigned long long timeout_ns; /* bounded-wait limit per wait; 0 = 2 s               */
   int pack_rows; /* DG_LAYOUT_PACKED only: rows per tile of the packed weights when one
                     tile of the kernel (block_n rows) spans several of them -- block_n a
