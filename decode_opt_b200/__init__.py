@@ -236,9 +236,8 @@ def default_config(m: int, n: int, k: int, layout: int = LAYOUT_RAW, pdl: bool =
             raise ValueError(f"no cluster-reduction plan for M={m} N={n} K={k}: needs the cluster schedule "
                              f"(and N a multiple of 128 for quantised output) ({p256.error})")
         if p256.cluster < 2:
-            # The quantisation and the lines gather run in the cluster
-            # reduction: at least two CTAs per tile (a CTA without a K chunk
-            # adds a zero partial).
+            # The quantisation runs in the cluster reduction: at least two
+            # CTAs per tile (a CTA without a K chunk adds a zero partial).
             base = replace(base, split_k=2)
             err = base.plan(m, n, k).error
             if err is not None:
